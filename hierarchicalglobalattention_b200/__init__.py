@@ -1,0 +1,11 @@
+"""B200-native (sm_100a) implementation of HGA's routed-attention hot path.
+
+Drop-in for the reference's ``HierarchicalGlobalAttentionRouted`` module, its ``KvRouter``
+(``ChunkRouter`` / ``RoutedKV`` / ``RouterConfig`` / KV-cache stores) and its Qwen3 patch
+(``replace_qwen_attention_with_router``).  Compute runs in hand-written CUDA kernels behind the C
+ABI of ``libhga_b200.so`` (include/hga_b200.h); PyTorch provides device memory, streams and the
+projection GEMMs.
+"""
+from . import _lib, ops  # noqa: F401
+
+__all__ = ["_lib", "ops"]

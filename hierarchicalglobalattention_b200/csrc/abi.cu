@@ -1,0 +1,143 @@
+// extern "C" entry points of libhga_b200.so: argument validation, dispatch, error reporting.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "hga_common.cuh"
+
+namespace hga {
+cudaError_t launch_summaries(const hga_params& p, int64_t S, int64_t pos0, const void* k_raw, const void* k_rope,
+                             const void* v, int64_t kv_cap, const void* cos, const void* sin, int rot_dtype,
+                             int64_t rot_row0, void* ck, void* gk, void* gv, int64_t sum_cap, int64_t out_chunk0,
+                             cudaStream_t st);
+cudaError_t launch_route_prefill(const hga_params& p, int64_t S, const void* q, int q_layout, const void* ck,
+                                 const void* gk, int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0,
+                                 int32_t* open_gid, int32_t* open_t0, float* dbg1, float* dbg2, cudaStream_t st,
+                                 int* smem_bytes_out);
+cudaError_t launch_attend_simt(const hga_params& p, int64_t S, const void* q, int q_layout, const void* k_rope,
+                               const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0,
+                               int Kg, void* out, int out_layout, cudaStream_t st);
+bool attend_tc_supported(const hga_params& p);
+cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const void* q, int q_layout, const void* k_rope,
+                             const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0,
+                             int Kg, void* out, int out_layout, cudaStream_t st);
+}  // namespace hga
+
+static thread_local char g_err[512];
+
+static int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+static int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return HGA_OK;
+  if (e == cudaErrorInvalidConfiguration)
+    return fail(HGA_E_UNSUPPORTED, "%s: shape needs more shared memory than one CTA can hold", what);
+  return fail(HGA_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+static int check_params(const hga_params* p) {
+  if (!p) return fail(HGA_E_INVALID, "params is NULL");
+  if (p->batch <= 0 || p->nhead <= 0 || p->kv_heads <= 0 || p->head_dim <= 0)
+    return fail(HGA_E_INVALID, "batch/nhead/kv_heads/head_dim must be positive");
+  if (p->nhead % p->kv_heads) return fail(HGA_E_INVALID, "nhead %% kv_heads != 0");
+  if (p->head_dim % 2 || p->head_dim > 256) return fail(HGA_E_UNSUPPORTED, "head_dim must be even and <= 256");
+  if (p->chunk_size <= 0 || p->group_size <= 0 || p->chunk_size % p->group_size)
+    return fail(HGA_E_INVALID, "chunk_size must be a positive multiple of group_size");
+  if (p->chunk_size > 128) return fail(HGA_E_UNSUPPORTED, "chunk_size > 128 is not supported");
+  if (p->dtype < HGA_DTYPE_F32 || p->dtype > HGA_DTYPE_F16) return fail(HGA_E_INVALID, "unknown dtype %d", p->dtype);
+  return HGA_OK;
+}
+
+static int route_sizes(const hga_params* p, int64_t S, int* Kc, int* Kg) {
+  const int C = p->chunk_size, M = C / p->group_size;
+  const int64_t N = (S + C - 1) / C;
+  *Kc = p->topk_chunks > 0 ? (int)(p->topk_chunks < N ? p->topk_chunks : N) : 0;
+  const int Tg = *Kc * M;
+  int kg = p->topk_groups > 0 ? (p->topk_groups < Tg ? p->topk_groups : Tg) : 0;
+  const int kgr = p->topk_groups > 0 ? ((p->topk_groups / 2) < Tg ? p->topk_groups / 2 : Tg) : 0;
+  if (kgr == 0) kg = 0;
+  *Kg = kg;
+  return 0;
+}
+
+extern "C" {
+
+const char* hga_version(void) { return "hga_b200 0.1 (sm_100a)"; }
+const char* hga_last_error(void) { return g_err; }
+
+int hga_summaries(const hga_params* p, int64_t seq_len, int64_t pos0, const void* k_raw, const void* k_rope,
+                  const void* v, int64_t kv_cap, const void* cos, const void* sin, int32_t rot_dtype,
+                  int64_t rot_row0, void* chunk_k, void* group_k, void* group_v, int64_t sum_cap,
+                  int64_t out_chunk0, cudaStream_t stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (seq_len <= 0) return HGA_OK;
+  if (!k_raw || !k_rope || !v || !cos || !sin || !chunk_k || !group_k)
+    return fail(HGA_E_INVALID, "hga_summaries: NULL tensor");
+  if (kv_cap < seq_len) return fail(HGA_E_INVALID, "hga_summaries: kv_cap < seq_len");
+  if (pos0 % p->chunk_size) return fail(HGA_E_INVALID, "hga_summaries: pos0 must be chunk aligned");
+  if (pos0 < rot_row0) return fail(HGA_E_INVALID, "hga_summaries: rotary table starts after pos0");
+  const int64_t N = (seq_len + p->chunk_size - 1) / p->chunk_size;
+  if (out_chunk0 < 0 || out_chunk0 + N > sum_cap) return fail(HGA_E_INVALID, "hga_summaries: summary capacity too small");
+  if (rot_dtype != HGA_DTYPE_F32 && rot_dtype != p->dtype)
+    return fail(HGA_E_INVALID, "hga_summaries: rot_dtype must be fp32 or the model dtype");
+  return cuda_status(hga::launch_summaries(*p, seq_len, pos0, k_raw, k_rope, v, kv_cap, cos, sin, rot_dtype, rot_row0,
+                                           chunk_k, group_k, group_v, sum_cap, out_chunk0, stream),
+                     "hga_summaries");
+}
+
+int hga_route_prefill(const hga_params* p, int64_t seq_len, const void* q, int32_t q_layout, const void* chunk_k,
+                      const void* group_k, int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid,
+                      int32_t* open_t0, float* dbg_l1, float* dbg_l2, cudaStream_t stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (seq_len <= 0) return HGA_OK;
+  int Kc, Kg;
+  route_sizes(p, seq_len, &Kc, &Kg);
+  if (!q || !chunk_k || !group_k) return fail(HGA_E_INVALID, "hga_route_prefill: NULL tensor");
+  if ((Kc && (!sel_chunk || !sel_t0)) || (Kg && (!open_gid || !open_t0)))
+    return fail(HGA_E_INVALID, "hga_route_prefill: NULL output list");
+  if (q_layout != 0 && q_layout != 1) return fail(HGA_E_INVALID, "q_layout must be 0 or 1");
+  const int64_t N = (seq_len + p->chunk_size - 1) / p->chunk_size;
+  if (sum_cap < N) return fail(HGA_E_INVALID, "hga_route_prefill: sum_cap < number of chunks");
+  if ((int64_t)Kc * (p->chunk_size / p->group_size) > 256)
+    return fail(HGA_E_UNSUPPORTED, "hga_route_prefill: topk_chunks * groups_per_chunk > 256");
+  int smem = 0;
+  return cuda_status(hga::launch_route_prefill(*p, seq_len, q, q_layout, chunk_k, group_k, sum_cap, sel_chunk, sel_t0,
+                                               open_gid, open_t0, dbg_l1, dbg_l2, stream, &smem),
+                     "hga_route_prefill");
+}
+
+int hga_attend_prefill(const hga_params* p, int64_t seq_len, const void* q, int32_t q_layout, const void* k_rope,
+                       const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0, void* out,
+                       int32_t out_layout, int32_t impl, cudaStream_t stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (seq_len <= 0) return HGA_OK;
+  int Kc, Kg;
+  route_sizes(p, seq_len, &Kc, &Kg);
+  if (!q || !k_rope || !v || !out) return fail(HGA_E_INVALID, "hga_attend_prefill: NULL tensor");
+  if (Kg && (!open_gid || !open_t0)) return fail(HGA_E_INVALID, "hga_attend_prefill: NULL open lists");
+  if (kv_cap < seq_len) return fail(HGA_E_INVALID, "hga_attend_prefill: kv_cap < seq_len");
+  if (q_layout != 0 && q_layout != 1) return fail(HGA_E_INVALID, "q_layout must be 0 or 1");
+  if (out_layout != 0 && out_layout != 1) return fail(HGA_E_INVALID, "out_layout must be 0 or 1");
+  const bool tc_ok = hga::attend_tc_supported(*p);
+  if (impl == 2 && !tc_ok)
+    return fail(HGA_E_UNSUPPORTED, "tensor-core attention needs bf16, head_dim 128, chunk 64, group 16");
+  if ((impl == 0 && tc_ok) || impl == 2)
+    return cuda_status(hga::launch_attend_tc(*p, seq_len, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg, out,
+                                             out_layout, stream),
+                       "hga_attend_prefill(tcgen05)");
+  if (impl != 0 && impl != 1) return fail(HGA_E_INVALID, "impl must be 0, 1 or 2");
+  return cuda_status(hga::launch_attend_simt(*p, seq_len, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg, out,
+                                             out_layout, stream),
+                     "hga_attend_prefill");
+}
+
+}  // extern "C"

@@ -1,0 +1,150 @@
+"""Tensor-level wrappers of the C ABI (device tensors in, device tensors out).
+
+Every function validates shapes / dtypes / devices, allocates its outputs through PyTorch's
+caching allocator and launches on the current CUDA stream.  Tensors must live on a CUDA device:
+there is no CPU path.
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import HgaParams, check, lib, ptr, stream_ptr
+
+Q_BHSD, Q_BSHD = 0, 1
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and t.device.type != "cuda":
+            raise _lib.HgaError("hga ops run on CUDA tensors only (no CPU fallback); got device "
+                                f"{t.device}")
+
+
+def route_sizes(p: HgaParams, seq_len: int) -> Tuple[int, int, int, int]:
+    """(N, Kc, Kg, Kg_request) exactly as vectorized.py:304, 365-366 size them."""
+    C = p.chunk_size
+    M = C // p.group_size
+    N = (seq_len + C - 1) // C
+    Kc = min(p.topk_chunks, N) if p.topk_chunks > 0 else 0
+    Tg = Kc * M
+    Kg = min(p.topk_groups, Tg) if p.topk_groups > 0 else 0
+    Kgr = min(p.topk_groups // 2, Tg) if p.topk_groups > 0 else 0
+    if Kgr == 0:
+        Kg = 0
+    return N, Kc, Kg, Kgr
+
+
+def q_layout_of(q: torch.Tensor) -> int:
+    """0 for a contiguous [B,H,S,Dh] tensor, 1 for a [B,H,S,Dh] view of a contiguous [B,S,H,Dh]."""
+    if q.is_contiguous():
+        return Q_BHSD
+    if q.transpose(1, 2).is_contiguous():
+        return Q_BSHD
+    raise _lib.HgaError("q must be contiguous [B,H,S,Dh] or a transposed view of contiguous [B,S,H,Dh]")
+
+
+def kv_cap_of(t: torch.Tensor) -> int:
+    """Rows allocated per (batch, kv-head) of a [B,KVH,S,Dh] view into a [B,KVH,cap,Dh] buffer."""
+    B, KVH, S, Dh = t.shape
+    if t.stride(3) != 1 or t.stride(2) != Dh or t.stride(1) % Dh or t.stride(0) != KVH * t.stride(1):
+        raise _lib.HgaError(f"K/V tensor must be a row-slice of a contiguous [B,KVH,cap,Dh] buffer; strides {t.stride()}")
+    return t.stride(1) // Dh
+
+
+def summaries(p: HgaParams, k_raw: torch.Tensor, k_rope: torch.Tensor, v: torch.Tensor,
+              cos: torch.Tensor, sin: torch.Tensor, *, seq_len: Optional[int] = None, pos0: int = 0,
+              rot_row0: int = 0, out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
+              out_chunk0: int = 0, with_group_v: bool = True):
+    """Chunk / group summaries of k_* [B,KVH,S,Dh] (see hga_summaries).  cos/sin [R, Dh].
+
+    Returns (chunk_k [B,KVH,N,Dh], group_k [B,KVH,N,M,Dh], group_v or None), or fills ``out``
+    (capacity buffers, chunk slots [out_chunk0, out_chunk0+N)).
+    """
+    _require_cuda(k_raw, k_rope, v, cos, sin)
+    B, KVH, S, Dh = k_raw.shape
+    S = S if seq_len is None else seq_len
+    C = p.chunk_size
+    M = C // p.group_size
+    N = (S + C - 1) // C
+    cap = kv_cap_of(k_raw)
+    if kv_cap_of(k_rope) != cap or kv_cap_of(v) != cap:
+        raise _lib.HgaError("k_raw / k_rope / v must share one capacity layout")
+    for t in (k_rope, v):
+        if t.dtype != k_raw.dtype:
+            raise _lib.HgaError("k_raw / k_rope / v dtypes differ")
+    if cos.dtype not in (torch.float32, k_raw.dtype) or sin.dtype != cos.dtype:
+        raise _lib.HgaError("cos/sin must be fp32 or the model dtype")
+    cos, sin = cos.contiguous(), sin.contiguous()
+    if out is None:
+        ck = torch.empty(B, KVH, N, Dh, device=k_raw.device, dtype=k_raw.dtype)
+        gk = torch.empty(B, KVH, N, M, Dh, device=k_raw.device, dtype=k_raw.dtype)
+        gv = torch.empty_like(gk) if with_group_v else None
+        sum_cap = N
+    else:
+        ck, gk, gv = out
+        sum_cap = ck.shape[2]
+    rot_dtype = _lib.DTYPE_CODE[cos.dtype]
+    check(lib().hga_summaries(ctypes_params(p), S, pos0, ptr(k_raw), ptr(k_rope), ptr(v), cap, ptr(cos), ptr(sin),
+                              rot_dtype, rot_row0, ptr(ck), ptr(gk), ptr(gv), sum_cap, out_chunk0,
+                              stream_ptr(k_raw.device)), "hga_summaries")
+    return ck, gk, gv
+
+
+def ctypes_params(p: HgaParams):
+    import ctypes
+    return ctypes.byref(p)
+
+
+def route_prefill(p: HgaParams, q: torch.Tensor, chunk_k: torch.Tensor, group_k: torch.Tensor,
+                  seq_len: Optional[int] = None, debug: bool = False) -> Dict[str, torch.Tensor]:
+    """Two-level prefill routing (see hga_route_prefill).  q [B,H,S,Dh] (or a BSHD view)."""
+    _require_cuda(q, chunk_k, group_k)
+    B, H, S, Dh = q.shape
+    S = S if seq_len is None else seq_len
+    N, Kc, Kg, _ = route_sizes(p, S)
+    dev = q.device
+    C = p.chunk_size
+    M = C // p.group_size
+    res = {
+        "sel_chunk": torch.empty(B, H, N, Kc, device=dev, dtype=torch.int32),
+        "sel_t0": torch.empty(B, H, N, Kc, device=dev, dtype=torch.int32),
+        "open_gid": torch.empty(B, H, N, Kg, device=dev, dtype=torch.int32),
+        "open_t0": torch.empty(B, H, N, Kg, device=dev, dtype=torch.int32),
+    }
+    if debug:
+        res["dbg_l1"] = torch.full((B, H, N, C, N), float("nan"), device=dev, dtype=torch.float32)
+        res["dbg_l2"] = torch.full((B, H, N, C, Kc * M), float("nan"), device=dev, dtype=torch.float32)
+    sum_cap = chunk_k.stride(1) // Dh
+    if (chunk_k.stride(-1) != 1 or chunk_k.stride(2) != Dh or group_k.stride(-1) != 1
+            or group_k.stride(1) != sum_cap * M * Dh or chunk_k.stride(0) != chunk_k.shape[1] * chunk_k.stride(1)):
+        raise _lib.HgaError("summaries must be row-slices of contiguous [B,KVH,cap,(M,)Dh] buffers")
+    check(lib().hga_route_prefill(ctypes_params(p), S, ptr(q), q_layout_of(q), ptr(chunk_k), ptr(group_k), sum_cap,
+                                  ptr(res["sel_chunk"]), ptr(res["sel_t0"]), ptr(res["open_gid"]),
+                                  ptr(res["open_t0"]), ptr(res.get("dbg_l1")), ptr(res.get("dbg_l2")),
+                                  stream_ptr(dev)), "hga_route_prefill")
+    return res
+
+
+def attend_prefill(p: HgaParams, q: torch.Tensor, k_rope: torch.Tensor, v: torch.Tensor,
+                   open_gid: torch.Tensor, open_t0: torch.Tensor, seq_len: Optional[int] = None,
+                   out_layout: int = Q_BSHD, impl: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Working-set attention (see hga_attend_prefill).  Returns [B,H,S,Dh] (a view of a BSHD
+    buffer when out_layout == 1)."""
+    _require_cuda(q, k_rope, v, open_gid, open_t0)
+    B, H, S, Dh = q.shape
+    S = S if seq_len is None else seq_len
+    cap = kv_cap_of(k_rope)
+    if kv_cap_of(v) != cap:
+        raise _lib.HgaError("k_rope and v must share one capacity layout")
+    if out is None:
+        if out_layout == Q_BSHD:
+            out = torch.empty(B, S, H, Dh, device=q.device, dtype=q.dtype)
+        else:
+            out = torch.empty(B, H, S, Dh, device=q.device, dtype=q.dtype)
+    check(lib().hga_attend_prefill(ctypes_params(p), S, ptr(q), q_layout_of(q), ptr(k_rope), ptr(v), cap,
+                                   ptr(open_gid), ptr(open_t0), ptr(out), out_layout, impl, stream_ptr(q.device)),
+          "hga_attend_prefill")
+    return out.transpose(1, 2) if out_layout == Q_BSHD else out

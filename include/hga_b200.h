@@ -1,0 +1,93 @@
+/*
+ * hga_b200.h — C ABI of the B200 (sm_100a) kernels for HGA's routed-attention hot path.
+ *
+ * Plain pointers and sizes only: every tensor is device memory owned by the caller (in the
+ * Python host layer: the PyTorch caching allocator), every call is asynchronous on the given
+ * CUDA stream, and nothing here allocates device memory.  Every entry point returns 0 on
+ * success or a negative HGA_E* code; hga_last_error() then holds a message for the calling
+ * host thread.
+ *
+ * Layout conventions (row-major, innermost last):
+ *   q                 [B, H,   S,   Dh]   (q_layout 0)  or [B, S, H, Dh] (q_layout 1)
+ *   k_raw, k_rope, v  [B, KVH, cap, Dh]   token rows of one (batch, kv-head) are contiguous;
+ *                                          `kv_cap` = rows allocated per (batch, kv-head)
+ *   chunk_k           [B, KVH, ccap, Dh]
+ *   group_k, group_v  [B, KVH, ccap, M, Dh] `sum_cap` = chunks allocated per (batch, kv-head)
+ *   rotary cos / sin  [R, Dh]             row r = absolute position rot_row0 + r
+ * N = ceil(S / chunk_size) query chunks; M = chunk_size / group_size groups per chunk.
+ */
+#ifndef HGA_B200_H_
+#define HGA_B200_H_
+
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { HGA_DTYPE_F32 = 0, HGA_DTYPE_BF16 = 1, HGA_DTYPE_F16 = 2 };
+enum { HGA_OK = 0, HGA_E_INVALID = -1, HGA_E_UNSUPPORTED = -2, HGA_E_CUDA = -3, HGA_E_DEVICE = -4 };
+
+/* Hyper-parameters of one routed-attention layer.  Mirrors RouterConfig + ChunkPlacementPolicy
+ * (ExistingModelFineTuning/KvRouter/chunk_router.py:59-90, chunk_placement_policy.py:13-38). */
+typedef struct hga_params {
+  int32_t batch, nhead, kv_heads, head_dim;
+  int32_t chunk_size, group_size;
+  int32_t topk_chunks, topk_groups;
+  int32_t keep_first, keep_last;
+  int32_t cutoff_pair; /* mixed-RoPE cutoff: pairs < cutoff_pair are summed token-wise (vectorized.py:146-165) */
+  int32_t dtype;       /* HGA_DTYPE_* of q / k / v / summaries / outputs */
+  float scale;         /* head_dim ** -0.5 (chunk_router.py:84-85) */
+  float group_kv_scale;/* 1 / (group_size + sqrt(group_size)) (chunk_router.py:87-90) */
+} hga_params;
+
+const char* hga_version(void);
+const char* hga_last_error(void);
+
+/* (1) Summary builder — mixed-RoPE chunk and group key summaries plus scaled group value sums.
+ * Replaces vectorized.py:265-287 (_rope_summary, :168-183) for the chunk-parallel prefill and
+ * ChunkRouter._rope_summary_at / _seed_store_from_block / _close_active_chunk
+ * (chunk_router.py:553-599, 631-657, 693-700) for the store.
+ * Summarises tokens [0, seq_len) of the K/V rows (a partial last chunk uses the middle of its
+ * valid tokens as anchor, vectorized.py:265-270) into chunk slots [out_chunk0, out_chunk0+N).
+ * Token 0 sits at absolute position pos0 (a multiple of chunk_size).  cos/sin are read at the
+ * anchor positions; rot_dtype = HGA_DTYPE_F32 for an fp32 table, or p->dtype for a table already
+ * cast to the model dtype (what HierarchicalGlobalAttentionRouted.py:168 hands the router). */
+int hga_summaries(const hga_params* p, int64_t seq_len, int64_t pos0,
+                  const void* k_raw, const void* k_rope, const void* v, int64_t kv_cap,
+                  const void* cos, const void* sin, int32_t rot_dtype, int64_t rot_row0,
+                  void* chunk_k, void* group_k, void* group_v, int64_t sum_cap, int64_t out_chunk0,
+                  cudaStream_t stream);
+
+/* (2) Two-level router of the chunk-parallel prefill (vectorized.py:296-384).
+ * For every (b, h, query chunk n) writes the selected routed chunks and the opened groups that
+ * some query row can see, each with t0 = first query row (0..chunk_size-1) of the chunk that sees
+ * it; rows t >= t0 see it (the reference's cumulative-OR visibility).  Lists are sorted by
+ * chunk / group id and padded with -1:
+ *   sel_chunk, sel_t0 [B, H, N, Kc]   Kc = min(topk_chunks, N)
+ *   open_gid,  open_t0 [B, H, N, Kg]  Kg = min(topk_groups, Kc*M); gid = chunk*M + group
+ * Ties are broken by higher score, then lower index.  dbg_l1 [B,H,N,C,N] / dbg_l2 [B,H,N,C,Kc*M]
+ * (fp32, may be NULL) receive the rounded routing scores (l2 in open-candidate order: selected
+ * chunks ascending, groups ascending) for the parity tests. */
+int hga_route_prefill(const hga_params* p, int64_t seq_len, const void* q, int32_t q_layout,
+                      const void* chunk_k, const void* group_k, int64_t sum_cap,
+                      int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid, int32_t* open_t0,
+                      float* dbg_l1, float* dbg_l2, cudaStream_t stream);
+
+/* (3)+(4) Working-set attention of the chunk-parallel prefill: replaces the token-segment
+ * assembly of vectorized.py:386-490 and RoutedKV.attend(use_summaries=False)
+ * (chunk_router.py:139-158).  Query row t of chunk n attends, with an fp32 online softmax, to
+ * the causal prefix of its own chunk, the keep_last window [l_lo, n), the keep_first window
+ * [0, f_hi) and every opened group with t0 <= t.  Output [B,H,S,Dh] (out_layout 0) or
+ * [B,S,H,Dh] (out_layout 1) in p->dtype.  impl: 0 = auto, 1 = portable SIMT kernel,
+ * 2 = tcgen05/TMEM tensor-core kernel (bf16, head_dim 128, chunk 64, group 16). */
+int hga_attend_prefill(const hga_params* p, int64_t seq_len, const void* q, int32_t q_layout,
+                       const void* k_rope, const void* v, int64_t kv_cap,
+                       const int32_t* open_gid, const int32_t* open_t0,
+                       void* out, int32_t out_layout, int32_t impl, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HGA_B200_H_ */

@@ -1,0 +1,49 @@
+"""The C-ABI library loads and exports every entry point include/hga_b200.h declares (no GPU)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    names = []
+    for fn in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if fn.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", fn)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names += re.findall(r"\b(hga_[a-z0-9_]+)\s*\(", src)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    from hierarchicalglobalattention_b200 import _lib
+    h = _lib.lib()
+    declared = _declared()
+    assert declared, "no declarations found"
+    missing = [n for n in declared if not hasattr(h, n)]
+    assert not missing, missing
+    assert set(_lib.exported_symbols()) <= set(declared)
+
+
+def test_invalid_arguments_fail_loudly_without_touching_the_device():
+    from hierarchicalglobalattention_b200 import _lib
+    h = _lib.lib()
+    rc = h.hga_summaries(None, 10, 0, None, None, None, 10, None, None, 0, 0, None, None, None, 1, 0, None)
+    assert rc == -1 and b"NULL" in h.hga_last_error()
+    p = _lib.make_params(batch=1, nhead=3, kv_heads=2, head_dim=16, chunk_size=8, group_size=4, topk_chunks=1,
+                         topk_groups=2, keep_first=0, keep_last=0, theta=1e4, dtype=__import__("torch").float32)
+    rc = h.hga_route_prefill(ctypes.byref(p), 16, 1, 0, 1, 1, 2, 1, 1, 1, 1, None, None, None)
+    assert rc == -1 and b"kv_heads" in h.hga_last_error()
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    from hierarchicalglobalattention_b200 import _lib, ops
+    p = _lib.make_params(batch=1, nhead=2, kv_heads=1, head_dim=16, chunk_size=8, group_size=4, topk_chunks=1,
+                         topk_groups=2, keep_first=0, keep_last=0, theta=1e4, dtype=torch.float32)
+    k = torch.zeros(1, 1, 16, 16)
+    with pytest.raises(_lib.HgaError, match="CUDA"):
+        ops.summaries(p, k, k, k, torch.zeros(16, 16), torch.zeros(16, 16))
