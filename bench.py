@@ -1,0 +1,318 @@
+"""Benchmark: HGA routed-attention layer prefill at 32K (Qwen3-30B-A3B attention shape) on B200.
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--seq S]
+
+One step = one forward of ``HierarchicalGlobalAttentionRouted`` (fused QKV GEMM, q/k RMSNorm +
+RoPE prologue, summary builder, two-level router, working-set attention, o_proj) over one
+synthetic batch (seeded N(0,1) hidden states, N(0,0.02) weights).
+Prints ONE JSON line (rank 0).  See DESIGN.md for the metric definitions.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG1 = dict(d_model=2048, nhead=32, kv_heads=4, head_dim=128, qk_norm=True, theta=1e6, chunk_size=64,
+            group_size=16, keep_first=2, keep_last=8, topk_chunks=16, topk_groups=64)
+METRIC = "HGA prefill tokens/s @32K Qwen3-30B attn"
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def build_module(device, dtype, seed=0):
+    from hierarchicalglobalattention_b200 import HierarchicalGlobalAttentionRouted
+    torch.manual_seed(seed)
+    m = HierarchicalGlobalAttentionRouted(**CFG1)
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if "norm" not in n:
+                p.normal_(0.0, 0.02)
+    return m.to(device=device, dtype=dtype).eval()
+
+
+def visible_pairs(routed, S, C, kf, kl, gs):
+    """Sum over query rows of visible keys (algorithmic attention work) from the routing lists."""
+    t0 = routed.routing["open_t0"]
+    valid = t0 >= 0
+    cnt = torch.where(valid, (C - t0).clamp_min(0) * gs, torch.zeros_like(t0)).sum().item()
+    N = (S + C - 1) // C
+    B, H = t0.shape[:2]
+    pairs = cnt
+    for n in range(N):
+        nv = min(C, S - n * C)
+        f_hi = min(n, kf) if kf > 0 else 0
+        l_lo = min(max(n - kl, kf), n) if kl > 0 else n
+        pairs += B * H * (nv * (nv + 1) // 2 + nv * C * ((n - l_lo) + f_hi))
+    # rows past the valid tail of the last chunk never count: opened-group rows use C - t0; fix the tail
+    return int(pairs)
+
+
+def run_ours(args, rank, world, device):
+    import hierarchicalglobalattention_b200 as hga
+    from hierarchicalglobalattention_b200 import router as router_mod
+    dtype = torch.bfloat16
+    S = args.seq
+    m = build_module(device, dtype)
+    g = torch.Generator(device="cpu").manual_seed(1234 + rank)
+    x_host = torch.randn(1, S, CFG1["d_model"], generator=g).to(dtype).pin_memory()
+    x = x_host.to(device)
+    out_host = torch.empty(1, S, CFG1["d_model"], dtype=dtype).pin_memory()
+
+    # instrument the attention launch with CUDA events on its stream
+    att_events = []
+    orig_attend = router_mod.RoutedKV.attend
+    last = {}
+
+    def timed_attend(self, q, use_summaries=False):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = orig_attend(self, q, use_summaries)
+        e1.record()
+        att_events.append((e0, e1))
+        last["routed"] = self
+        return r
+
+    router_mod.RoutedKV.attend = timed_attend
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            m(x)
+        torch.cuda.synchronize()
+        att_events.clear()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(device.index or 0) as clk:
+            st.record()
+            for _ in range(args.steps):
+                m(x)
+            en.record()
+            torch.cuda.synchronize()
+        dev_ms = st.elapsed_time(en)
+        att_ms = [a.elapsed_time(b) for a, b in att_events]
+        # end-to-end through the public module: pinned H2D of the step's input, D2H of its output
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        e_st, e_en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_st.record()
+        for _ in range(args.steps):
+            xi = x_host.to(device, non_blocking=True)
+            y, _ = m(xi)
+            out_host.copy_(y, non_blocking=True)
+        e_en.record()
+        torch.cuda.synchronize()
+        e2e_ms = e_st.elapsed_time(e_en)
+    router_mod.RoutedKV.attend = orig_attend
+    routed = last["routed"]
+    pairs = visible_pairs(routed, S, CFG1["chunk_size"], CFG1["keep_first"], CFG1["keep_last"], CFG1["group_size"])
+    t = torch.tensor([dev_ms, e2e_ms], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    dev_ms, e2e_ms = t.tolist()
+    return dict(dev_ms=dev_ms, e2e_ms=e2e_ms, att_ms=statistics.mean(att_ms), pairs=pairs, clocks=clk.summary(),
+                launches_per_step=5, h2d=x_host.numel() * 2, d2h=out_host.numel() * 2)
+
+
+def cpu_sample(seconds_hint: float = 20.0, S: int = 32768, n_sample_chunks: int = 6):
+    """Oracle port of the reference path on the host cores, on a bounded sample of the workload.
+
+    The sample: the full-sequence projections + q/k RMSNorm + RoPE + summaries (every key of the
+    32K context is needed by the routed chunks), then routing + attention + o_proj for
+    ``n_sample_chunks`` steady-state query chunks, extrapolated linearly to all chunks.
+    """
+    from oracle import hga_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    p = O.OracleParams(nhead=32, kv_heads=4, head_dim=128, chunk_size=64, group_size=16, topk_chunks=16,
+                       topk_groups=64, keep_first=2, keep_last=8, theta=1e6)
+    dtype = torch.bfloat16
+    g = torch.Generator().manual_seed(7)
+    D = CFG1["d_model"]
+    x = torch.randn(1, S, D, generator=g).to(dtype)
+    wq = (torch.randn(32 * 128, D, generator=g) * 0.02).to(dtype)
+    wk = (torch.randn(4 * 128, D, generator=g) * 0.02).to(dtype)
+    wv = (torch.randn(4 * 128, D, generator=g) * 0.02).to(dtype)
+    wo = (torch.randn(D, 32 * 128, generator=g) * 0.02).to(dtype)
+    ones = torch.ones(128, dtype=dtype)
+    N = S // 64
+    chunks = list(range(N - n_sample_chunks, N))
+    t0 = time.perf_counter()
+    B = 1
+    q_raw = O.rms_norm((x @ wq.t()).view(B, S, 32, 128), ones, 1e-6).transpose(1, 2)
+    k_raw = O.rms_norm((x @ wk.t()).view(B, S, 4, 128), ones, 1e-6).transpose(1, 2)
+    v = (x @ wv.t()).view(B, S, 4, 128).transpose(1, 2)
+    cos, sin = O.module_rotary(p.theta, 128, S)
+    q_rope = O._rotate(q_raw.float(), cos, sin).to(dtype)
+    k_rope = O._rotate(k_raw.float(), cos, sin).to(dtype)
+    ck, gk, _ = O.summaries_prefill(p, k_raw.contiguous(), k_rope.contiguous(), v.contiguous(), cos.to(dtype),
+                                    sin.to(dtype))
+    t1 = time.perf_counter()
+    route = O.route_prefill(p, q_rope, ck, gk, S, chunks=chunks, ties=False)
+    heads = O.attend_prefill(p, q_rope, k_rope.contiguous(), v.contiguous(), route, S, chunks=chunks)
+    rows = slice(chunks[0] * 64, S)
+    _ = heads[:, :, rows].transpose(1, 2).reshape(B, -1, 32 * 128) @ wo.t()
+    t2 = time.perf_counter()
+    total = (t1 - t0) + (t2 - t1) * N / len(chunks)
+    return {"value": S / total, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": (f"oracle restatement, bf16, S={S}: full-sequence projections/norm/RoPE/summaries "
+                       f"({t1 - t0:.1f}s) + routing/attention/o_proj of {len(chunks)} of {N} query chunks "
+                       f"({t2 - t1:.1f}s) extrapolated linearly"),
+            "measured_s": t2 - t0}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seq", type=int, default=32768)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    config = {"workload": "configs[1]: one Qwen3-30B-A3B-shaped HGA attention layer, prefill",
+              "model": "HierarchicalGlobalAttentionRouted(d_model=2048, nhead=32, kv_heads=4, head_dim=128, qk_norm)",
+              "global_batch": world, "seq_len": args.seq, "parallelism": f"replicas{world}" if world > 1 else "single",
+              "routing": "chunk 64, group 16, keep_first 2, keep_last 8, topk_chunks 16, topk_groups 64",
+              "l2": "inputs larger than L2 (134 MB hidden states per step)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        vals = []
+        for i in range(args.warmup + args.steps):
+            r = cpu_sample(S=args.seq)
+            if i >= args.warmup:
+                vals.append(r)
+        v = statistics.mean(r["value"] for r in vals)
+        cb = dict(vals[-1])
+        cb["value"] = v
+        cb.pop("measured_s", None)
+        print(json.dumps({"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+                          "warmup": args.warmup, "ms_per_step": args.seq / v * 1e3, "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                          "config": config, "impl": "reference", "cpu_baseline": cb,
+                          "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    if world > 1:
+        torch.distributed.init_process_group("nccl")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    import hierarchicalglobalattention_b200.build as hb
+    hb.build()
+    r = run_ours(args, rank, world, device)
+    if rank != 0:
+        torch.distributed.destroy_process_group()
+        return
+    hbm, tf_burst, tf_sus, kind = _peaks()
+    S = args.seq
+    tokens = S * world * args.steps
+    value = tokens / (r["dev_ms"] / 1e3)
+    e2e = tokens / (r["e2e_ms"] / 1e3)
+    flops = 4 * CFG1["head_dim"] * r["pairs"]
+    achieved = flops / (r["att_ms"] / 1e3) / 1e12
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "attention_traffic.json")) as f:
+            traffic = json.load(f).get("bytes_per_launch")
+    except Exception:
+        pass
+    cpu = None
+    if not args.no_cpu_baseline:
+        try:
+            cpu = cpu_sample(S=S)
+            cpu.pop("measured_s", None)
+        except Exception as e:  # keep the GPU line even if the host sample fails
+            cpu = {"error": str(e)[:200]}
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["dev_ms"] / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+            "roofline": {"kernel": "hga attention (working-set)", "bound": "tensor", "achieved": achieved,
+                         "peak": tf_sus, "unit": "TFLOP/s", "frac": achieved / tf_sus, "traffic": traffic,
+                         "peak_kind": f"{kind} bf16 sustained", "attention_ms": r["att_ms"],
+                         "visible_pairs": r["pairs"]},
+            "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["launches_per_step"] * args.steps}
+    print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

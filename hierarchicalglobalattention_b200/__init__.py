@@ -7,5 +7,10 @@ ABI of ``libhga_b200.so`` (include/hga_b200.h); PyTorch provides device memory, 
 projection GEMMs.
 """
 from . import _lib, ops  # noqa: F401
+from .config import ChunkPlacementPolicy, RouterConfig
+from .module import HierarchicalGlobalAttentionRouted
+from .router import ChunkRouter, RoutedKV
+from .store import KVCacheStore, VramKVCacheStore
 
-__all__ = ["_lib", "ops"]
+__all__ = ["ChunkPlacementPolicy", "RouterConfig", "HierarchicalGlobalAttentionRouted", "ChunkRouter",
+           "RoutedKV", "KVCacheStore", "VramKVCacheStore", "ops"]

@@ -47,7 +47,11 @@ _SIGNATURES = {
                                          _P, _P, _P]),
     "hga_attend_prefill": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _P, _I32, _P, _P, _I64, _P, _P, _P, _I32,
                                           _I32, _P]),
+    "hga_qkv_prologue": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _P, _I64, _P, _P, ctypes.c_float, _I32, _P,
+                                        _P, _I32, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _P]),
 }
+
+ROT_F32, ROT_MODEL, ROT_F32_ROUNDED = 0, 1, 2
 
 
 def exported_symbols():

@@ -17,6 +17,10 @@ cudaError_t launch_route_prefill(const hga_params& p, int64_t S, const void* q, 
 cudaError_t launch_attend_simt(const hga_params& p, int64_t S, const void* q, int q_layout, const void* k_rope,
                                const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0,
                                int Kg, void* out, int out_layout, cudaStream_t st);
+cudaError_t launch_prologue(const hga_params& p, int64_t S, const void* qkv, int64_t row_stride, const void* qw,
+                            const void* kw, float eps, int norm_mode, const void* cos, const void* sin,
+                            int rope_mode, int64_t rot_row0, int64_t pos0, void* q_out, void* kraw_out,
+                            void* krope_out, void* v_out, int64_t kv_cap, int64_t kv_row0, cudaStream_t st);
 bool attend_tc_supported(const hga_params& p);
 cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const void* q, int q_layout, const void* k_rope,
                              const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0,
@@ -72,7 +76,7 @@ const char* hga_version(void) { return "hga_b200 0.1 (sm_100a)"; }
 const char* hga_last_error(void) { return g_err; }
 
 int hga_summaries(const hga_params* p, int64_t seq_len, int64_t pos0, const void* k_raw, const void* k_rope,
-                  const void* v, int64_t kv_cap, const void* cos, const void* sin, int32_t rot_dtype,
+                  const void* v, int64_t kv_cap, const void* cos, const void* sin, int32_t rot_mode,
                   int64_t rot_row0, void* chunk_k, void* group_k, void* group_v, int64_t sum_cap,
                   int64_t out_chunk0, cudaStream_t stream) {
   int rc = check_params(p);
@@ -85,9 +89,9 @@ int hga_summaries(const hga_params* p, int64_t seq_len, int64_t pos0, const void
   if (pos0 < rot_row0) return fail(HGA_E_INVALID, "hga_summaries: rotary table starts after pos0");
   const int64_t N = (seq_len + p->chunk_size - 1) / p->chunk_size;
   if (out_chunk0 < 0 || out_chunk0 + N > sum_cap) return fail(HGA_E_INVALID, "hga_summaries: summary capacity too small");
-  if (rot_dtype != HGA_DTYPE_F32 && rot_dtype != p->dtype)
-    return fail(HGA_E_INVALID, "hga_summaries: rot_dtype must be fp32 or the model dtype");
-  return cuda_status(hga::launch_summaries(*p, seq_len, pos0, k_raw, k_rope, v, kv_cap, cos, sin, rot_dtype, rot_row0,
+  if (rot_mode < HGA_ROT_F32 || rot_mode > HGA_ROT_F32_ROUNDED)
+    return fail(HGA_E_INVALID, "hga_summaries: unknown rot_mode %d", rot_mode);
+  return cuda_status(hga::launch_summaries(*p, seq_len, pos0, k_raw, k_rope, v, kv_cap, cos, sin, rot_mode, rot_row0,
                                            chunk_k, group_k, group_v, sum_cap, out_chunk0, stream),
                      "hga_summaries");
 }
@@ -138,6 +142,25 @@ int hga_attend_prefill(const hga_params* p, int64_t seq_len, const void* q, int3
   return cuda_status(hga::launch_attend_simt(*p, seq_len, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg, out,
                                              out_layout, stream),
                      "hga_attend_prefill");
+}
+
+int hga_qkv_prologue(const hga_params* p, int64_t seq_len, const void* qkv, int64_t row_stride, const void* q_norm_w,
+                     const void* k_norm_w, float eps, int32_t norm_mode, const void* cos, const void* sin,
+                     int32_t rope_mode, int64_t rot_row0, int64_t pos0, void* q_rope, void* k_raw, void* k_rope,
+                     void* v, int64_t kv_cap, int64_t kv_row0, cudaStream_t stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (seq_len <= 0) return HGA_OK;
+  if (!qkv || !cos || !sin || !q_rope || !k_raw || !k_rope || !v) return fail(HGA_E_INVALID, "hga_qkv_prologue: NULL tensor");
+  if (row_stride < (int64_t)(p->nhead + 2 * p->kv_heads) * p->head_dim)
+    return fail(HGA_E_INVALID, "hga_qkv_prologue: row_stride smaller than (H + 2*KVH) * Dh");
+  if (kv_row0 < 0 || kv_row0 + seq_len > kv_cap) return fail(HGA_E_INVALID, "hga_qkv_prologue: kv capacity too small");
+  if (pos0 < rot_row0) return fail(HGA_E_INVALID, "hga_qkv_prologue: rotary table starts after pos0");
+  if ((norm_mode != 0 && norm_mode != 1) || (rope_mode != 0 && rope_mode != 1))
+    return fail(HGA_E_INVALID, "hga_qkv_prologue: norm_mode / rope_mode must be 0 or 1");
+  return cuda_status(hga::launch_prologue(*p, seq_len, qkv, row_stride, q_norm_w, k_norm_w, eps, norm_mode, cos, sin,
+                                          rope_mode, rot_row0, pos0, q_rope, k_raw, k_rope, v, kv_cap, kv_row0, stream),
+                     "hga_qkv_prologue");
 }
 
 }  // extern "C"

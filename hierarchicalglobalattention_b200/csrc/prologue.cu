@@ -1,0 +1,113 @@
+// Fused projection epilogue: q/k RMSNorm + RoPE + head-major K/V layout in one pass.
+//
+// Input: the fused QKV projection output, one row per token: [q heads | k heads | v heads] x Dh.
+// Output: q_rope [B,S,H,Dh] (token-major, what the router and attention read through q_layout 1),
+// and k_raw / k_rope / v rows [B,KVH,cap,Dh] (the KV-store layout).
+// Reference arithmetic (one rounding per torch op):
+//   norm_mode 0 (HierarchicalGlobalAttentionRouted.py:56-67, :151-152):
+//       y = T( (fp32(w) * x) * rsqrt(mean(x^2) + eps) )
+//   norm_mode 1 (HF Qwen3MoeRMSNorm, used by qwen_routed_attention.py:171-172):
+//       y = T( w * T( x * rsqrt(mean(x^2) + eps) ) )
+//   rope_mode 0 (HierarchicalGlobalAttentionRouted.py:156-157): fp32 math on fp32 cos/sin, one rounding
+//   rope_mode 1 (HF apply_rotary_pos_emb, qwen_routed_attention.py:176): model-dtype math,
+//       y = T( T(x*cos) + T(rot(x)*sin) ) with cos/sin in the model dtype.
+// rsqrt is evaluated as a correctly rounded 1/sqrt (what torch's CPU kernel computes).
+// One warp per (token, projected head row); the row is staged in smem for the rotate-half partner.
+#include "hga_common.cuh"
+
+namespace hga {
+
+constexpr int kProWarps = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(kProWarps * 32) prologue_kernel(
+    hga_params p, int64_t S, const T* __restrict__ qkv, int64_t row_stride, const T* __restrict__ qw,
+    const T* __restrict__ kw, float eps, int norm_mode, const void* __restrict__ cos_t,
+    const void* __restrict__ sin_t, int rope_mode, int64_t rot_row0, int64_t pos0, T* __restrict__ q_out,
+    T* __restrict__ kraw_out, T* __restrict__ krope_out, T* __restrict__ v_out, int64_t kv_cap, int64_t kv_row0) {
+  extern __shared__ float prow[];
+  const int H = p.nhead, KVH = p.kv_heads, Dh = p.head_dim, half = Dh / 2;
+  const int rows_per_tok = H + 2 * KVH;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* buf = prow + warp * Dh;
+  const int64_t gw = (int64_t)blockIdx.x * kProWarps + warp;
+  const int64_t total = (int64_t)p.batch * S * rows_per_tok;
+  if (gw >= total) return;
+  const int r = (int)(gw % rows_per_tok);
+  const int64_t bt = gw / rows_per_tok;  // b * S + t
+  const int64_t t = bt % S;
+  const int b = (int)(bt / S);
+  const T* src = qkv + bt * row_stride + (int64_t)r * Dh;
+  const bool is_q = r < H, is_k = r >= H && r < H + KVH;
+  const int kvh = is_q ? 0 : (is_k ? r - H : r - H - KVH);
+  // load + optional RMSNorm
+  const T* w = is_q ? qw : (is_k ? kw : nullptr);
+  float ss = 0.f;
+  for (int d = lane; d < Dh; d += 32) {
+    const float x = Num<T>::to_f(src[d]);
+    buf[d] = x;
+    ss = __fadd_rn(ss, __fmul_rn(x, x));
+  }
+  if (!is_q && !is_k) {  // v: layout transform only
+    T* dst = v_out + (((int64_t)b * KVH + kvh) * kv_cap + kv_row0 + t) * Dh;
+    for (int d = lane; d < Dh; d += 32) dst[d] = src[d];
+    return;
+  }
+  if (w) {
+    for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const float mean = __fdiv_rn(ss, (float)Dh);
+    const float rs = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    for (int d = lane; d < Dh; d += 32) {
+      const float x = buf[d];
+      const float wf = Num<T>::to_f(w[d]);
+      float y;
+      if (norm_mode == 0) y = Num<T>::round(__fmul_rn(__fmul_rn(wf, x), rs));
+      else y = Num<T>::round(__fmul_rn(wf, Num<T>::round(__fmul_rn(x, rs))));
+      buf[d] = y;
+    }
+  }
+  __syncwarp();
+  // RoPE
+  const int64_t rr = (pos0 + t - rot_row0) * Dh;
+  T* dst_rope;
+  if (is_q) dst_rope = q_out + (bt * H + r) * Dh;
+  else dst_rope = krope_out + (((int64_t)b * KVH + kvh) * kv_cap + kv_row0 + t) * Dh;
+  T* dst_raw = is_k ? kraw_out + (((int64_t)b * KVH + kvh) * kv_cap + kv_row0 + t) * Dh : nullptr;
+  for (int d = lane; d < Dh; d += 32) {
+    const float x = buf[d];
+    const float xp = d < half ? -buf[d + half] : buf[d - half];
+    float y;
+    if (rope_mode == 0) {
+      const float cs = ((const float*)cos_t)[rr + d], sn = ((const float*)sin_t)[rr + d];
+      y = __fadd_rn(__fmul_rn(x, cs), __fmul_rn(xp, sn));
+    } else {
+      const float cs = Num<T>::to_f(((const T*)cos_t)[rr + d]), sn = Num<T>::to_f(((const T*)sin_t)[rr + d]);
+      y = __fadd_rn(Num<T>::round(__fmul_rn(x, cs)), Num<T>::round(__fmul_rn(xp, sn)));
+    }
+    dst_rope[d] = Num<T>::from_f(y);
+    if (dst_raw) dst_raw[d] = Num<T>::from_f(x);
+  }
+}
+
+cudaError_t launch_prologue(const hga_params& p, int64_t S, const void* qkv, int64_t row_stride, const void* qw,
+                            const void* kw, float eps, int norm_mode, const void* cos, const void* sin,
+                            int rope_mode, int64_t rot_row0, int64_t pos0, void* q_out, void* kraw_out,
+                            void* krope_out, void* v_out, int64_t kv_cap, int64_t kv_row0, cudaStream_t st) {
+  const int64_t rows = (int64_t)p.batch * S * (p.nhead + 2 * p.kv_heads);
+  const int64_t blocks = (rows + kProWarps - 1) / kProWarps;
+  const size_t smem = (size_t)kProWarps * p.head_dim * sizeof(float);
+#define HGA_PRO(T)                                                                                              \
+  prologue_kernel<T><<<(unsigned)blocks, kProWarps * 32, smem, st>>>(                                          \
+      p, S, (const T*)qkv, row_stride, (const T*)qw, (const T*)kw, eps, norm_mode, cos, sin, rope_mode, rot_row0, \
+      pos0, (T*)q_out, (T*)kraw_out, (T*)krope_out, (T*)v_out, kv_cap, kv_row0);                                \
+  return cudaGetLastError();
+  switch (p.dtype) {
+    case HGA_DTYPE_F32: HGA_PRO(float)
+    case HGA_DTYPE_BF16: HGA_PRO(__nv_bfloat16)
+    case HGA_DTYPE_F16: HGA_PRO(__half)
+  }
+#undef HGA_PRO
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace hga

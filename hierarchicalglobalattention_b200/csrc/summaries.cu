@@ -22,7 +22,7 @@ __global__ void __launch_bounds__(256) summaries_kernel(
     hga_params p, int64_t S, int64_t pos0, const T* __restrict__ k_raw, const T* __restrict__ k_rope,
     const T* __restrict__ v, int64_t kv_cap, const R* __restrict__ cos_t, const R* __restrict__ sin_t,
     int64_t rot_row0, T* __restrict__ chunk_k, T* __restrict__ group_k, T* __restrict__ group_v,
-    int64_t sum_cap, int64_t out_chunk0, int N) {
+    int64_t sum_cap, int64_t out_chunk0, int N, int round_tab) {
   extern __shared__ float sm_sum[];  // [2][Dh]: raw sums for the rotation partner exchange
   const int Dh = p.head_dim, C = p.chunk_size, gs = p.group_size, M = C / gs, half = Dh / 2;
   const int d = threadIdx.x;
@@ -79,7 +79,8 @@ __global__ void __launch_bounds__(256) summaries_kernel(
     __syncthreads();
     if (active) {
       const int64_t rr = (pos0 + anchor - rot_row0) * Dh + d;
-      const float cs = Num<R>::to_f(cos_t[rr]), sn = Num<R>::to_f(sin_t[rr]);
+      float cs = Num<R>::to_f(cos_t[rr]), sn = Num<R>::to_f(sin_t[rr]);
+      if (round_tab) { cs = Num<T>::round(cs); sn = Num<T>::round(sn); }
       float ep;
       if (d < half) ep = __fsub_rn(__fmul_rn(rs, cs), __fmul_rn(sm_sum[d + half], sn));
       else          ep = __fadd_rn(__fmul_rn(rs, cs), __fmul_rn(sm_sum[d - half], sn));
@@ -104,7 +105,8 @@ __global__ void __launch_bounds__(256) summaries_kernel(
   __syncthreads();
   if (active) {
     const int64_t rr = (pos0 + anchor - rot_row0) * Dh + d;
-    const float cs = Num<R>::to_f(cos_t[rr]), sn = Num<R>::to_f(sin_t[rr]);
+    float cs = Num<R>::to_f(cos_t[rr]), sn = Num<R>::to_f(sin_t[rr]);
+      if (round_tab) { cs = Num<T>::round(cs); sn = Num<T>::round(sn); }
     float ep;
     if (d < half) ep = __fsub_rn(__fmul_rn(rs, cs), __fmul_rn(sm_sum[d + half], sn));
     else          ep = __fadd_rn(__fmul_rn(rs, cs), __fmul_rn(sm_sum[d - half], sn));
@@ -118,26 +120,27 @@ template <typename T, typename R>
 static cudaError_t launch_summaries_t(const hga_params& p, int64_t S, int64_t pos0, const void* k_raw,
                                       const void* k_rope, const void* v, int64_t kv_cap, const void* cos,
                                       const void* sin, int64_t rot_row0, void* ck, void* gk, void* gv,
-                                      int64_t sum_cap, int64_t out_chunk0, cudaStream_t st) {
+                                      int64_t sum_cap, int64_t out_chunk0, int round_tab, cudaStream_t st) {
   const int N = (int)((S + p.chunk_size - 1) / p.chunk_size);
   const int threads = ((p.head_dim + 31) / 32) * 32;
   const dim3 grid((unsigned)(N * p.batch * p.kv_heads));
   summaries_kernel<T, R><<<grid, threads, 2 * p.head_dim * sizeof(float), st>>>(
       p, S, pos0, (const T*)k_raw, (const T*)k_rope, (const T*)v, kv_cap, (const R*)cos, (const R*)sin,
-      rot_row0, (T*)ck, (T*)gk, (T*)gv, sum_cap, out_chunk0, N);
+      rot_row0, (T*)ck, (T*)gk, (T*)gv, sum_cap, out_chunk0, N, round_tab);
   return cudaGetLastError();
 }
 
 cudaError_t launch_summaries(const hga_params& p, int64_t S, int64_t pos0, const void* k_raw,
                              const void* k_rope, const void* v, int64_t kv_cap, const void* cos,
-                             const void* sin, int rot_dtype, int64_t rot_row0, void* ck, void* gk,
+                             const void* sin, int rot_mode, int64_t rot_row0, void* ck, void* gk,
                              void* gv, int64_t sum_cap, int64_t out_chunk0, cudaStream_t st) {
+  const int round_tab = rot_mode == HGA_ROT_F32_ROUNDED;
 #define HGA_SUM(T)                                                                                    \
-  return rot_dtype == HGA_DTYPE_F32                                                                   \
+  return rot_mode != HGA_ROT_MODEL                                                                     \
              ? launch_summaries_t<T, float>(p, S, pos0, k_raw, k_rope, v, kv_cap, cos, sin, rot_row0, \
-                                            ck, gk, gv, sum_cap, out_chunk0, st)                      \
+                                            ck, gk, gv, sum_cap, out_chunk0, round_tab, st)           \
              : launch_summaries_t<T, T>(p, S, pos0, k_raw, k_rope, v, kv_cap, cos, sin, rot_row0, ck, \
-                                        gk, gv, sum_cap, out_chunk0, st);
+                                        gk, gv, sum_cap, out_chunk0, 0, st);
   switch (p.dtype) {
     case HGA_DTYPE_F32: HGA_SUM(float)
     case HGA_DTYPE_BF16: HGA_SUM(__nv_bfloat16)

@@ -57,11 +57,12 @@ def kv_cap_of(t: torch.Tensor) -> int:
 def summaries(p: HgaParams, k_raw: torch.Tensor, k_rope: torch.Tensor, v: torch.Tensor,
               cos: torch.Tensor, sin: torch.Tensor, *, seq_len: Optional[int] = None, pos0: int = 0,
               rot_row0: int = 0, out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
-              out_chunk0: int = 0, with_group_v: bool = True):
+              out_chunk0: int = 0, with_group_v: bool = True, round_table: bool = False):
     """Chunk / group summaries of k_* [B,KVH,S,Dh] (see hga_summaries).  cos/sin [R, Dh].
 
     Returns (chunk_k [B,KVH,N,Dh], group_k [B,KVH,N,M,Dh], group_v or None), or fills ``out``
-    (capacity buffers, chunk slots [out_chunk0, out_chunk0+N)).
+    (capacity buffers, chunk slots [out_chunk0, out_chunk0+N)).  ``round_table`` rounds an fp32
+    table to the model dtype at use (the chunk-parallel path's ``cos.to(x.dtype)``).
     """
     _require_cuda(k_raw, k_rope, v, cos, sin)
     B, KVH, S, Dh = k_raw.shape
@@ -86,9 +87,12 @@ def summaries(p: HgaParams, k_raw: torch.Tensor, k_rope: torch.Tensor, v: torch.
     else:
         ck, gk, gv = out
         sum_cap = ck.shape[2]
-    rot_dtype = _lib.DTYPE_CODE[cos.dtype]
+    if cos.dtype == torch.float32 and k_raw.dtype != torch.float32:
+        rot_mode = _lib.ROT_F32_ROUNDED if round_table else _lib.ROT_F32
+    else:
+        rot_mode = _lib.ROT_MODEL if cos.dtype != torch.float32 else _lib.ROT_F32
     check(lib().hga_summaries(ctypes_params(p), S, pos0, ptr(k_raw), ptr(k_rope), ptr(v), cap, ptr(cos), ptr(sin),
-                              rot_dtype, rot_row0, ptr(ck), ptr(gk), ptr(gv), sum_cap, out_chunk0,
+                              rot_mode, rot_row0, ptr(ck), ptr(gk), ptr(gv), sum_cap, out_chunk0,
                               stream_ptr(k_raw.device)), "hga_summaries")
     return ck, gk, gv
 
@@ -148,3 +152,46 @@ def attend_prefill(p: HgaParams, q: torch.Tensor, k_rope: torch.Tensor, v: torch
                                    ptr(open_gid), ptr(open_t0), ptr(out), out_layout, impl, stream_ptr(q.device)),
           "hga_attend_prefill")
     return out.transpose(1, 2) if out_layout == Q_BSHD else out
+
+
+def qkv_prologue(p: HgaParams, qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, *,
+                 q_norm_w: Optional[torch.Tensor] = None, k_norm_w: Optional[torch.Tensor] = None,
+                 eps: float = 1e-6, norm_mode: int = 0, rope_mode: int = 0, rot_row0: int = 0, pos0: int = 0,
+                 kv_out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None, kv_row0: int = 0):
+    """Fused q/k RMSNorm + RoPE + layout (see hga_qkv_prologue).
+
+    qkv [B, S, (H + 2*KVH) * Dh] (a fused projection output).  Returns (q_rope [B,H,S,Dh] view of a
+    [B,S,H,Dh] buffer, k_raw, k_rope, v [B,KVH,S,Dh] row-slices of the kv_out buffers or fresh
+    tensors)."""
+    _require_cuda(qkv, cos, sin)
+    B, S, W = qkv.shape
+    H, KVH, Dh = p.nhead, p.kv_heads, p.head_dim
+    if qkv.stride(2) != 1 or qkv.stride(0) != S * qkv.stride(1):
+        raise _lib.HgaError("qkv must be contiguous in its token rows")
+    row_stride = qkv.stride(1)
+    if W < (H + 2 * KVH) * Dh:
+        raise _lib.HgaError("qkv rows are narrower than (H + 2*KVH) * Dh")
+    want_rope_dtype = torch.float32 if rope_mode == 0 else qkv.dtype
+    if cos.dtype != want_rope_dtype or sin.dtype != want_rope_dtype:
+        raise _lib.HgaError(f"rope_mode {rope_mode} needs a {want_rope_dtype} table")
+    cos, sin = cos.contiguous(), sin.contiguous()
+    dev = qkv.device
+    q = torch.empty(B, S, H, Dh, device=dev, dtype=qkv.dtype)
+    if kv_out is None:
+        kraw = torch.empty(B, KVH, S, Dh, device=dev, dtype=qkv.dtype)
+        krope = torch.empty_like(kraw)
+        v = torch.empty_like(kraw)
+        cap = S
+    else:
+        kraw, krope, v = kv_out
+        cap = kv_cap_of(kraw)
+    for w in (q_norm_w, k_norm_w):
+        if w is not None and (w.numel() != Dh or w.dtype != qkv.dtype or not w.is_contiguous()):
+            raise _lib.HgaError("norm weights must be contiguous [Dh] tensors in the model dtype")
+    check(lib().hga_qkv_prologue(ctypes_params(p), S, ptr(qkv), row_stride, ptr(q_norm_w), ptr(k_norm_w), float(eps),
+                                 norm_mode, ptr(cos), ptr(sin), rope_mode, rot_row0, pos0, ptr(q), ptr(kraw),
+                                 ptr(krope), ptr(v), cap, kv_row0, stream_ptr(dev)), "hga_qkv_prologue")
+    if kv_out is not None:
+        sl = slice(kv_row0, kv_row0 + S)
+        return q.transpose(1, 2), kraw[:, :, sl], krope[:, :, sl], v[:, :, sl]
+    return q.transpose(1, 2), kraw, krope, v

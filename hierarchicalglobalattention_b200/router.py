@@ -1,0 +1,191 @@
+"""ChunkRouter / RoutedKV on the B200 kernels.
+
+Same entry points, arguments and return contract as the reference's router
+(ExistingModelFineTuning/KvRouter/chunk_router.py:93-516): ``route_query_block`` returns a list of
+``(RoutedKV, lo, hi)`` segments and the caller runs ``routed.attend(q[:, :, lo:hi],
+use_summaries=False)`` on each.  What changes is the representation: a ``RoutedKV`` holds the
+*compact* working set (the selected chunk / group lists with their first-visible query row, plus
+the store's token buffers) instead of materialised ``[B,H,N,R,Dh]`` K/V copies and
+``[B,H,N,C,R]`` masks, and ``attend`` runs the working-set attention kernel over it.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+from . import _lib, ops
+from .config import RouterConfig
+from .store import KVCacheStore
+
+
+@dataclass
+class RoutedKV:
+    """Compact routed context of one query block (data only; ``attend`` computes the attention).
+
+    ``chunked`` (the chunk-parallel prefill): ``routing`` holds ``open_gid`` / ``open_t0``
+    ``[B,H,N,Kg]`` and ``sel_chunk`` / ``sel_t0`` ``[B,H,N,Kc]``; keys are read from ``token_k`` /
+    ``token_v`` ``[B,KVH,cap,Dh]`` rows [0, seq_len).
+    """
+
+    params: _lib.HgaParams
+    seq_len: int
+    token_k: torch.Tensor
+    token_v: torch.Tensor
+    routing: Dict[str, torch.Tensor]
+    scale: float
+    chunked: bool = False
+    chunk_size: int = 0
+    decode: Optional[object] = None
+    out: Optional[torch.Tensor] = field(default=None, repr=False)  # optional [B,S,H,Dh] destination
+
+    def attend(self, q: torch.Tensor, use_summaries: bool = False) -> torch.Tensor:
+        """Token-only attention over the routed keys: ``q`` [B,H,L,Dh] -> [B,H,L,Dh].
+
+        Only the exact-token attention of the routed module is provided (the summary-attending
+        variant is a different model family); ``use_summaries=True`` is rejected loudly.
+        """
+        if use_summaries:
+            raise NotImplementedError("summary-attending attention is not part of the B200 hot path; "
+                                      "call attend(q, use_summaries=False)")
+        if self.chunked:
+            return ops.attend_prefill(self.params, q, self.token_k, self.token_v, self.routing["open_gid"],
+                                      self.routing["open_t0"], seq_len=self.seq_len, out=self.out)
+        return self.decode.attend(q)
+
+
+class ChunkRouter:
+    """Router over a tiered store; chunk-parallel prefill and incremental decode."""
+
+    def __init__(self, cfg: RouterConfig, store: KVCacheStore) -> None:
+        self.cfg = cfg
+        self.store = store
+        self._active_kraw: Dict[int, Optional[torch.Tensor]] = {}
+        self._active_len: Dict[int, int] = {}
+        self._rot_cache: Dict[Tuple[str, int], Tuple[torch.Tensor, torch.Tensor]] = {}
+
+    # ---------------------------------------------------------------------------------------
+    def reset(self) -> None:
+        self.store.reset()
+        self._active_kraw.clear()
+        self._active_len.clear()
+
+    def expected_position(self, layer: int) -> int:
+        return self.store.num_closed_chunks(layer) * self.cfg.chunk_size + self._active_len.get(layer, 0)
+
+    def is_empty(self, layer: int) -> bool:
+        return self.expected_position(layer) == 0
+
+    def rotary_table(self, start_pos: int, length: int, device) -> Tuple[torch.Tensor, torch.Tensor]:
+        """fp32 cos/sin ``[1, 1, length, Dh]`` for positions [start_pos, start_pos+length)
+        (chunk_router.py:457-461, 702-709)."""
+        cos, sin = self._rotary(device, start_pos + length)
+        return cos[start_pos:].view(1, 1, length, -1), sin[start_pos:].view(1, 1, length, -1)
+
+    def _rotary(self, device, length: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        key = (str(device), 0)
+        cached = self._rot_cache.get(key)
+        if cached is None or cached[0].shape[0] < length:
+            n = max(length, 2 * cached[0].shape[0] if cached is not None else length)
+            half = self.cfg.head_dim // 2
+            inv = 1.0 / (self.cfg.theta ** (torch.arange(half, device=device, dtype=torch.float32) / half))
+            f = torch.arange(n, device=device, dtype=torch.float32).unsqueeze(-1) * inv
+            emb = torch.cat((f, f), dim=-1)
+            cached = (emb.cos(), emb.sin())
+            self._rot_cache[key] = cached
+        return cached
+
+    # ---------------------------------------------------------------------------------------
+    def route_query_block(self, layer: int, q: torch.Tensor, k_rope: torch.Tensor, k_raw: torch.Tensor,
+                          v: torch.Tensor, start_pos: int, cos: Optional[torch.Tensor] = None,
+                          sin: Optional[torch.Tensor] = None, populate_store: bool = True,
+                          max_chunks_at_once: Optional[int] = None, return_positions: bool = False,
+                          _round_table: bool = False, _out: Optional[torch.Tensor] = None,
+                          ) -> List[Tuple[RoutedKV, int, int]]:
+        """Route a block of new queries (chunk_router.py:463-516).
+
+        * the block stays inside one chunk -> one incremental ``decode_block`` segment;
+        * a fresh multi-chunk block (start_pos 0) -> one chunk-parallel segment (summary builder,
+          two-level router, working-set attention kernels), the store seeded from it;
+        * multiple chunks over resident context -> one incremental segment per chunk.
+        """
+        C = self.cfg.chunk_size
+        S = q.shape[2]
+        first_chunk, last_chunk = start_pos // C, (start_pos + S - 1) // C
+        if return_positions:
+            raise NotImplementedError("return_positions (the DCA attend variant) is not part of the B200 hot path")
+        if first_chunk == last_chunk:
+            return [(self.decode_block(layer, q, k_rope, k_raw, v, start_pos), 0, S)]
+        if start_pos == 0:
+            return [(self._prefill_chunk_parallel(layer, q, k_rope, k_raw, v, cos, sin, populate_store,
+                                                  _round_table, _out), 0, S)]
+        segs = []
+        p, done = start_pos, 0
+        while done < S:
+            take = min(C - (p % C), S - done)
+            sl = slice(done, done + take)
+            segs.append((self.decode_block(layer, q[:, :, sl], k_rope[:, :, sl], k_raw[:, :, sl], v[:, :, sl], p),
+                         done, done + take))
+            p += take
+            done += take
+        return segs
+
+    def _prefill_chunk_parallel(self, layer, q, k_rope, k_raw, v, cos, sin, populate_store, round_table, out):
+        cfg, store = self.cfg, self.store
+        B, H, S, Dh = q.shape
+        C = cfg.chunk_size
+        hp = cfg.hga_params(store.policy, B, q.dtype)
+        if cos is None or sin is None:
+            cos_t, sin_t = self._rotary(q.device, S)
+            cos_t, sin_t = cos_t[:S], sin_t[:S]
+            round_table = True
+        else:
+            cos_t, sin_t = cos.reshape(-1, Dh)[-S:], sin.reshape(-1, Dh)[-S:]
+        # (1) routing summaries of the chunk-parallel path
+        ck, gk, _ = ops.summaries(hp, k_raw, k_rope, v, cos_t, sin_t, round_table=round_table, with_group_v=False)
+        # (2) two-level routing
+        routing = ops.route_prefill(hp, q, ck, gk)
+        if populate_store:
+            self._seed_store(layer, hp, k_rope, k_raw, v, S)
+        return RoutedKV(params=hp, seq_len=S, token_k=k_rope, token_v=v, routing=routing, scale=cfg.scale,
+                        chunked=True, chunk_size=C, out=out)
+
+    def _seed_store(self, layer, hp, k_rope, k_raw, v, S):
+        """Store seed of a fresh prefill (chunk_router.py:553-599): summaries of the closed chunks with
+        fixed anchors and fp32 rotary rows, token rows, and the partial active chunk."""
+        cfg, store = self.cfg, self.store
+        C = cfg.chunk_size
+        n_closed = S // C
+        st = store.ensure_capacity(layer, max(n_closed, 1), S)
+        if n_closed:
+            cos32, sin32 = self._rotary(k_raw.device, S)
+            ops.summaries(hp, k_raw, k_rope, v, cos32, sin32, seq_len=n_closed * C,
+                          out=(st.chunk_k, st.group_k, st.group_v), out_chunk0=0)
+        if st.token_k.data_ptr() != k_rope.data_ptr():
+            store.write_tokens(layer, 0, k_rope, v)
+        store.mark_closed(layer, n_closed)
+        rem = S - n_closed * C
+        self._active_len[layer] = rem
+        self._active_kraw[layer] = k_raw[:, :, n_closed * C:].clone() if rem else None
+
+    # ---------------------------------------------------------------------------------------
+    def decode_block(self, layer, q, k_rope, k_raw, v, start_pos, return_positions: bool = False) -> RoutedKV:
+        """Incremental routing of L <= chunk_size new tokens inside the active chunk
+        (chunk_router.py:279-407)."""
+        from .decode import decode_block
+        return decode_block(self, layer, q, k_rope, k_raw, v, start_pos)
+
+    def prefill(self, layer, q, k_rope, k_raw, v, start_pos: int = 0) -> torch.Tensor:
+        """Stream a prefix chunk by chunk through the incremental path (chunk_router.py:410-442)."""
+        C = self.cfg.chunk_size
+        S = q.shape[2]
+        outs, p, done = [], start_pos, 0
+        while done < S:
+            take = min(C - (p % C), S - done)
+            sl = slice(done, done + take)
+            routed = self.decode_block(layer, q[:, :, sl], k_rope[:, :, sl], k_raw[:, :, sl], v[:, :, sl], p)
+            outs.append(routed.attend(q[:, :, sl], use_summaries=False))
+            p += take
+            done += take
+        return torch.cat(outs, dim=2)

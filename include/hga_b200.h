@@ -27,6 +27,10 @@ extern "C" {
 #endif
 
 enum { HGA_DTYPE_F32 = 0, HGA_DTYPE_BF16 = 1, HGA_DTYPE_F16 = 2 };
+/* How hga_summaries reads its rotary table. */
+enum { HGA_ROT_F32 = 0,         /* fp32 table, used as fp32 (ChunkRouter._rotary_for_positions) */
+       HGA_ROT_MODEL = 1,       /* table already in the model dtype */
+       HGA_ROT_F32_ROUNDED = 2  /* fp32 table, each entry rounded to the model dtype first (cos.to(x.dtype)) */ };
 enum { HGA_OK = 0, HGA_E_INVALID = -1, HGA_E_UNSUPPORTED = -2, HGA_E_CUDA = -3, HGA_E_DEVICE = -4 };
 
 /* Hyper-parameters of one routed-attention layer.  Mirrors RouterConfig + ChunkPlacementPolicy
@@ -52,11 +56,12 @@ const char* hga_last_error(void);
  * Summarises tokens [0, seq_len) of the K/V rows (a partial last chunk uses the middle of its
  * valid tokens as anchor, vectorized.py:265-270) into chunk slots [out_chunk0, out_chunk0+N).
  * Token 0 sits at absolute position pos0 (a multiple of chunk_size).  cos/sin are read at the
- * anchor positions; rot_dtype = HGA_DTYPE_F32 for an fp32 table, or p->dtype for a table already
- * cast to the model dtype (what HierarchicalGlobalAttentionRouted.py:168 hands the router). */
+ * anchor positions, interpreted per rot_mode (HGA_ROT_*): the chunk-parallel path rounds the fp32
+ * table to the model dtype (HierarchicalGlobalAttentionRouted.py:168), the store seed uses fp32
+ * (chunk_router.py:702-709).  group_v may be NULL. */
 int hga_summaries(const hga_params* p, int64_t seq_len, int64_t pos0,
                   const void* k_raw, const void* k_rope, const void* v, int64_t kv_cap,
-                  const void* cos, const void* sin, int32_t rot_dtype, int64_t rot_row0,
+                  const void* cos, const void* sin, int32_t rot_mode, int64_t rot_row0,
                   void* chunk_k, void* group_k, void* group_v, int64_t sum_cap, int64_t out_chunk0,
                   cudaStream_t stream);
 
@@ -86,6 +91,22 @@ int hga_attend_prefill(const hga_params* p, int64_t seq_len, const void* q, int3
                        const void* k_rope, const void* v, int64_t kv_cap,
                        const int32_t* open_gid, const int32_t* open_t0,
                        void* out, int32_t out_layout, int32_t impl, cudaStream_t stream);
+
+/* Projection epilogue of the routed module: q/k RMSNorm + RoPE + KV-store layout in one pass.
+ * Replaces the eager prologue of HierarchicalGlobalAttentionRouted.forward
+ * (HierarchicalGlobalAttentionRouted.py:151-157) and QwenRoutedAttention.forward
+ * (qwen_routed_attention.py:171-176).  qkv: [B, S, row_stride] rows holding H query heads, then
+ * KVH key heads, then KVH value heads (Dh each) — one fused projection GEMM.  q_norm_w / k_norm_w
+ * (Dh, model dtype) may be NULL (no qk norm).  norm_mode 0 = fp32 weight product (the routed
+ * module's RMSNorm), 1 = HF Qwen3 RMSNorm rounding.  rope_mode 0 = fp32 math on an fp32 table,
+ * 1 = model-dtype math on a model-dtype table (HF apply_rotary_pos_emb).  Table row r = absolute
+ * position rot_row0 + r; token t sits at absolute position pos0 + t.  Writes q_rope [B,S,H,Dh]
+ * and rows [kv_row0, kv_row0+S) of k_raw / k_rope / v [B,KVH,kv_cap,Dh]. */
+int hga_qkv_prologue(const hga_params* p, int64_t seq_len, const void* qkv, int64_t row_stride,
+                     const void* q_norm_w, const void* k_norm_w, float eps, int32_t norm_mode,
+                     const void* cos, const void* sin, int32_t rope_mode, int64_t rot_row0, int64_t pos0,
+                     void* q_rope, void* k_raw, void* k_rope, void* v, int64_t kv_cap, int64_t kv_row0,
+                     cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -4,6 +4,7 @@ import os
 import re
 
 import pytest
+import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -47,3 +48,18 @@ def test_ops_refuse_cpu_tensors():
     k = torch.zeros(1, 1, 16, 16)
     with pytest.raises(_lib.HgaError, match="CUDA"):
         ops.summaries(p, k, k, k, torch.zeros(16, 16), torch.zeros(16, 16))
+
+
+def test_module_state_dict_loads_from_reference_layout():
+    import hierarchicalglobalattention_b200 as hga
+    m = hga.HierarchicalGlobalAttentionRouted(d_model=256, nhead=4, kv_heads=2, qk_norm=True)
+    names = set(m.state_dict())
+    assert names == {"q_proj.weight", "k_proj.weight", "v_proj.weight", "o_proj.weight", "q_norm.weight",
+                     "k_norm.weight"}
+
+
+def test_module_fails_loudly_on_cpu():
+    import hierarchicalglobalattention_b200 as hga
+    m = hga.HierarchicalGlobalAttentionRouted(d_model=64, nhead=4, kv_heads=2)
+    with pytest.raises(Exception, match="CUDA"):
+        m(torch.randn(1, 130, 64))
