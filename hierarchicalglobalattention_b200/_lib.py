@@ -47,6 +47,7 @@ _SIGNATURES = {
                                          _P, _P, _P]),
     "hga_attend_prefill": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _P, _I32, _P, _P, _I64, _P, _P, _P, _I32,
                                           _I32, _P]),
+    "hga_device_status": (ctypes.c_int, [_P, _I32]),
     "hga_qkv_prologue": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _P, _I64, _P, _P, ctypes.c_float, _I32, _P,
                                         _P, _I32, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _P]),
 }
@@ -116,3 +117,10 @@ def make_params(*, batch, nhead, kv_heads, head_dim, chunk_size, group_size, top
         dtype=DTYPE_CODE[dtype], scale=head_dim ** -0.5,
         group_kv_scale=1.0 / (group_size + math.sqrt(group_size)),
     )
+
+
+def device_status(clear: bool = True) -> int:
+    """Error word of the tensor-core kernels (0 = no bounded wait timed out)."""
+    code = ctypes.c_int32(0)
+    check(lib().hga_device_status(ctypes.byref(code), 1 if clear else 0), "hga_device_status")
+    return int(code.value)

@@ -25,6 +25,7 @@ bool attend_tc_supported(const hga_params& p);
 cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const void* q, int q_layout, const void* k_rope,
                              const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0,
                              int Kg, void* out, int out_layout, cudaStream_t st);
+int tc_error_status(bool clear);
 }  // namespace hga
 
 static thread_local char g_err[512];
@@ -134,14 +135,26 @@ int hga_attend_prefill(const hga_params* p, int64_t seq_len, const void* q, int3
   const bool tc_ok = hga::attend_tc_supported(*p);
   if (impl == 2 && !tc_ok)
     return fail(HGA_E_UNSUPPORTED, "tensor-core attention needs bf16, head_dim 128, chunk 64, group 16");
-  if ((impl == 0 && tc_ok) || impl == 2)
-    return cuda_status(hga::launch_attend_tc(*p, seq_len, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg, out,
-                                             out_layout, stream),
-                       "hga_attend_prefill(tcgen05)");
+  if ((impl == 0 && tc_ok) || impl == 2) {
+    const cudaError_t e = hga::launch_attend_tc(*p, seq_len, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg,
+                                                out, out_layout, stream);
+    // windows wider than the tensor-core kernel's unit table (or misaligned pointers) go to the
+    // portable kernel when the caller let us choose
+    if (!(impl == 0 && (e == cudaErrorNotSupported || e == cudaErrorMisalignedAddress)))
+      return cuda_status(e, "hga_attend_prefill(tcgen05)");
+    (void)cudaGetLastError();
+  }
   if (impl != 0 && impl != 1) return fail(HGA_E_INVALID, "impl must be 0, 1 or 2");
   return cuda_status(hga::launch_attend_simt(*p, seq_len, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg, out,
                                              out_layout, stream),
                      "hga_attend_prefill");
+}
+
+int hga_device_status(int32_t* code, int32_t clear) {
+  const int v = hga::tc_error_status(clear != 0);
+  if (v < 0) return fail(HGA_E_CUDA, "hga_device_status: cannot read the device error word");
+  if (code) *code = v;
+  return HGA_OK;
 }
 
 int hga_qkv_prologue(const hga_params* p, int64_t seq_len, const void* qkv, int64_t row_stride, const void* q_norm_w,

@@ -1,9 +1,577 @@
-// tcgen05 / TMEM working-set attention (placeholder until the tensor-core kernel lands).
+// Working-set attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+// Shape: bf16, head_dim 128, chunk 64, group 16.  One CTA per (query chunk n, pair of query heads
+// sharing a KV head, batch b): the MMA M dimension is 128 = 2 heads x 64 query rows.  The key
+// set of the CTA is the union of both heads' working sets, walked as 16-token "units"
+// (one routing group each):
+//   current chunk (4 units, causal), keep_last window, keep_first window (both heads see all of
+//   them), then the union of the two heads' opened groups (each head sees its own ones from its
+//   first-visible row t0 on).
+// Per 128-key tile (8 units):
+//   TMA warp      : 16-row boxes of K and V per unit into a 2-stage SW128 smem ring
+//   MMA warp      : S = Q.K^T  (M128 N128 K16 x8, A/B from smem, D in TMEM, double-buffered)
+//                   O += P.V   (A = P from TMEM, B = V from smem as MN-major, D = O in TMEM)
+//   4 softmax warps: one thread per query row (TMEM lane): mask, online softmax in the exp2
+//                   domain with lazy rescaling (only when the row max grows by > 2^8), P -> TMEM
+// Every mbarrier wait is bounded; on timeout the CTA records an error code (hga_tc_status) and
+// leaves after releasing its TMEM.
+#include <cuda.h>
+
 #include "hga_common.cuh"
+
 namespace hga {
-bool attend_tc_supported(const hga_params& p) { (void)p; return false; }
-cudaError_t launch_attend_tc(const hga_params&, int64_t, const void*, int, const void*, const void*, int64_t,
-                             const int32_t*, const int32_t*, int, void*, int, cudaStream_t) {
-  return cudaErrorNotSupported;
+
+__device__ int g_tc_error = 0;
+
+namespace tc {
+
+constexpr int kThreads = 192;  // warp0 TMA, warp1 MMA, warps2-5 softmax/epilogue
+constexpr int kUnitsPerTile = 8;
+constexpr int kMaxUnits = 336;  // current 4 + windows <= 64 + opened union <= 256, rounded up to whole tiles
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
+
+struct Unit {
+  int pos;      // first token row of the unit inside the (b, kvh) row block
+  int tmin0;    // first visible query row for head 0 (64 = never)
+  int tmin1;    // same for head 1
+  int causal;   // 1: key j of the unit is visible to row t iff t >= tmin + j
+};
+
+struct SmemLayout {
+  static constexpr int kQ = 0;                       // 2 x 16 KB (dh halves), rows 0..127
+  static constexpr int kStage = 32768;               // 2 stages x (K 2x16KB + V 2x16KB)
+  static constexpr int kStageBytes = 65536;
+  static constexpr int kUnits = kStage + 2 * kStageBytes;
+  static constexpr int kBars = kUnits + kMaxUnits * 16;
+  static constexpr int kMisc = kBars + 16 * 8;
+  static constexpr int kTotal = kMisc + 64;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; returns false (and raises the CTA abort flag + global error) on timeout.
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  unsigned it = 0;
+  while (!mbar_try(bar, parity)) {
+    if (((++it) & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicCAS(&g_tc_error, 0, code);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// UMMA shared-memory descriptor, 128B swizzle.  lbo/sbo in bytes.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3fff);
+  d |= (uint64_t)((lbo >> 4) & 0x3fff) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3fff) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (sm100)
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: kind::f16, bf16 x bf16 -> f32, M=128, N=128.
+__host__ __device__ constexpr uint32_t idesc_bf16(bool b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((128u >> 3) << 17) |
+         ((128u >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+#define HGA_LD32(taddr, r)                                                                                        \
+  asm volatile(                                                                                                   \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18," \
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                                              \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), \
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),     \
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),    \
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                 \
+      : "r"(taddr))
+
+#define HGA_ST32(taddr, r)                                                                                         \
+  asm volatile(                                                                                                    \
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18," \
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),                                    \
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), \
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),   \
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),   \
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]))
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+struct Args {
+  int S, H, KVH, N, Kg, keep_first, keep_last, out_layout, q_layout;
+  int64_t kv_cap;
+  float scale_log2;
+  const int32_t* open_gid;
+  const int32_t* open_t0;
+  __nv_bfloat16* out;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attend_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const Args a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int n = blockIdx.x, hp = blockIdx.y, b = blockIdx.z;
+  const int h0 = 2 * hp, h1 = h0 + 1;
+  const int kvh = h0 / (a.H / a.KVH);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int C = 64, gs = 16;
+  const int row0 = n * C;
+  const int nvalid = (a.S - row0) < C ? (a.S - row0) : C;
+
+  Unit* units = reinterpret_cast<Unit*>(smem + SmemLayout::kUnits);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::kBars);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* p_full = bars + 7;    // [2]
+  uint64_t* pv_done = bars + 9;
+  int* misc = reinterpret_cast<int*>(smem + SmemLayout::kMisc);
+  volatile int* abort_flag = misc + 0;
+  int* n_units_s = misc + 1;
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(misc + 2);
+  int* la_s = misc + 3;
+  int* nb_s = misc + 4;
+
+  // ---- set-up: barriers, TMEM, unit table -------------------------------------------------
+  int f_hi, l_lo;
+  windows(n, a.keep_first, a.keep_last, f_hi, l_lo);
+  const int n_shared = 4 + 4 * (n - l_lo) + 4 * f_hi;
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(kv_full + i, 1);
+      mbar_init(kv_empty + i, 1);
+      mbar_init(s_full + i, 1);
+      mbar_init(p_full + i, 128);
+    }
+    mbar_init(pv_done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    *abort_flag = 0;
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_base_s)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  // shared units: current chunk (causal), last window, first window
+  for (int u = tid; u < n_shared; u += kThreads) {
+    Unit e;
+    if (u < 4) {
+      e.pos = row0 + u * gs; e.tmin0 = e.tmin1 = u * gs; e.causal = 1;
+    } else if (u < 4 + 4 * (n - l_lo)) {
+      e.pos = l_lo * C + (u - 4) * gs; e.tmin0 = e.tmin1 = 0; e.causal = 0;
+    } else {
+      e.pos = (u - 4 - 4 * (n - l_lo)) * gs; e.tmin0 = e.tmin1 = 0; e.causal = 0;
+    }
+    units[u] = e;
+  }
+  // opened groups: list A (head 0) in order, then the B-only entries (head 1)
+  const size_t tile0 = (((size_t)b * a.H + h0) * a.N + n) * a.Kg;
+  const size_t tile1 = (((size_t)b * a.H + h1) * a.N + n) * a.Kg;
+  if (warp == 2) {
+    int la = 0, lb = 0;
+    for (int base = 0; base < a.Kg; base += 32) {
+      const int j = base + lane;
+      const bool va = j < a.Kg && a.open_gid[tile0 + j] >= 0 && a.open_t0[tile0 + j] < nvalid;
+      const bool vb = j < a.Kg && a.open_gid[tile1 + j] >= 0 && a.open_t0[tile1 + j] < nvalid;
+      la += __popc(__ballot_sync(0xffffffffu, va));
+      lb += __popc(__ballot_sync(0xffffffffu, vb));
+    }
+    if (lane == 0) { *la_s = la; *nb_s = lb; }
+  }
+  __syncthreads();
+  const int la = *la_s, lb = *nb_s;
+  // valid entries are a prefix of each list (the router pads with -1 after the visible ones)
+  for (int i = tid; i < la; i += kThreads) {
+    const int g = a.open_gid[tile0 + i];
+    int t1 = C;
+    int lo = 0, hi = lb - 1;  // binary search g in list B
+    while (lo <= hi) {
+      const int mid = (lo + hi) >> 1;
+      const int x = a.open_gid[tile1 + mid];
+      if (x == g) { t1 = a.open_t0[tile1 + mid]; break; }
+      if (x < g) lo = mid + 1; else hi = mid - 1;
+    }
+    Unit e; e.pos = g * gs; e.tmin0 = a.open_t0[tile0 + i]; e.tmin1 = t1; e.causal = 0;
+    units[n_shared + i] = e;
+  }
+  if (warp == 3) {
+    int written = 0;
+    for (int base = 0; base < lb; base += 32) {
+      const int j = base + lane;
+      bool keep = false;
+      int g = 0;
+      if (j < lb) {
+        g = a.open_gid[tile1 + j];
+        keep = true;
+        int lo = 0, hi = la - 1;
+        while (lo <= hi) {
+          const int mid = (lo + hi) >> 1;
+          const int x = a.open_gid[tile0 + mid];
+          if (x == g) { keep = false; break; }
+          if (x < g) lo = mid + 1; else hi = mid - 1;
+        }
+      }
+      const unsigned bal = __ballot_sync(0xffffffffu, keep);
+      if (keep) {
+        const int slot = n_shared + la + written + __popc(bal & ((1u << lane) - 1u));
+        Unit e; e.pos = g * gs; e.tmin0 = C; e.tmin1 = a.open_t0[tile1 + j]; e.causal = 0;
+        units[slot] = e;
+      }
+      written += __popc(bal);
+    }
+    if (lane == 0) *n_units_s = n_shared + la + written;
+  }
+  __syncthreads();
+  const int n_units = *n_units_s;
+  const int ntiles = (n_units + kUnitsPerTile - 1) / kUnitsPerTile;
+  // pad the last tile with never-visible copies of unit 0 (finite data, zero probability)
+  for (int u = n_units + tid; u < ntiles * kUnitsPerTile; u += kThreads) {
+    Unit e = units[0]; e.tmin0 = e.tmin1 = 1 << 20; e.causal = 0;
+    units[u] = e;
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_base_s;
+
+  unsigned char* q_s = smem + SmemLayout::kQ;
+  if (warp == 0) {
+    // ------------------------------- TMA producer -------------------------------------------
+    if (lane == 0) {
+      mbar_expect_tx(q_full, 32768);
+      for (int hh = 0; hh < 2; ++hh)
+        for (int kb = 0; kb < 2; ++kb) {
+          unsigned char* dst = q_s + kb * 16384 + hh * 8192;
+          if (a.q_layout == 1) tma_load_3d(dst, &tm_q, kb * 64, h0 + hh, b * a.S + row0, q_full);
+          else tma_load_2d(dst, &tm_q, kb * 64, (b * a.H + h0 + hh) * a.S + row0, q_full);
+        }
+      const int64_t kvrow = ((int64_t)b * a.KVH + kvh) * a.kv_cap;
+      for (int i = 0; i < ntiles; ++i) {
+        const int st = i & 1;
+        if (i >= 2 && !mbar_wait(kv_empty + st, ((i >> 1) - 1) & 1, abort_flag, 1)) break;
+        unsigned char* kdst = smem + SmemLayout::kStage + st * SmemLayout::kStageBytes;
+        unsigned char* vdst = kdst + 32768;
+        mbar_expect_tx(kv_full + st, 65536);
+        for (int u = 0; u < kUnitsPerTile; ++u) {
+          const int row = (int)(kvrow + units[i * kUnitsPerTile + u].pos);
+          for (int kb = 0; kb < 2; ++kb) {
+            tma_load_2d(kdst + kb * 16384 + u * 2048, &tm_k, kb * 64, row, kv_full + st);
+            tma_load_2d(vdst + kb * 16384 + u * 2048, &tm_v, kb * 64, row, kv_full + st);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------- MMA issuer ---------------------------------------------
+    if (lane == 0) {
+      const uint32_t id_qk = idesc_bf16(false), id_pv = idesc_bf16(true);
+      const uint32_t q_addr = smem_u32(q_s);
+      bool ok = mbar_wait(q_full, 0, abort_flag, 2);
+      fence_after();
+      for (int i = 0; ok && i <= ntiles; ++i) {
+        if (i < ntiles) {
+          const int st = i & 1;
+          if (!mbar_wait(kv_full + st, (i >> 1) & 1, abort_flag, 3)) break;
+          if (i >= 2 && !mbar_wait(pv_done, (i - 2) & 1, abort_flag, 4)) break;
+          fence_after();
+          const uint32_t k_addr = smem_u32(smem + SmemLayout::kStage + st * SmemLayout::kStageBytes);
+          const uint32_t d = tmem + (st ? kColS1 : kColS0);
+          for (int kb = 0; kb < 2; ++kb)
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t da = sdesc(q_addr + kb * 16384 + kk * 32, 16, 1024);
+              const uint64_t db = sdesc(k_addr + kb * 16384 + kk * 32, 16, 1024);
+              mma_ss(d, da, db, id_qk, (kb | kk) != 0);
+            }
+          mma_commit(s_full + st);
+        }
+        if (i >= 1) {
+          const int j = i - 1, st = j & 1;
+          if (!mbar_wait(p_full + st, (j >> 1) & 1, abort_flag, 5)) break;
+          fence_after();
+          const uint32_t v_addr = smem_u32(smem + SmemLayout::kStage + st * SmemLayout::kStageBytes + 32768);
+          const uint32_t p_col = tmem + (st ? kColS1 : kColS0);
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t db = sdesc(v_addr + kk * 2048, 16384, 1024);
+            mma_ts(tmem + kColO, p_col + kk * 8, db, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(pv_done);
+          mma_commit(kv_empty + st);
+        }
+      }
+    }
+  } else {
+    // ------------------------------- softmax / epilogue -------------------------------------
+    const int quarter = warp & 3;          // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;   // 0..127
+    const int head_sel = row >> 6;         // 0 -> h0, 1 -> h1
+    const int t = row & 63;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int i = 0; i < ntiles && ok; ++i) {
+      const int st = i & 1;
+      ok = mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 6);
+      if (!ok) break;
+      fence_after();
+      const uint32_t s_addr = tmem + lane_addr + (st ? kColS1 : kColS0);
+      uint32_t r[128];
+      HGA_LD32(s_addr + 0, (r + 0));
+      HGA_LD32(s_addr + 32, (r + 32));
+      HGA_LD32(s_addr + 64, (r + 64));
+      HGA_LD32(s_addr + 96, (r + 96));
+      tmem_wait_ld();
+      float mx = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < kUnitsPerTile; ++u) {
+        const Unit e = units[i * kUnitsPerTile + u];
+        const int tmin = head_sel ? e.tmin1 : e.tmin0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int c = u * 16 + j;
+          const bool vis = t < nvalid && t >= tmin + (e.causal ? j : 0);
+          const float s = vis ? __uint_as_float(r[c]) * a.scale_log2 : -INFINITY;
+          r[c] = __float_as_uint(s);
+          mx = fmaxf(mx, s);
+        }
+      }
+      const float m_new = fmaxf(m_run, mx);
+      if (m_new > m_run + 8.f || (m_run == -INFINITY && m_new != -INFINITY)) {
+        const float alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
+        l_run *= alpha;
+        if (i > 0 && m_run != -INFINITY) {
+          // O holds sum over tiles < i: wait for the last P.V, then rescale this row
+          ok = mbar_wait(pv_done, (i - 1) & 1, abort_flag, 7);
+          if (!ok) break;
+          fence_after();
+          const uint32_t o_addr = tmem + lane_addr + kColO;
+          for (int c0 = 0; c0 < 128; c0 += 32) {
+            uint32_t o[32];
+            HGA_LD32(o_addr + c0, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            HGA_ST32(o_addr + c0, o);
+          }
+          tmem_wait_st();
+        }
+        m_run = m_new;
+      }
+      float psum = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float s0 = __uint_as_float(r[2 * c]), s1 = __uint_as_float(r[2 * c + 1]);
+        const float p0 = (s0 == -INFINITY) ? 0.f : exp2f(s0 - m_run);
+        const float p1 = (s1 == -INFINITY) ? 0.f : exp2f(s1 - m_run);
+        psum += p0 + p1;
+        __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
+        pk[c] = *reinterpret_cast<uint32_t*>(&v2);
+      }
+      l_run += psum;
+      HGA_ST32(s_addr + 0, pk);
+      HGA_ST32(s_addr + 32, (pk + 32));
+      tmem_wait_st();
+      fence_before();
+      mbar_arrive(p_full + st);
+    }
+    // epilogue
+    if (ok && ntiles > 0) ok = mbar_wait(pv_done, (ntiles - 1) & 1, abort_flag, 8);
+    if (ok) {
+      fence_after();
+      const int h = head_sel ? h1 : h0;
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const uint32_t o_addr = tmem + lane_addr + kColO;
+      __nv_bfloat16* dst = nullptr;
+      if (t < nvalid) {
+        const int64_t tt = row0 + t;
+        dst = a.out_layout == 1 ? a.out + (((int64_t)b * a.S + tt) * a.H + h) * 128
+                                : a.out + (((int64_t)b * a.H + h) * a.S + tt) * 128;
+      }
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        uint32_t o[32];
+        HGA_LD32(o_addr + c0, o);
+        tmem_wait_ld();
+        if (dst) {
+          uint32_t w[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            __nv_bfloat162 v2 = __floats2bfloat162_rn(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
+            w[c] = *reinterpret_cast<uint32_t*>(&v2);
+          }
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) d4[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+        }
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// ---- host side: tensor maps through the driver entry point (no libcuda link needed) ---------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+static bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                     const cuuint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace tc
+
+bool attend_tc_supported(const hga_params& p) {
+  return p.dtype == HGA_DTYPE_BF16 && p.head_dim == 128 && p.chunk_size == 64 && p.group_size == 16 &&
+         (p.nhead / p.kv_heads) % 2 == 0 && p.keep_last <= 1 << 20 && p.keep_first <= 1 << 20;
+}
+
+cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const void* q, int q_layout, const void* k_rope,
+                             const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0, int Kg,
+                             void* out, int out_layout, cudaStream_t st) {
+  using namespace tc;
+  const int N = (int)((S + 63) / 64);
+  // windows wider than the unit table hold go through the portable kernel
+  const int kl = p.keep_last < N ? p.keep_last : N, kf = p.keep_first < N ? p.keep_first : N;
+  if (kl + kf > 16 || Kg > 128) return cudaErrorNotSupported;
+  if (((uintptr_t)q | (uintptr_t)k_rope | (uintptr_t)v | (uintptr_t)out) & 15) return cudaErrorMisalignedAddress;
+  CUtensorMap mq, mk, mv;
+  const cuuint64_t rows_kv = (cuuint64_t)p.batch * p.kv_heads * kv_cap;
+  const cuuint64_t dkv[2] = {128, rows_kv}, skv[1] = {256};
+  const cuuint32_t bkv[2] = {64, 16};
+  if (!make_map(&mk, k_rope, 2, dkv, skv, bkv) || !make_map(&mv, v, 2, dkv, skv, bkv)) return cudaErrorInvalidValue;
+  if (q_layout == 1) {
+    const cuuint64_t dq[3] = {128, (cuuint64_t)p.nhead, (cuuint64_t)(p.batch * S)};
+    const cuuint64_t sq[2] = {256, (cuuint64_t)p.nhead * 256};
+    const cuuint32_t bq[3] = {64, 1, 64};
+    if (!make_map(&mq, q, 3, dq, sq, bq)) return cudaErrorInvalidValue;
+  } else {
+    const cuuint64_t dq[2] = {128, (cuuint64_t)p.batch * p.nhead * S};
+    const cuuint64_t sq[1] = {256};
+    const cuuint32_t bq[2] = {64, 64};
+    if (!make_map(&mq, q, 2, dq, sq, bq)) return cudaErrorInvalidValue;
+  }
+  Args a;
+  a.S = (int)S; a.H = p.nhead; a.KVH = p.kv_heads; a.N = N; a.Kg = Kg;
+  a.keep_first = p.keep_first; a.keep_last = p.keep_last; a.out_layout = out_layout; a.q_layout = q_layout;
+  a.kv_cap = kv_cap;
+  a.scale_log2 = p.scale * 1.4426950408889634f;
+  a.open_gid = open_gid; a.open_t0 = open_t0;
+  a.out = (__nv_bfloat16*)out;
+  const int smem = SmemLayout::kTotal + 1024;
+  cudaError_t e = cudaFuncSetAttribute(attend_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(N, p.nhead / 2, p.batch);
+  attend_tc_kernel<<<grid, kThreads, smem, st>>>(mq, mk, mv, a);
+  return cudaGetLastError();
+}
+
+int tc_error_status(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int));
+  }
+  return v;
+}
+
 }  // namespace hga

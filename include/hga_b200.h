@@ -108,6 +108,11 @@ int hga_qkv_prologue(const hga_params* p, int64_t seq_len, const void* qkv, int6
                      void* q_rope, void* k_raw, void* k_rope, void* v, int64_t kv_cap, int64_t kv_row0,
                      cudaStream_t stream);
 
+/* Device-side error word of the tensor-core kernels: 0, or the code of the first bounded
+ * mbarrier wait that timed out (the CTA then released its TMEM and returned without output).
+ * Synchronous (reads device memory); clear != 0 resets the word. */
+int hga_device_status(int32_t* code, int32_t clear);
+
 #ifdef __cplusplus
 }
 #endif
