@@ -45,6 +45,8 @@ _SIGNATURES = {
                                      _P, _P, _P, _I64, _I64, _P]),
     "hga_route_prefill": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _P, _I32, _P, _P, _I64, _P, _P, _P, _P,
                                          _P, _P, _P]),
+    "hga_route_prefill_impl": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _P, _I32, _P, _P, _I64, _P, _P, _P,
+                                              _P, _P, _P, _I32, _P]),
     "hga_attend_prefill": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _P, _I32, _P, _P, _I64, _P, _P, _P, _I32,
                                           _I32, _P]),
     "hga_device_status": (ctypes.c_int, [_P, _I32]),

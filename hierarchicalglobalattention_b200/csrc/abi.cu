@@ -26,6 +26,11 @@ cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const void* q, int 
                              const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0,
                              int Kg, void* out, int out_layout, cudaStream_t st);
 int tc_error_status(bool clear);
+int route_tc_error_status(bool clear);
+bool route_tc_supported(const hga_params& p, int64_t S);
+cudaError_t launch_route_tc(const hga_params& p, int64_t S, const void* q, int q_layout, const void* ck, const void* gk,
+                            int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid, int32_t* open_t0,
+                            float* dbg1, float* dbg2, cudaStream_t st);
 }  // namespace hga
 
 static thread_local char g_err[512];
@@ -73,6 +78,11 @@ static int route_sizes(const hga_params* p, int64_t S, int* Kc, int* Kg) {
 
 extern "C" {
 
+int hga_route_prefill_impl(const hga_params* p, int64_t seq_len, const void* q, int32_t q_layout, const void* chunk_k,
+                           const void* group_k, int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0,
+                           int32_t* open_gid, int32_t* open_t0, float* dbg_l1, float* dbg_l2, int32_t impl,
+                           cudaStream_t stream);
+
 const char* hga_version(void) { return "hga_b200 0.1 (sm_100a)"; }
 const char* hga_last_error(void) { return g_err; }
 
@@ -100,6 +110,14 @@ int hga_summaries(const hga_params* p, int64_t seq_len, int64_t pos0, const void
 int hga_route_prefill(const hga_params* p, int64_t seq_len, const void* q, int32_t q_layout, const void* chunk_k,
                       const void* group_k, int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid,
                       int32_t* open_t0, float* dbg_l1, float* dbg_l2, cudaStream_t stream) {
+  return hga_route_prefill_impl(p, seq_len, q, q_layout, chunk_k, group_k, sum_cap, sel_chunk, sel_t0, open_gid,
+                                open_t0, dbg_l1, dbg_l2, 0, stream);
+}
+
+int hga_route_prefill_impl(const hga_params* p, int64_t seq_len, const void* q, int32_t q_layout, const void* chunk_k,
+                           const void* group_k, int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0,
+                           int32_t* open_gid, int32_t* open_t0, float* dbg_l1, float* dbg_l2, int32_t impl,
+                           cudaStream_t stream) {
   int rc = check_params(p);
   if (rc) return rc;
   if (seq_len <= 0) return HGA_OK;
@@ -113,6 +131,17 @@ int hga_route_prefill(const hga_params* p, int64_t seq_len, const void* q, int32
   if (sum_cap < N) return fail(HGA_E_INVALID, "hga_route_prefill: sum_cap < number of chunks");
   if ((int64_t)Kc * (p->chunk_size / p->group_size) > 256)
     return fail(HGA_E_UNSUPPORTED, "hga_route_prefill: topk_chunks * groups_per_chunk > 256");
+  const bool tc_ok = hga::route_tc_supported(*p, seq_len);
+  if (impl == 2 && !tc_ok)
+    return fail(HGA_E_UNSUPPORTED, "tensor-core router needs bf16, head_dim 128, chunk 64, group 16, topk_chunks <= 32");
+  if ((impl == 0 && tc_ok) || impl == 2) {
+    const cudaError_t e = hga::launch_route_tc(*p, seq_len, q, q_layout, chunk_k, group_k, sum_cap, sel_chunk, sel_t0,
+                                               open_gid, open_t0, dbg_l1, dbg_l2, stream);
+    if (!(impl == 0 && (e == cudaErrorMisalignedAddress || e == cudaErrorInvalidConfiguration)))
+      return cuda_status(e, "hga_route_prefill(tcgen05)");
+    (void)cudaGetLastError();
+  }
+  if (impl != 0 && impl != 1) return fail(HGA_E_INVALID, "impl must be 0, 1 or 2");
   int smem = 0;
   return cuda_status(hga::launch_route_prefill(*p, seq_len, q, q_layout, chunk_k, group_k, sum_cap, sel_chunk, sel_t0,
                                                open_gid, open_t0, dbg_l1, dbg_l2, stream, &smem),
@@ -152,8 +181,9 @@ int hga_attend_prefill(const hga_params* p, int64_t seq_len, const void* q, int3
 
 int hga_device_status(int32_t* code, int32_t clear) {
   const int v = hga::tc_error_status(clear != 0);
-  if (v < 0) return fail(HGA_E_CUDA, "hga_device_status: cannot read the device error word");
-  if (code) *code = v;
+  const int w = hga::route_tc_error_status(clear != 0);
+  if (v < 0 || w < 0) return fail(HGA_E_CUDA, "hga_device_status: cannot read the device error word");
+  if (code) *code = v ? v : w;
   return HGA_OK;
 }
 

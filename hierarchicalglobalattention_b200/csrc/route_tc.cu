@@ -1,0 +1,500 @@
+// Two-level prefill router on the tensor cores (bf16, head_dim 128, chunk 64, group 16).
+//
+// Same selection rules, tie order and outputs as the portable router (route_prefill.cu, which
+// states the reference lines it follows); the scoring contractions run on tcgen05 and the
+// per-row selections run one thread per query row on TMEM-resident scores:
+//   CTA = (query chunk n, pair of query heads sharing a KV head, batch b); M = 128 rows.
+//   level 1: the routed pool [f_hi, l_lo) streams through smem in 128-chunk tiles (TMA);
+//            S = Q.CK^T lands in TMEM (double-buffered); each row thread keeps its running
+//            top-Kc requests in registers (16-bit score key | 16-bit pool index) and finally
+//            max-pools them into smem (atomicMax) with the first requesting row (atomicMin).
+//   select : one warp per head picks Kc pooled chunks (radix select), forces the previous chunk.
+//   level 2: the chosen chunks' group summaries (<= 128 rows per head) are gathered into a
+//            256-row SW128 tile; one N=256 MMA scores both heads; each row thread selects its
+//            Kg_request groups by a 16-bit radix select; one warp per head picks Kg pooled groups.
+#include "tc_common.cuh"
+
+namespace hga {
+namespace rtc {
+
+using namespace tc;
+
+constexpr int kThreads = 192;
+
+struct Args {
+  int S, H, KVH, N, Kc, Kg, Kgr, keep_first, keep_last, q_layout;
+  int64_t sum_cap;
+  float scale;
+  const __nv_bfloat16* group_k;
+  int32_t *sel_chunk, *sel_t0, *open_gid, *open_t0;
+  float *dbg_l1, *dbg_l2;
+};
+
+__device__ __forceinline__ uint32_t ord16(float s) {  // order-preserving key of a bf16 value, 0 reserved
+  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(s));
+  return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
+}
+
+__device__ __forceinline__ float bf16_score(uint32_t acc_bits, float scale) {
+  return Num<__nv_bfloat16>::round(__fmul_rn(Num<__nv_bfloat16>::round(__uint_as_float(acc_bits)), scale));
+}
+
+// Smem layout (bytes from the 1024-aligned base).  pooled/t0 arrays are sized by N at launch.
+struct L {
+  static constexpr int kQ = 0, kTile = 32768, kTileBytes = 65536;  // 2 x 32 KB stages, reused as the L2 tile
+  static constexpr int kFixed = kTile + kTileBytes;
+};
+struct Misc {
+  uint64_t bars[10];
+  uint32_t tmem;
+  int abort;
+  int ksel[2];
+  int sel[2][32];
+  int selt0[2][32];
+  uint32_t gpool[2][128];
+  uint32_t gt0[2][128];
+};
+
+// Warp-wide radix select over keys[0..n) (unique 32-bit keys, 0 = absent): flags the k largest.
+__device__ void warp_select_u32(const uint32_t* keys, int n, int k, unsigned char* flag) {
+  const int lane = threadIdx.x & 31;
+  int nreal = 0;
+  for (int i = lane; i < n; i += 32) nreal += keys[i] != 0u;
+  for (int o = 16; o; o >>= 1) nreal += __shfl_xor_sync(0xffffffffu, nreal, o);
+  if (nreal <= k) {
+    for (int i = lane; i < n; i += 32) flag[i] = keys[i] != 0u;
+    __syncwarp();
+    return;
+  }
+  uint32_t T = 0;
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t cand = T | (1u << bit);
+    int cnt = 0;
+    for (int i = lane; i < n; i += 32) cnt += keys[i] >= cand;
+    for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    if (cnt >= k) T = cand;
+  }
+  for (int i = lane; i < n; i += 32) flag[i] = keys[i] >= T;  // keys are unique: exactly k
+  __syncwarp();
+}
+
+template <int KL>
+__global__ void __launch_bounds__(kThreads, 1)
+    route_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ck, const Args a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int n = blockIdx.x, hp = blockIdx.y, b = blockIdx.z;
+  const int h0 = 2 * hp;
+  const int kvh = h0 / (a.H / a.KVH);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int C = 64, M = 4;
+  const int row0 = n * C;
+  const int nvalid = (a.S - row0) < C ? (a.S - row0) : C;
+  const int N = a.N;
+  uint32_t* pooled = reinterpret_cast<uint32_t*>(smem + L::kFixed);     // [2][N]
+  uint32_t* t0c = pooled + 2 * N;                                        // [2][N]
+  unsigned char* flags = reinterpret_cast<unsigned char*>(t0c + 2 * N);  // [2][N]
+  Misc* ms = reinterpret_cast<Misc*>(flags + ((2 * N + 15) & ~15));
+  volatile int* abort_flag = &ms->abort;
+  uint64_t* q_full = ms->bars + 0;
+  uint64_t* ck_full = ms->bars + 1;   // [2]
+  uint64_t* ck_empty = ms->bars + 3;  // [2]
+  uint64_t* s_full = ms->bars + 5;    // [2]
+  uint64_t* s_free = ms->bars + 7;    // [2]
+  uint64_t* s2_full = ms->bars + 9;
+
+  int f_hi, l_lo;
+  windows(n, a.keep_first, a.keep_last, f_hi, l_lo);
+  const int pool_lo = f_hi, npool = l_lo > f_hi ? l_lo - f_hi : 0;
+  const size_t out0 = (((size_t)b * a.H + h0) * N + n);
+  const size_t out1 = out0 + N;  // head h0+1
+  for (int i = tid; i < 2 * a.Kc; i += kThreads) {
+    const size_t o = (i < a.Kc ? out0 : out1) * a.Kc + (i % a.Kc);
+    a.sel_chunk[o] = -1;
+    a.sel_t0[o] = -1;
+  }
+  for (int i = tid; i < 2 * a.Kg; i += kThreads) {
+    const size_t o = (i < a.Kg ? out0 : out1) * a.Kg + (i % a.Kg);
+    a.open_gid[o] = -1;
+    a.open_t0[o] = -1;
+  }
+  if (a.Kc == 0 || npool == 0) return;
+  const int ntile = (npool + 127) / 128;
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(ck_full + i, 1);
+      mbar_init(ck_empty + i, 1);
+      mbar_init(s_full + i, 1);
+      mbar_init(s_free + i, 128);
+    }
+    mbar_init(s2_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    ms->abort = 0;
+  }
+  for (int i = tid; i < 2 * npool; i += kThreads) {
+    pooled[(i / npool) * N + i % npool] = 0u;
+    t0c[(i / npool) * N + i % npool] = 0xffffffffu;
+  }
+  for (int i = tid; i < 2 * 128; i += kThreads) {
+    ms->gpool[i / 128][i % 128] = 0u;
+    ms->gt0[i / 128][i % 128] = 0xffffffffu;
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&ms->tmem)),
+                 "r"(256));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = ms->tmem;
+  unsigned char* q_s = smem + L::kQ;
+  unsigned char* tile_s = smem + L::kTile;
+
+  // ================================ level 1 ===================================================
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(q_full, 32768);
+      for (int hh = 0; hh < 2; ++hh)
+        for (int kb = 0; kb < 2; ++kb) {
+          unsigned char* dst = q_s + kb * 16384 + hh * 8192;
+          if (a.q_layout == 1) tma_load_3d(dst, &tm_q, kb * 64, h0 + hh, b * a.S + row0, q_full);
+          else tma_load_2d(dst, &tm_q, kb * 64, (b * a.H + h0 + hh) * a.S + row0, q_full);
+        }
+      const int64_t ckrow = ((int64_t)b * a.KVH + kvh) * a.sum_cap + pool_lo;
+      for (int i = 0; i < ntile; ++i) {
+        const int st = i & 1;
+        if (i >= 2 && !mbar_wait(ck_empty + st, ((i >> 1) - 1) & 1, abort_flag, 11)) break;
+        mbar_expect_tx(ck_full + st, 32768);
+        for (int kb = 0; kb < 2; ++kb)
+          tma_load_2d(tile_s + st * 32768 + kb * 16384, &tm_ck, kb * 64, (int)(ckrow + 128 * i), ck_full + st);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16(false);
+      const uint32_t q_addr = smem_u32(q_s);
+      bool ok = mbar_wait(q_full, 0, abort_flag, 12);
+      for (int i = 0; ok && i < ntile; ++i) {
+        const int st = i & 1;
+        if (!mbar_wait(ck_full + st, (i >> 1) & 1, abort_flag, 13)) break;
+        if (i >= 2 && !mbar_wait(s_free + st, ((i >> 1) - 1) & 1, abort_flag, 14)) break;
+        fence_after();
+        const uint32_t k_addr = smem_u32(tile_s + st * 32768);
+        for (int kb = 0; kb < 2; ++kb)
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ss(tmem + st * 128, sdesc(q_addr + kb * 16384 + kk * 32, 16, 1024),
+                   sdesc(k_addr + kb * 16384 + kk * 32, 16, 1024), idesc, (kb | kk) != 0);
+        mma_commit(s_full + st);
+        mma_commit(ck_empty + st);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int hs = row >> 6, t = row & 63;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const bool rvalid = t < nvalid;
+    uint32_t lst[KL];
+#pragma unroll
+    for (int j = 0; j < KL; ++j) lst[j] = 0u;
+    const size_t dbg_row = ((hs ? out1 : out0) * C + t) * (size_t)N + pool_lo;
+    for (int i = 0; i < ntile; ++i) {
+      const int st = i & 1;
+      if (!mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 15)) break;
+      fence_after();
+      const uint32_t sa = tmem + lane_addr + st * 128;
+      const int cmax = (npool - 128 * i) < 128 ? (npool - 128 * i) : 128;
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t r[32];
+        HGA_LD32(sa + 32 * c4, r);
+        tmem_wait_ld();
+        if (rvalid) {
+#pragma unroll
+          for (int cc = 0; cc < 32; ++cc) {
+            const int c = 32 * c4 + cc;
+            if (c < cmax) {
+              const float s = bf16_score(r[cc], a.scale);
+              const uint32_t cr = 128 * i + c;
+              if (a.dbg_l1) a.dbg_l1[dbg_row + cr] = s;
+              uint32_t x = (ord16(s) << 16) | (0xffffu - cr);
+              if (x > lst[KL - 1]) {
+#pragma unroll
+                for (int j = 0; j < KL; ++j) {
+                  const uint32_t hi = max(lst[j], x);
+                  x = min(lst[j], x);
+                  lst[j] = hi;
+                }
+              }
+            }
+          }
+        }
+      }
+      fence_before();
+      mbar_arrive(s_free + st);
+    }
+    // requests -> pooled max score and first requesting row per chunk
+    const int k1 = a.Kc < npool ? a.Kc : npool;
+    if (rvalid) {
+#pragma unroll
+      for (int j = 0; j < KL; ++j) {
+        if (j < k1 && lst[j] != 0u) {
+          const int c = 0xffff - (int)(lst[j] & 0xffffu);
+          atomicMax(&pooled[hs * N + c], lst[j] >> 16);
+          atomicMin(&t0c[hs * N + c], (uint32_t)t);
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // ================================ chunk choice (one warp per head) ==========================
+  if (warp == 2 || warp == 3) {
+    const int hs = warp - 2;
+    uint32_t* keys = pooled + hs * N;
+    unsigned char* fl = flags + hs * N;
+    for (int c = lane; c < npool; c += 32) keys[c] = keys[c] ? ((keys[c] << 16) | (0xffffu - c)) : 0u;
+    __syncwarp();
+    warp_select_u32(keys, npool, a.Kc, fl);
+    const int prev = n - 1;
+    const bool prev_in = n > 0 && prev >= pool_lo && prev < l_lo;
+    if (prev_in) {
+      const int pr = prev - pool_lo;
+      int nsel = 0;
+      for (int c = lane; c < npool; c += 32) nsel += fl[c];
+      for (int o = 16; o; o >>= 1) nsel += __shfl_xor_sync(0xffffffffu, nsel, o);
+      if (!fl[pr]) {
+        if (nsel >= a.Kc) {  // drop the lowest-ranked chosen chunk (lowest score, then highest index)
+          uint32_t mn = 0xffffffffu;
+          for (int c = lane; c < npool; c += 32)
+            if (fl[c]) mn = min(mn, keys[c]);
+          for (int o = 16; o; o >>= 1) mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+          for (int c = lane; c < npool; c += 32)
+            if (fl[c] && keys[c] == mn) fl[c] = 0;
+        }
+        __syncwarp();
+        if (lane == 0) fl[pr] = 1;
+      }
+      __syncwarp();
+      if (lane == 0) t0c[hs * N + pr] = 0;
+      __syncwarp();
+    }
+    int k = 0;
+    const size_t o = (hs ? out1 : out0) * a.Kc;
+    for (int base = 0; base < npool; base += 32) {
+      const int c = base + lane;
+      const bool s = c < npool && fl[c];
+      const unsigned bal = __ballot_sync(0xffffffffu, s);
+      if (s) {
+        const int slot = k + __popc(bal & ((1u << lane) - 1u));
+        const int t0 = (int)t0c[hs * N + c];
+        ms->sel[hs][slot] = pool_lo + c;
+        ms->selt0[hs][slot] = t0;
+        a.sel_chunk[o + slot] = pool_lo + c;
+        a.sel_t0[o + slot] = t0;
+      }
+      k += __popc(bal);
+    }
+    if (lane == 0) ms->ksel[hs] = k;
+  }
+  __syncthreads();
+  const bool do_l2 = a.Kg > 0 && a.Kgr > 0 && !ms->abort;
+
+  // ================================ level 2 ===================================================
+  if (do_l2) {
+    // gather the chosen chunks' group summaries: head hs -> rows [hs*128, hs*128 + 4*ksel)
+    const __nv_bfloat16* gk = a.group_k + ((size_t)b * a.KVH + kvh) * a.sum_cap * M * 128;
+    for (int pc = tid; pc < 256 * 16; pc += kThreads) {
+      const int rrow = pc >> 4, c16 = pc & 15;
+      const int hs = rrow >> 7, j = rrow & 127;
+      uint4 val = make_uint4(0, 0, 0, 0);
+      if (j < 4 * ms->ksel[hs]) {
+        const int chunk = ms->sel[hs][j >> 2];
+        val = *reinterpret_cast<const uint4*>(gk + ((size_t)chunk * M + (j & 3)) * 128 + c16 * 8);
+      }
+      const int kb = c16 >> 3, cc = c16 & 7;
+      *reinterpret_cast<uint4*>(tile_s + kb * 32768 + rrow * 128 + ((cc ^ (rrow & 7)) << 4)) = val;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    fence_before();
+    __syncthreads();
+    fence_after();
+    if (warp == 1 && lane == 0) {
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((256u >> 3) << 17) | ((128u >> 4) << 24);
+      const uint32_t q_addr = smem_u32(q_s), g_addr = smem_u32(tile_s);
+      for (int kb = 0; kb < 2; ++kb)
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ss(tmem, sdesc(q_addr + kb * 16384 + kk * 32, 16, 1024), sdesc(g_addr + kb * 32768 + kk * 32, 16, 1024),
+                 idesc, (kb | kk) != 0);
+      mma_commit(s2_full);
+    }
+    if (warp >= 2) {
+      const int quarter = warp & 3;
+      const int row = quarter * 32 + lane;
+      const int hs = row >> 6, t = row & 63;
+      const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+      const int th = 4 * ms->ksel[hs];
+      const bool ok = mbar_wait(s2_full, 0, abort_flag, 16);
+      fence_after();
+      uint32_t r[128];
+      if (ok) {
+        const uint32_t sa = tmem + lane_addr + hs * 128;
+        HGA_LD32(sa + 0, (r + 0));
+        HGA_LD32(sa + 32, (r + 32));
+        HGA_LD32(sa + 64, (r + 64));
+        HGA_LD32(sa + 96, (r + 96));
+        tmem_wait_ld();
+      }
+      const bool rvalid = ok && t < nvalid;
+      const size_t dbg_row = ((hs ? out1 : out0) * C + t) * (size_t)(a.Kc * M);
+      int nreal = 0;
+#pragma unroll
+      for (int j = 0; j < 128; ++j) {
+        uint32_t key = 0u;
+        if (rvalid && j < th) {
+          if (t >= ms->selt0[hs][j >> 2]) {
+            const float s = bf16_score(r[j], a.scale);
+            key = ord16(s);
+            if (a.dbg_l2) a.dbg_l2[dbg_row + j] = s;
+          } else if (a.dbg_l2) {
+            a.dbg_l2[dbg_row + j] = kNeg;
+          }
+        }
+        r[j] = key;
+        nreal += key != 0u;
+      }
+      if (rvalid && nreal > 0) {
+        // requests = keys > T plus the lowest-index keys == T (Kgr in total)
+        uint32_t T = 0;
+        int need = 1 << 30;
+        const bool all = a.Kgr >= a.Kc * M || nreal <= a.Kgr;
+        if (!all) {
+          for (int bit = 15; bit >= 0; --bit) {
+            const uint32_t cand = T | (1u << bit);
+            int cnt = 0;
+#pragma unroll
+            for (int j = 0; j < 128; ++j) cnt += r[j] >= cand;
+            if (cnt >= a.Kgr) T = cand;
+          }
+          int gt = 0;
+#pragma unroll
+          for (int j = 0; j < 128; ++j) gt += r[j] > T;
+          need = a.Kgr - gt;
+        }
+#pragma unroll
+        for (int j = 0; j < 128; ++j) {
+          bool req = false;
+          if (r[j] != 0u) {
+            if (all || r[j] > T) req = true;
+            else if (r[j] == T && need > 0) { req = true; --need; }
+          }
+          if (req) {
+            atomicMin(&ms->gt0[hs][j], (uint32_t)t);
+            atomicMax(&ms->gpool[hs][j], r[j]);
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (warp == 2 || warp == 3) {
+      const int hs = warp - 2;
+      const int th = 4 * ms->ksel[hs];
+      unsigned char* fl = flags + hs * N;
+      uint32_t* keys = pooled + hs * N;  // reused as 32-bit unique keys of the groups
+      for (int j = lane; j < th; j += 32) {
+        const uint32_t g = ms->gpool[hs][j];
+        keys[j] = (ms->gt0[hs][j] != 0xffffffffu) ? ((g << 16) | (0xffffu - j)) : 0u;
+      }
+      __syncwarp();
+      if (a.Kg >= a.Kc * M) {
+        for (int j = lane; j < th; j += 32) fl[j] = keys[j] != 0u;
+        __syncwarp();
+      } else {
+        warp_select_u32(keys, th, a.Kg, fl);
+      }
+      int k = 0;
+      const size_t o = (hs ? out1 : out0) * a.Kg;
+      for (int base = 0; base < th; base += 32) {
+        const int j = base + lane;
+        const bool s = j < th && fl[j];
+        const unsigned bal = __ballot_sync(0xffffffffu, s);
+        if (s) {
+          const int slot = k + __popc(bal & ((1u << lane) - 1u));
+          a.open_gid[o + slot] = ms->sel[hs][j >> 2] * M + (j & 3);
+          a.open_t0[o + slot] = (int)ms->gt0[hs][j];
+        }
+        k += __popc(bal);
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+  }
+}
+
+}  // namespace rtc
+
+bool route_tc_supported(const hga_params& p, int64_t S) {
+  const int64_t N = (S + 63) / 64;
+  const int Kc = p.topk_chunks > 0 ? (int)(p.topk_chunks < N ? p.topk_chunks : N) : 0;
+  return p.dtype == HGA_DTYPE_BF16 && p.head_dim == 128 && p.chunk_size == 64 && p.group_size == 16 &&
+         (p.nhead / p.kv_heads) % 2 == 0 && Kc <= 32 && N < 65536 && S * p.batch < (1ll << 31);
+}
+
+cudaError_t launch_route_tc(const hga_params& p, int64_t S, const void* q, int q_layout, const void* ck, const void* gk,
+                            int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid, int32_t* open_t0,
+                            float* dbg1, float* dbg2, cudaStream_t st) {
+  using namespace tc;
+  const int N = (int)((S + 63) / 64);
+  const int Kc = p.topk_chunks > 0 ? (p.topk_chunks < N ? p.topk_chunks : N) : 0;
+  const int Tg = Kc * 4;
+  int Kg = p.topk_groups > 0 ? (p.topk_groups < Tg ? p.topk_groups : Tg) : 0;
+  const int Kgr = p.topk_groups > 0 ? ((p.topk_groups / 2) < Tg ? p.topk_groups / 2 : Tg) : 0;
+  if (Kgr == 0) Kg = 0;
+  if (((uintptr_t)q | (uintptr_t)ck | (uintptr_t)gk) & 15) return cudaErrorMisalignedAddress;
+  if ((int64_t)p.batch * p.kv_heads * sum_cap >= (1ll << 31)) return cudaErrorInvalidConfiguration;
+  CUtensorMap mq, mck;
+  const cuuint64_t dck[2] = {128, (cuuint64_t)p.batch * p.kv_heads * sum_cap}, sck[1] = {256};
+  const cuuint32_t bck[2] = {64, 128};
+  if (!make_map(&mck, ck, 2, dck, sck, bck)) return cudaErrorInvalidValue;
+  if (q_layout == 1) {
+    const cuuint64_t dq[3] = {128, (cuuint64_t)p.nhead, (cuuint64_t)(p.batch * S)};
+    const cuuint64_t sq[2] = {256, (cuuint64_t)p.nhead * 256};
+    const cuuint32_t bq[3] = {64, 1, 64};
+    if (!make_map(&mq, q, 3, dq, sq, bq)) return cudaErrorInvalidValue;
+  } else {
+    const cuuint64_t dq[2] = {128, (cuuint64_t)p.batch * p.nhead * S};
+    const cuuint64_t sq[1] = {256};
+    const cuuint32_t bq[2] = {64, 64};
+    if (!make_map(&mq, q, 2, dq, sq, bq)) return cudaErrorInvalidValue;
+  }
+  rtc::Args a;
+  a.S = (int)S; a.H = p.nhead; a.KVH = p.kv_heads; a.N = N; a.Kc = Kc; a.Kg = Kg; a.Kgr = Kgr;
+  a.keep_first = p.keep_first; a.keep_last = p.keep_last; a.q_layout = q_layout; a.sum_cap = sum_cap;
+  a.scale = p.scale; a.group_k = (const __nv_bfloat16*)gk;
+  a.sel_chunk = sel_chunk; a.sel_t0 = sel_t0; a.open_gid = open_gid; a.open_t0 = open_t0;
+  a.dbg_l1 = dbg1; a.dbg_l2 = dbg2;
+  const int smem = rtc::L::kFixed + 2 * N * 4 * 2 + ((2 * N + 15) & ~15) + (int)sizeof(rtc::Misc) + 1024;
+  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
+  dim3 grid(N, p.nhead / 2, p.batch);
+  cudaError_t e;
+  if (Kc <= 16) {
+    e = cudaFuncSetAttribute(rtc::route_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    rtc::route_tc_kernel<16><<<grid, rtc::kThreads, smem, st>>>(mq, mck, a);
+  } else {
+    e = cudaFuncSetAttribute(rtc::route_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    rtc::route_tc_kernel<32><<<grid, rtc::kThreads, smem, st>>>(mq, mck, a);
+  }
+  return cudaGetLastError();
+}
+
+HGA_DEFINE_ERROR_READER(route_tc_error_status)
+
+}  // namespace hga

@@ -103,8 +103,9 @@ def ctypes_params(p: HgaParams):
 
 
 def route_prefill(p: HgaParams, q: torch.Tensor, chunk_k: torch.Tensor, group_k: torch.Tensor,
-                  seq_len: Optional[int] = None, debug: bool = False) -> Dict[str, torch.Tensor]:
-    """Two-level prefill routing (see hga_route_prefill).  q [B,H,S,Dh] (or a BSHD view)."""
+                  seq_len: Optional[int] = None, debug: bool = False, impl: int = 0) -> Dict[str, torch.Tensor]:
+    """Two-level prefill routing (see hga_route_prefill_impl).  q [B,H,S,Dh] (or a BSHD view).
+    impl: 0 auto, 1 portable SIMT router, 2 tcgen05 router."""
     _require_cuda(q, chunk_k, group_k)
     B, H, S, Dh = q.shape
     S = S if seq_len is None else seq_len
@@ -125,10 +126,10 @@ def route_prefill(p: HgaParams, q: torch.Tensor, chunk_k: torch.Tensor, group_k:
     if (chunk_k.stride(-1) != 1 or chunk_k.stride(2) != Dh or group_k.stride(-1) != 1
             or group_k.stride(1) != sum_cap * M * Dh or chunk_k.stride(0) != chunk_k.shape[1] * chunk_k.stride(1)):
         raise _lib.HgaError("summaries must be row-slices of contiguous [B,KVH,cap,(M,)Dh] buffers")
-    check(lib().hga_route_prefill(ctypes_params(p), S, ptr(q), q_layout_of(q), ptr(chunk_k), ptr(group_k), sum_cap,
-                                  ptr(res["sel_chunk"]), ptr(res["sel_t0"]), ptr(res["open_gid"]),
-                                  ptr(res["open_t0"]), ptr(res.get("dbg_l1")), ptr(res.get("dbg_l2")),
-                                  stream_ptr(dev)), "hga_route_prefill")
+    check(lib().hga_route_prefill_impl(ctypes_params(p), S, ptr(q), q_layout_of(q), ptr(chunk_k), ptr(group_k),
+                                       sum_cap, ptr(res["sel_chunk"]), ptr(res["sel_t0"]), ptr(res["open_gid"]),
+                                       ptr(res["open_t0"]), ptr(res.get("dbg_l1")), ptr(res.get("dbg_l2")), impl,
+                                       stream_ptr(dev)), "hga_route_prefill")
     return res
 
 

@@ -99,7 +99,9 @@ class VramKVCacheStore(KVCacheStore):
         return st
 
     def _token_tensor(self, rows: int) -> torch.Tensor:
-        return torch.empty(self.B, self.kvh, rows, self.dh, device=self.compute_device, dtype=self.dtype)
+        # zero-filled: the tensor-core kernels stream whole 16-row units, so rows past the
+        # valid length must hold finite values (a NaN in V would poison P.V even at P = 0)
+        return torch.zeros(self.B, self.kvh, rows, self.dh, device=self.compute_device, dtype=self.dtype)
 
     def ensure_capacity(self, layer: int, n_chunks: int, n_tokens: Optional[int] = None) -> LayerBuffers:
         """Grow (by doubling) so that ``n_chunks`` closed chunks and ``n_tokens`` token rows fit."""

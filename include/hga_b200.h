@@ -80,13 +80,24 @@ int hga_route_prefill(const hga_params* p, int64_t seq_len, const void* q, int32
                       int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid, int32_t* open_t0,
                       float* dbg_l1, float* dbg_l2, cudaStream_t stream);
 
+/* hga_route_prefill with an explicit kernel choice: impl 0 = auto, 1 = portable SIMT router,
+ * 2 = tcgen05 router (bf16, head_dim 128, chunk 64, group 16, topk_chunks <= 32).  Both
+ * implement the same rules and tie order; the tensor-core one accumulates the scoring dot
+ * products in a different order (same fp32 accumulator, same bf16 rounding points). */
+int hga_route_prefill_impl(const hga_params* p, int64_t seq_len, const void* q, int32_t q_layout,
+                           const void* chunk_k, const void* group_k, int64_t sum_cap,
+                           int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid, int32_t* open_t0,
+                           float* dbg_l1, float* dbg_l2, int32_t impl, cudaStream_t stream);
+
 /* (3)+(4) Working-set attention of the chunk-parallel prefill: replaces the token-segment
  * assembly of vectorized.py:386-490 and RoutedKV.attend(use_summaries=False)
  * (chunk_router.py:139-158).  Query row t of chunk n attends, with an fp32 online softmax, to
  * the causal prefix of its own chunk, the keep_last window [l_lo, n), the keep_first window
  * [0, f_hi) and every opened group with t0 <= t.  Output [B,H,S,Dh] (out_layout 0) or
  * [B,S,H,Dh] (out_layout 1) in p->dtype.  impl: 0 = auto, 1 = portable SIMT kernel,
- * 2 = tcgen05/TMEM tensor-core kernel (bf16, head_dim 128, chunk 64, group 16). */
+ * 2 = tcgen05/TMEM tensor-core kernel (bf16, head_dim 128, chunk 64, group 16).  The tensor-core
+ * kernel streams whole 16-row units: K/V rows [seq_len, round_up(seq_len, 16)) of every
+ * (batch, kv-head) block must hold finite values (the stores zero-fill their buffers). */
 int hga_attend_prefill(const hga_params* p, int64_t seq_len, const void* q, int32_t q_layout,
                        const void* k_rope, const void* v, int64_t kv_cap,
                        const int32_t* open_gid, const int32_t* open_t0,

