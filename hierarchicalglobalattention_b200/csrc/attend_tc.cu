@@ -7,38 +7,44 @@
 //   current chunk (4 units, causal), keep_last window, keep_first window (both heads see all of
 //   them), then the union of the two heads' opened groups (each head sees its own ones from its
 //   first-visible row t0 on).
-// Per 128-key tile (8 units):
+// For every row a unit's visible keys form a prefix (causal: keys j <= t - 16u; otherwise all or
+// none), so masking is one count per (row, unit).
+// Per 64-key tile (4 units):
 //   TMA warp      : 16-row boxes of K and V per unit into a 2-stage SW128 smem ring
-//   MMA warp      : S = Q.K^T  (M128 N128 K16 x8, A/B from smem, D in TMEM, double-buffered)
+//   MMA warp      : S = Q.K^T  (M128 N64, A/B from smem, D in TMEM, double-buffered)
 //                   O += P.V   (A = P from TMEM, B = V from smem as MN-major, D = O in TMEM)
-//   4 softmax warps: one thread per query row (TMEM lane): mask, online softmax in the exp2
-//                   domain with lazy rescaling (only when the row max grows by > 2^8), P -> TMEM
-// Every mbarrier wait is bounded; on timeout the CTA records an error code (hga_tc_status) and
-// leaves after releasing its TMEM.
+//   4 softmax warps: one thread per query row (TMEM lane): online softmax in the exp2 domain with
+//                   lazy rescaling (only when the row max grows by > 2^8), P -> TMEM as bf16.
+//                   TMEM loads/stores are warp-collective, so a rescale is decided per warp.
+// ~105 KB smem and 256 TMEM columns per CTA, so two CTAs share an SM and hide each other's
+// serial phases.  Every mbarrier wait is bounded; on timeout the CTA records an error code
+// (hga_device_status) and leaves after releasing its TMEM.
 #include "tc_common.cuh"
 
 namespace hga {
 namespace tc {
 
 constexpr int kThreads = 192;  // warp0 TMA, warp1 MMA, warps2-5 softmax/epilogue
-constexpr int kUnitsPerTile = 8;
-constexpr int kMaxUnits = 336;  // current 4 + windows <= 64 + opened union <= 256, rounded up to whole tiles
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+constexpr int kUnitsPerTile = 4;
+constexpr int kMaxUnits = 328;  // current 4 + windows <= 64 + opened union <= 256, rounded up to whole tiles
+constexpr int kMaxKg = 128;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColS0 = 0, kColS1 = 64, kColO = 128;
 
 struct Unit {
-  int pos;      // first token row of the unit inside the (b, kvh) row block
-  int tmin0;    // first visible query row for head 0 (64 = never)
-  int tmin1;    // same for head 1
-  int causal;   // 1: key j of the unit is visible to row t iff t >= tmin + j
+  int pos;    // first token row of the unit inside the (b, kvh) row block
+  int tmin0;  // first visible query row for head 0 (>= 64: never)
+  int tmin1;  // same for head 1
+  int causal; // 1: key j of the unit is visible to row t iff t >= tmin + j
 };
 
 struct SmemLayout {
-  static constexpr int kQ = 0;                       // 2 x 16 KB (dh halves), rows 0..127
-  static constexpr int kStage = 32768;               // 2 stages x (K 2x16KB + V 2x16KB)
-  static constexpr int kStageBytes = 65536;
+  static constexpr int kQ = 0;              // 2 x 16 KB (dh halves), rows 0..127
+  static constexpr int kStage = 32768;      // 2 stages x (K 2x8KB + V 2x8KB)
+  static constexpr int kStageBytes = 32768;
   static constexpr int kUnits = kStage + 2 * kStageBytes;
-  static constexpr int kBars = kUnits + kMaxUnits * 16;
+  static constexpr int kLists = kUnits + kMaxUnits * 16;  // [4][kMaxKg] ints: gid0, t00, gid1, t01
+  static constexpr int kBars = kLists + 4 * kMaxKg * 4;
   static constexpr int kMisc = kBars + 16 * 8;
   static constexpr int kTotal = kMisc + 64;
 };
@@ -52,7 +58,18 @@ struct Args {
   __nv_bfloat16* out;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
     attend_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const Args a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -66,19 +83,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nvalid = (a.S - row0) < C ? (a.S - row0) : C;
 
   Unit* units = reinterpret_cast<Unit*>(smem + SmemLayout::kUnits);
+  int* lists = reinterpret_cast<int*>(smem + SmemLayout::kLists);
+  int* gidA = lists;
+  int* t0A = lists + kMaxKg;
+  int* gidB = lists + 2 * kMaxKg;
+  int* t0B = lists + 3 * kMaxKg;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::kBars);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;   // [2]
   uint64_t* kv_empty = bars + 3;  // [2]
   uint64_t* s_full = bars + 5;    // [2]
   uint64_t* p_full = bars + 7;    // [2]
-  uint64_t* pv_done = bars + 9;
+  uint64_t* pv_done = bars + 9;   // one completion per P.V (its waits are never more than one phase behind)
+  uint64_t* o_done = bars + 10;   // single completion after the last P.V (the epilogue's wait)
   int* misc = reinterpret_cast<int*>(smem + SmemLayout::kMisc);
   volatile int* abort_flag = misc + 0;
   int* n_units_s = misc + 1;
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(misc + 2);
   int* la_s = misc + 3;
-  int* nb_s = misc + 4;
+  int* lb_s = misc + 4;
 
   // ---- set-up: barriers, TMEM, unit table -------------------------------------------------
   int f_hi, l_lo;
@@ -93,6 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(p_full + i, 128);
     }
     mbar_init(pv_done, 1);
+    mbar_init(o_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     *abort_flag = 0;
   }
@@ -101,7 +125,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  // shared units: current chunk (causal), last window, first window
+  // stage both heads' open lists in smem (coalesced); visible entries are a prefix of each list
+  const size_t tile0 = (((size_t)b * a.H + h0) * a.N + n) * a.Kg;
+  const size_t tile1 = (((size_t)b * a.H + h1) * a.N + n) * a.Kg;
+  for (int i = tid; i < a.Kg; i += kThreads) {
+    gidA[i] = a.open_gid[tile0 + i];
+    t0A[i] = a.open_t0[tile0 + i];
+    gidB[i] = a.open_gid[tile1 + i];
+    t0B[i] = a.open_t0[tile1 + i];
+  }
   for (int u = tid; u < n_shared; u += kThreads) {
     Unit e;
     if (u < 4) {
@@ -113,34 +145,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     units[u] = e;
   }
-  // opened groups: list A (head 0) in order, then the B-only entries (head 1)
-  const size_t tile0 = (((size_t)b * a.H + h0) * a.N + n) * a.Kg;
-  const size_t tile1 = (((size_t)b * a.H + h1) * a.N + n) * a.Kg;
+  __syncthreads();
   if (warp == 2) {
     int la = 0, lb = 0;
     for (int base = 0; base < a.Kg; base += 32) {
       const int j = base + lane;
-      const bool va = j < a.Kg && a.open_gid[tile0 + j] >= 0 && a.open_t0[tile0 + j] < nvalid;
-      const bool vb = j < a.Kg && a.open_gid[tile1 + j] >= 0 && a.open_t0[tile1 + j] < nvalid;
+      const bool va = j < a.Kg && gidA[j] >= 0 && t0A[j] < nvalid;
+      const bool vb = j < a.Kg && gidB[j] >= 0 && t0B[j] < nvalid;
       la += __popc(__ballot_sync(0xffffffffu, va));
       lb += __popc(__ballot_sync(0xffffffffu, vb));
     }
-    if (lane == 0) { *la_s = la; *nb_s = lb; }
+    if (lane == 0) { *la_s = la; *lb_s = lb; }
   }
   __syncthreads();
-  const int la = *la_s, lb = *nb_s;
-  // valid entries are a prefix of each list (the router pads with -1 after the visible ones)
+  const int la = *la_s, lb = *lb_s;
+  // opened groups: list A (head 0) in order, then the B-only entries (head 1)
   for (int i = tid; i < la; i += kThreads) {
-    const int g = a.open_gid[tile0 + i];
-    int t1 = C;
-    int lo = 0, hi = lb - 1;  // binary search g in list B
+    const int g = gidA[i];
+    int t1 = 1 << 20;
+    int lo = 0, hi = lb - 1;
     while (lo <= hi) {
       const int mid = (lo + hi) >> 1;
-      const int x = a.open_gid[tile1 + mid];
-      if (x == g) { t1 = a.open_t0[tile1 + mid]; break; }
+      const int x = gidB[mid];
+      if (x == g) { t1 = t0B[mid]; break; }
       if (x < g) lo = mid + 1; else hi = mid - 1;
     }
-    Unit e; e.pos = g * gs; e.tmin0 = a.open_t0[tile0 + i]; e.tmin1 = t1; e.causal = 0;
+    Unit e; e.pos = g * gs; e.tmin0 = t0A[i]; e.tmin1 = t1; e.causal = 0;
     units[n_shared + i] = e;
   }
   if (warp == 3) {
@@ -150,12 +180,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool keep = false;
       int g = 0;
       if (j < lb) {
-        g = a.open_gid[tile1 + j];
+        g = gidB[j];
         keep = true;
         int lo = 0, hi = la - 1;
         while (lo <= hi) {
           const int mid = (lo + hi) >> 1;
-          const int x = a.open_gid[tile0 + mid];
+          const int x = gidA[mid];
           if (x == g) { keep = false; break; }
           if (x < g) lo = mid + 1; else hi = mid - 1;
         }
@@ -163,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const unsigned bal = __ballot_sync(0xffffffffu, keep);
       if (keep) {
         const int slot = n_shared + la + written + __popc(bal & ((1u << lane) - 1u));
-        Unit e; e.pos = g * gs; e.tmin0 = C; e.tmin1 = a.open_t0[tile1 + j]; e.causal = 0;
+        Unit e; e.pos = g * gs; e.tmin0 = 1 << 20; e.tmin1 = t0B[j]; e.causal = 0;
         units[slot] = e;
       }
       written += __popc(bal);
@@ -199,13 +229,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = i & 1;
         if (i >= 2 && !mbar_wait(kv_empty + st, ((i >> 1) - 1) & 1, abort_flag, 1)) break;
         unsigned char* kdst = smem + SmemLayout::kStage + st * SmemLayout::kStageBytes;
-        unsigned char* vdst = kdst + 32768;
-        mbar_expect_tx(kv_full + st, 65536);
+        unsigned char* vdst = kdst + 16384;
+        mbar_expect_tx(kv_full + st, 32768);
         for (int u = 0; u < kUnitsPerTile; ++u) {
           const int row = (int)(kvrow + units[i * kUnitsPerTile + u].pos);
           for (int kb = 0; kb < 2; ++kb) {
-            tma_load_2d(kdst + kb * 16384 + u * 2048, &tm_k, kb * 64, row, kv_full + st);
-            tma_load_2d(vdst + kb * 16384 + u * 2048, &tm_v, kb * 64, row, kv_full + st);
+            tma_load_2d(kdst + kb * 8192 + u * 2048, &tm_k, kb * 64, row, kv_full + st);
+            tma_load_2d(vdst + kb * 8192 + u * 2048, &tm_v, kb * 64, row, kv_full + st);
           }
         }
       }
@@ -213,7 +243,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------- MMA issuer ---------------------------------------------
     if (lane == 0) {
-      const uint32_t id_qk = idesc_bf16(false), id_pv = idesc_bf16(true);
+      // S: M=128, N=64, B K-major.  O: M=128, N=128, B (V) MN-major.
+      const uint32_t id_qk = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+      const uint32_t id_pv = idesc_bf16(true);
       const uint32_t q_addr = smem_u32(q_s);
       bool ok = mbar_wait(q_full, 0, abort_flag, 2);
       fence_after();
@@ -226,112 +258,140 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t k_addr = smem_u32(smem + SmemLayout::kStage + st * SmemLayout::kStageBytes);
           const uint32_t d = tmem + (st ? kColS1 : kColS0);
           for (int kb = 0; kb < 2; ++kb)
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t da = sdesc(q_addr + kb * 16384 + kk * 32, 16, 1024);
-              const uint64_t db = sdesc(k_addr + kb * 16384 + kk * 32, 16, 1024);
-              mma_ss(d, da, db, id_qk, (kb | kk) != 0);
-            }
+            for (int kk = 0; kk < 4; ++kk)
+              mma_ss(d, sdesc(q_addr + kb * 16384 + kk * 32, 16, 1024), sdesc(k_addr + kb * 8192 + kk * 32, 16, 1024),
+                     id_qk, (kb | kk) != 0);
           mma_commit(s_full + st);
         }
         if (i >= 1) {
           const int j = i - 1, st = j & 1;
           if (!mbar_wait(p_full + st, (j >> 1) & 1, abort_flag, 5)) break;
           fence_after();
-          const uint32_t v_addr = smem_u32(smem + SmemLayout::kStage + st * SmemLayout::kStageBytes + 32768);
+          const uint32_t v_addr = smem_u32(smem + SmemLayout::kStage + st * SmemLayout::kStageBytes + 16384);
           const uint32_t p_col = tmem + (st ? kColS1 : kColS0);
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t db = sdesc(v_addr + kk * 2048, 16384, 1024);
-            mma_ts(tmem + kColO, p_col + kk * 8, db, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ts(tmem + kColO, p_col + kk * 8, sdesc(v_addr + kk * 2048, 8192, 1024), id_pv,
+                   (j > 0 || kk > 0) ? 1u : 0u);
           mma_commit(pv_done);
           mma_commit(kv_empty + st);
+          if (j == ntiles - 1) mma_commit(o_done);
         }
       }
     }
   } else {
     // ------------------------------- softmax / epilogue -------------------------------------
+    // tcgen05.ld / st are warp-collective (.sync.aligned): every branch around them is warp-uniform
     const int quarter = warp & 3;          // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;   // 0..127
     const int head_sel = row >> 6;         // 0 -> h0, 1 -> h1
     const int t = row & 63;
+    const bool rvalid = t < nvalid;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    float m_run = -INFINITY, l_run = 0.f;
+    const float sl2 = a.scale_log2;
+    float m_run = -INFINITY;  // running max in the scaled log2 domain
+    float l_run = 0.f;
     bool ok = true;
     for (int i = 0; i < ntiles && ok; ++i) {
       const int st = i & 1;
-      ok = mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 6);
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 6));
       if (!ok) break;
       fence_after();
       const uint32_t s_addr = tmem + lane_addr + (st ? kColS1 : kColS0);
-      uint32_t r[128];
+      uint32_t r[64];
       HGA_LD32(s_addr + 0, (r + 0));
       HGA_LD32(s_addr + 32, (r + 32));
-      HGA_LD32(s_addr + 64, (r + 64));
-      HGA_LD32(s_addr + 96, (r + 96));
-      tmem_wait_ld();
-      float mx = -INFINITY;
+      // visible-prefix length of each unit for this row
+      int cnt[kUnitsPerTile];
 #pragma unroll
       for (int u = 0; u < kUnitsPerTile; ++u) {
         const Unit e = units[i * kUnitsPerTile + u];
         const int tmin = head_sel ? e.tmin1 : e.tmin0;
+        int c = e.causal ? t - tmin + 1 : (t >= tmin ? 16 : 0);
+        c = c < 0 ? 0 : (c > 16 ? 16 : c);
+        cnt[u] = rvalid ? c : 0;
+      }
+      tmem_wait_ld();
+      float mx = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int c = u * 16 + j;
-          const bool vis = t < nvalid && t >= tmin + (e.causal ? j : 0);
-          const float s = vis ? __uint_as_float(r[c]) * a.scale_log2 : -INFINITY;
-          r[c] = __float_as_uint(s);
-          mx = fmaxf(mx, s);
+      for (int u = 0; u < kUnitsPerTile; ++u) {
+        if (cnt[u] == 16) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) mx = fmaxf(mx, __uint_as_float(r[u * 16 + j]));
+        } else if (cnt[u] > 0) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (j < cnt[u]) mx = fmaxf(mx, __uint_as_float(r[u * 16 + j]));
         }
       }
-      const float m_new = fmaxf(m_run, mx);
-      if (m_new > m_run + 8.f || (m_run == -INFINITY && m_new != -INFINITY)) {
-        const float alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
-        l_run *= alpha;
-        if (i > 0 && m_run != -INFINITY) {
-          // O holds sum over tiles < i: wait for the last P.V, then rescale this row
-          ok = mbar_wait(pv_done, (i - 1) & 1, abort_flag, 7);
-          if (!ok) break;
-          fence_after();
-          const uint32_t o_addr = tmem + lane_addr + kColO;
-          for (int c0 = 0; c0 < 128; c0 += 32) {
-            uint32_t o[32];
-            HGA_LD32(o_addr + c0, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            HGA_ST32(o_addr + c0, o);
-          }
-          tmem_wait_st();
+      const float m_tile = mx * sl2;
+      // lazy rescale: only when the max grows by more than 2^8 (or the first visible keys arrive)
+      float alpha = 1.f;
+      bool rescale_o = false;
+      if (m_tile > m_run + 8.f) {
+        if (m_run != -INFINITY) {
+          alpha = ex2(m_run - m_tile);
+          l_run *= alpha;
+          rescale_o = true;
         }
-        m_run = m_new;
+        m_run = m_tile;
+      }
+      if (__any_sync(0xffffffffu, rescale_o)) {
+        // O holds the sum over tiles < i: wait for the last P.V, then rescale (alpha = 1 elsewhere)
+        ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (i - 1) & 1, abort_flag, 7));
+        if (!ok) break;
+        fence_after();
+        const uint32_t o_addr = tmem + lane_addr + kColO;
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t o[32];
+          HGA_LD32(o_addr + c0, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+          HGA_ST32(o_addr + c0, o);
+        }
+        tmem_wait_st();
       }
       float psum = 0.f;
-      uint32_t pk[64];
+      uint32_t pk[32];
+      const float nm = -m_run;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float s0 = __uint_as_float(r[2 * c]), s1 = __uint_as_float(r[2 * c + 1]);
-        const float p0 = (s0 == -INFINITY) ? 0.f : exp2f(s0 - m_run);
-        const float p1 = (s1 == -INFINITY) ? 0.f : exp2f(s1 - m_run);
-        psum += p0 + p1;
-        __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
-        pk[c] = *reinterpret_cast<uint32_t*>(&v2);
+      for (int u = 0; u < kUnitsPerTile; ++u) {
+        if (cnt[u] == 16) {
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const float p0 = ex2(fmaf(__uint_as_float(r[u * 16 + j]), sl2, nm));
+            const float p1 = ex2(fmaf(__uint_as_float(r[u * 16 + j + 1]), sl2, nm));
+            psum += p0 + p1;
+            pk[(u * 16 + j) >> 1] = pack_bf16(p0, p1);
+          }
+        } else if (cnt[u] == 0) {
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) pk[(u * 16 + j) >> 1] = 0u;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const float p0 = j < cnt[u] ? ex2(fmaf(__uint_as_float(r[u * 16 + j]), sl2, nm)) : 0.f;
+            const float p1 = j + 1 < cnt[u] ? ex2(fmaf(__uint_as_float(r[u * 16 + j + 1]), sl2, nm)) : 0.f;
+            psum += p0 + p1;
+            pk[(u * 16 + j) >> 1] = pack_bf16(p0, p1);
+          }
+        }
       }
       l_run += psum;
-      HGA_ST32(s_addr + 0, pk);
-      HGA_ST32(s_addr + 32, (pk + 32));
+      HGA_ST32(s_addr, pk);
       tmem_wait_st();
       fence_before();
       mbar_arrive(p_full + st);
     }
     // epilogue
-    if (ok && ntiles > 0) ok = mbar_wait(pv_done, (ntiles - 1) & 1, abort_flag, 8);
+    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, 0, abort_flag, 8));
     if (ok) {
       fence_after();
       const int h = head_sel ? h1 : h0;
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       const uint32_t o_addr = tmem + lane_addr + kColO;
       __nv_bfloat16* dst = nullptr;
-      if (t < nvalid) {
+      if (rvalid) {
         const int64_t tt = row0 + t;
         dst = a.out_layout == 1 ? a.out + (((int64_t)b * a.S + tt) * a.H + h) * 128
                                 : a.out + (((int64_t)b * a.H + h) * a.S + tt) * 128;
@@ -343,10 +403,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (dst) {
           uint32_t w[16];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            __nv_bfloat162 v2 = __floats2bfloat162_rn(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
-            w[c] = *reinterpret_cast<uint32_t*>(&v2);
-          }
+          for (int c = 0; c < 16; ++c)
+            w[c] = pack_bf16(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
           uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
 #pragma unroll
           for (int c = 0; c < 4; ++c) d4[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
@@ -376,7 +434,8 @@ cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const void* q, int 
   const int N = (int)((S + 63) / 64);
   // windows wider than the unit table hold go through the portable kernel
   const int kl = p.keep_last < N ? p.keep_last : N, kf = p.keep_first < N ? p.keep_first : N;
-  if (kl + kf > 16 || Kg > 128) return cudaErrorNotSupported;
+  if (kl + kf > 16 || Kg > kMaxKg) return cudaErrorNotSupported;
+  if ((int64_t)p.batch * p.kv_heads * kv_cap >= (1ll << 31)) return cudaErrorNotSupported;
   if (((uintptr_t)q | (uintptr_t)k_rope | (uintptr_t)v | (uintptr_t)out) & 15) return cudaErrorMisalignedAddress;
   CUtensorMap mq, mk, mv;
   const cuuint64_t rows_kv = (cuuint64_t)p.batch * p.kv_heads * kv_cap;

@@ -203,7 +203,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const size_t dbg_row = ((hs ? out1 : out0) * C + t) * (size_t)N + pool_lo;
     for (int i = 0; i < ntile; ++i) {
       const int st = i & 1;
-      if (!mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 15)) break;
+      // tcgen05.ld is warp-collective: keep the branch around it warp-uniform
+      if (!__all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 15))) break;
       fence_after();
       const uint32_t sa = tmem + lane_addr + st * 128;
       const int cmax = (npool - 128 * i) < 128 ? (npool - 128 * i) : 128;
@@ -336,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int hs = row >> 6, t = row & 63;
       const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
       const int th = 4 * ms->ksel[hs];
-      const bool ok = mbar_wait(s2_full, 0, abort_flag, 16);
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(s2_full, 0, abort_flag, 16));
       fence_after();
       uint32_t r[128];
       if (ok) {

@@ -47,10 +47,10 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000)  // suspend at most ~20 us per attempt
       : "memory");
   return ok != 0;
 }
@@ -63,15 +63,14 @@ __device__ __forceinline__ unsigned long long global_ns() {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
-  unsigned it = 0;
+  // try_wait may suspend the thread for a hardware-defined time: check the clock and the CTA's
+  // abort flag after every attempt so the limit holds regardless of that time
   while (!mbar_try(bar, parity)) {
-    if (((++it) & 255u) == 0) {
-      if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
-        *abort_flag = 1;
-        atomicCAS(&g_tc_error, 0, code);
-        return false;
-      }
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      atomicCAS(&g_tc_error, 0, code);
+      return false;
     }
   }
   return true;
