@@ -186,7 +186,7 @@ def run_ours(args, rank, world, device):
                 launches_per_step=5, h2d=x_host.numel() * 2, d2h=out_host.numel() * 2)
 
 
-def cpu_sample(seconds_hint: float = 20.0, S: int = 32768, n_sample_chunks: int = 6):
+def cpu_sample(seconds_hint: float = 20.0, S: int = 32768, n_sample_chunks: int = 128):
     """Oracle port of the reference path on the host cores, on a bounded sample of the workload.
 
     The sample: the full-sequence projections + q/k RMSNorm + RoPE + summaries (every key of the

@@ -56,6 +56,7 @@ struct Misc {
 };
 
 // Warp-wide radix select over keys[0..n) (unique 32-bit keys, 0 = absent): flags the k largest.
+// Keys are cached in registers (up to 64 per lane, n <= 2048); larger n streams from smem.
 __device__ void warp_select_u32(const uint32_t* keys, int n, int k, unsigned char* flag) {
   const int lane = threadIdx.x & 31;
   int nreal = 0;
@@ -67,19 +68,35 @@ __device__ void warp_select_u32(const uint32_t* keys, int n, int k, unsigned cha
     return;
   }
   uint32_t T = 0;
-  for (int bit = 31; bit >= 0; --bit) {
-    const uint32_t cand = T | (1u << bit);
-    int cnt = 0;
-    for (int i = lane; i < n; i += 32) cnt += keys[i] >= cand;
-    for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-    if (cnt >= k) T = cand;
+  if (n <= 32 * 64) {
+    uint32_t kr[64];
+#pragma unroll
+    for (int m = 0; m < 64; ++m) kr[m] = (lane + 32 * m < n) ? keys[lane + 32 * m] : 0u;
+    const int mmax = (n + 31) / 32;
+    for (int bit = 31; bit >= 0; --bit) {
+      const uint32_t cand = T | (1u << bit);
+      int cnt = 0;
+#pragma unroll
+      for (int m = 0; m < 64; ++m)
+        if (m < mmax) cnt += kr[m] >= cand;
+      cnt = __reduce_add_sync(0xffffffffu, cnt);
+      if (cnt >= k) T = cand;
+    }
+  } else {
+    for (int bit = 31; bit >= 0; --bit) {
+      const uint32_t cand = T | (1u << bit);
+      int cnt = 0;
+      for (int i = lane; i < n; i += 32) cnt += keys[i] >= cand;
+      cnt = __reduce_add_sync(0xffffffffu, cnt);
+      if (cnt >= k) T = cand;
+    }
   }
   for (int i = lane; i < n; i += 32) flag[i] = keys[i] >= T;  // keys are unique: exactly k
   __syncwarp();
 }
 
 template <int KL>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     route_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ck, const Args a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -197,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int hs = row >> 6, t = row & 63;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const bool rvalid = t < nvalid;
-    uint32_t lst[KL];
+    uint32_t lst[KL];  // running top-KL request keys of this row, descending
 #pragma unroll
     for (int j = 0; j < KL; ++j) lst[j] = 0u;
     const size_t dbg_row = ((hs ? out1 : out0) * C + t) * (size_t)N + pool_lo;
@@ -217,10 +234,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int cc = 0; cc < 32; ++cc) {
             const int c = 32 * c4 + cc;
             if (c < cmax) {
-              const float s = bf16_score(r[cc], a.scale);
+              const float sc = bf16_score(r[cc], a.scale);
               const uint32_t cr = 128 * i + c;
-              if (a.dbg_l1) a.dbg_l1[dbg_row + cr] = s;
-              uint32_t x = (ord16(s) << 16) | (0xffffu - cr);
+              if (a.dbg_l1) a.dbg_l1[dbg_row + cr] = sc;
+              uint32_t x = (ord16(sc) << 16) | (0xffffu - cr);
               if (x > lst[KL - 1]) {
 #pragma unroll
                 for (int j = 0; j < KL; ++j) {
@@ -236,7 +253,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_before();
       mbar_arrive(s_free + st);
     }
-    // requests -> pooled max score and first requesting row per chunk
+    // requests = top k1 of the union of the four lists (4-way merge) -> pooled max score and
+    // first requesting row per chunk
     const int k1 = a.Kc < npool ? a.Kc : npool;
     if (rvalid) {
 #pragma unroll
@@ -339,20 +357,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int th = 4 * ms->ksel[hs];
       const bool ok = __all_sync(0xffffffffu, mbar_wait(s2_full, 0, abort_flag, 16));
       fence_after();
-      uint32_t r[128];
+      constexpr int KT = 4 * KL;  // candidate columns per head (Kc * M <= 4 * KL)
+      uint32_t r[KT];
       if (ok) {
         const uint32_t sa = tmem + lane_addr + hs * 128;
-        HGA_LD32(sa + 0, (r + 0));
-        HGA_LD32(sa + 32, (r + 32));
-        HGA_LD32(sa + 64, (r + 64));
-        HGA_LD32(sa + 96, (r + 96));
+#pragma unroll
+        for (int c0 = 0; c0 < KT; c0 += 32) HGA_LD32(sa + c0, (r + c0));
         tmem_wait_ld();
       }
       const bool rvalid = ok && t < nvalid;
       const size_t dbg_row = ((hs ? out1 : out0) * C + t) * (size_t)(a.Kc * M);
       int nreal = 0;
 #pragma unroll
-      for (int j = 0; j < 128; ++j) {
+      for (int j = 0; j < KT; ++j) {
         uint32_t key = 0u;
         if (rvalid && j < th) {
           if (t >= ms->selt0[hs][j >> 2]) {
@@ -366,35 +383,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         r[j] = key;
         nreal += key != 0u;
       }
-      if (rvalid && nreal > 0) {
-        // requests = keys > T plus the lowest-index keys == T (Kgr in total)
-        uint32_t T = 0;
-        int need = 1 << 30;
-        const bool all = a.Kgr >= a.Kc * M || nreal <= a.Kgr;
-        if (!all) {
-          for (int bit = 15; bit >= 0; --bit) {
-            const uint32_t cand = T | (1u << bit);
-            int cnt = 0;
+      // requests = keys > T plus the lowest-index keys == T (Kgr in total); every lane runs the
+      // warp reductions below, rows without real candidates contribute nothing
+      const bool active = rvalid && nreal > 0;
+      uint32_t T = 0;
+      int need = 1 << 30;
+      const bool all = a.Kgr >= a.Kc * M || nreal <= a.Kgr;
+      if (active && !all) {
+        for (int bit = 15; bit >= 0; --bit) {
+          const uint32_t cand = T | (1u << bit);
+          int cnt = 0;
 #pragma unroll
-            for (int j = 0; j < 128; ++j) cnt += r[j] >= cand;
-            if (cnt >= a.Kgr) T = cand;
-          }
-          int gt = 0;
-#pragma unroll
-          for (int j = 0; j < 128; ++j) gt += r[j] > T;
-          need = a.Kgr - gt;
+          for (int j = 0; j < KT; ++j) cnt += r[j] >= cand;
+          if (cnt >= a.Kgr) T = cand;
         }
+        int gt = 0;
 #pragma unroll
-        for (int j = 0; j < 128; ++j) {
-          bool req = false;
-          if (r[j] != 0u) {
-            if (all || r[j] > T) req = true;
-            else if (r[j] == T && need > 0) { req = true; --need; }
-          }
-          if (req) {
-            atomicMin(&ms->gt0[hs][j], (uint32_t)t);
-            atomicMax(&ms->gpool[hs][j], r[j]);
-          }
+        for (int j = 0; j < KT; ++j) gt += r[j] > T;
+        need = a.Kgr - gt;
+      }
+#pragma unroll
+      for (int j = 0; j < KT; ++j) {
+        bool req = false;
+        if (active && r[j] != 0u) {
+          if (all || r[j] > T) req = true;
+          else if (r[j] == T && need > 0) { req = true; --need; }
+        }
+        // warp-level min/max first: one smem atomic per group per warp
+        const uint32_t tmin = __reduce_min_sync(0xffffffffu, req ? (uint32_t)t : 0xffffffffu);
+        const uint32_t kmax = __reduce_max_sync(0xffffffffu, req ? r[j] : 0u);
+        if (lane == (j & 31) && kmax != 0u) {
+          atomicMin(&ms->gt0[hs][j], tmin);
+          atomicMax(&ms->gpool[hs][j], kmax);
         }
       }
     }
