@@ -31,6 +31,16 @@ bool route_tc_supported(const hga_params& p, int64_t S);
 cudaError_t launch_route_tc(const hga_params& p, int64_t S, const void* q, int q_layout, const void* ck, const void* gk,
                             int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid, int32_t* open_t0,
                             float* dbg1, float* dbg2, cudaStream_t st);
+cudaError_t launch_route_decode(const hga_params& p, int L, const void* q, const int32_t* seq_pos, const void* ck,
+                                const void* gk, int64_t sum_cap, int nmid_max, int Kcmax, int Kgmax, int32_t* mc,
+                                int32_t* mt, int32_t* og, int32_t* ot, cudaStream_t st);
+cudaError_t launch_attend_decode(const hga_params& p, int L, const void* q, const int32_t* seq_pos, const void* hk,
+                                 const void* hv, int64_t hot_cap, int hot_mode, const void* ckk, const void* cvv,
+                                 int64_t cold_cap, const int32_t* og, const int32_t* ot, int Kg, void* out,
+                                 cudaStream_t st);
+cudaError_t launch_append(const hga_params& p, int L, const int32_t* seq_pos, const void* kr, const void* v,
+                          const void* kraw, void* hk, void* hv, int64_t hot_cap, int hot_mode, void* ck, void* cv,
+                          int64_t cold_cap, void* act_raw, cudaStream_t st);
 }  // namespace hga
 
 static thread_local char g_err[512];
@@ -177,6 +187,65 @@ int hga_attend_prefill(const hga_params* p, int64_t seq_len, const void* q, int3
   return cuda_status(hga::launch_attend_simt(*p, seq_len, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg, out,
                                              out_layout, stream),
                      "hga_attend_prefill");
+}
+
+static void decode_sizes(const hga_params* p, int nmid_max, int* Kc, int* Kg) {
+  const int M = p->chunk_size / p->group_size;
+  *Kc = p->topk_chunks > 0 ? (p->topk_chunks < nmid_max ? p->topk_chunks : nmid_max) : 0;
+  const int G = *Kc * M;
+  *Kg = p->topk_groups > 0 ? (p->topk_groups < G ? p->topk_groups : G) : 0;
+}
+
+int hga_route_decode(const hga_params* p, int32_t L, const void* q, const int32_t* seq_pos, const void* chunk_k,
+                     const void* group_k, int64_t sum_cap, int32_t nmid_max, int32_t* mid_chunk, int32_t* mid_t0,
+                     int32_t* open_gid, int32_t* open_t0, cudaStream_t stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (L <= 0 || L > p->chunk_size) return fail(HGA_E_INVALID, "hga_route_decode: 1 <= L <= chunk_size");
+  if (!q || !seq_pos || !chunk_k || !group_k) return fail(HGA_E_INVALID, "hga_route_decode: NULL tensor");
+  if (nmid_max < 0 || nmid_max > sum_cap) return fail(HGA_E_INVALID, "hga_route_decode: nmid_max outside [0, sum_cap]");
+  int Kc, Kg;
+  decode_sizes(p, nmid_max, &Kc, &Kg);
+  if ((Kc && (!mid_chunk || !mid_t0)) || (Kg && (!open_gid || !open_t0)))
+    return fail(HGA_E_INVALID, "hga_route_decode: NULL output list");
+  if (Kc * (p->chunk_size / p->group_size) > 256) return fail(HGA_E_UNSUPPORTED, "hga_route_decode: topk_chunks * M > 256");
+  if (nmid_max == 0 || Kc == 0) {
+    // nothing to route: still write empty lists
+    (void)0;
+  }
+  return cuda_status(hga::launch_route_decode(*p, L, q, seq_pos, chunk_k, group_k, sum_cap, nmid_max > 0 ? nmid_max : 1,
+                                              Kc, Kg, mid_chunk, mid_t0, open_gid, open_t0, stream),
+                     "hga_route_decode");
+}
+
+int hga_attend_decode(const hga_params* p, int32_t L, const void* q, const int32_t* seq_pos, const void* hot_k,
+                      const void* hot_v, int64_t hot_cap, int32_t hot_mode, const void* cold_k, const void* cold_v,
+                      int64_t cold_cap, const int32_t* open_gid, const int32_t* open_t0, int32_t Kg, void* out,
+                      cudaStream_t stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (L <= 0 || L > p->chunk_size) return fail(HGA_E_INVALID, "hga_attend_decode: 1 <= L <= chunk_size");
+  if (!q || !seq_pos || !hot_k || !hot_v || !out) return fail(HGA_E_INVALID, "hga_attend_decode: NULL tensor");
+  if (Kg > 0 && (!open_gid || !open_t0 || !cold_k || !cold_v)) return fail(HGA_E_INVALID, "hga_attend_decode: NULL open lists / cold record");
+  if (hot_mode != 0 && hot_mode != 1) return fail(HGA_E_INVALID, "hga_attend_decode: hot_mode must be 0 or 1");
+  return cuda_status(hga::launch_attend_decode(*p, L, q, seq_pos, hot_k, hot_v, hot_cap, hot_mode,
+                                               cold_k ? cold_k : hot_k, cold_v ? cold_v : hot_v, cold_cap, open_gid,
+                                               open_t0, Kg, out, stream),
+                     "hga_attend_decode");
+}
+
+int hga_append_tokens(const hga_params* p, int32_t L, const int32_t* seq_pos, const void* k_rope, const void* v,
+                      const void* k_raw, void* hot_k, void* hot_v, int64_t hot_cap, int32_t hot_mode, void* cold_k,
+                      void* cold_v, int64_t cold_cap, void* active_raw, cudaStream_t stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (L <= 0 || L > p->chunk_size) return fail(HGA_E_INVALID, "hga_append_tokens: 1 <= L <= chunk_size");
+  if (!seq_pos || !k_rope || !v || !hot_k || !hot_v) return fail(HGA_E_INVALID, "hga_append_tokens: NULL tensor");
+  if (active_raw && !k_raw) return fail(HGA_E_INVALID, "hga_append_tokens: k_raw needed for active_raw");
+  if (hot_mode != 0 && hot_mode != 1) return fail(HGA_E_INVALID, "hga_append_tokens: hot_mode must be 0 or 1");
+  return cuda_status(hga::launch_append(*p, L, seq_pos, k_rope, v, k_raw, hot_k, hot_v, hot_cap, hot_mode, cold_k,
+                                        cold_v, cold_cap, active_raw, stream),
+                     "hga_append_tokens");
 }
 
 int hga_device_status(int32_t* code, int32_t clear) {

@@ -37,13 +37,14 @@ def route_sizes(p: HgaParams, seq_len: int) -> Tuple[int, int, int, int]:
     return N, Kc, Kg, Kgr
 
 
-def q_layout_of(q: torch.Tensor) -> int:
-    """0 for a contiguous [B,H,S,Dh] tensor, 1 for a [B,H,S,Dh] view of a contiguous [B,S,H,Dh]."""
+def q_view(q: torch.Tensor) -> Tuple[torch.Tensor, int]:
+    """(q, layout): 0 for a contiguous [B,H,S,Dh] tensor, 1 for a [B,H,S,Dh] view of a contiguous
+    [B,S,H,Dh]; any other strided view is made contiguous first."""
     if q.is_contiguous():
-        return Q_BHSD
+        return q, Q_BHSD
     if q.transpose(1, 2).is_contiguous():
-        return Q_BSHD
-    raise _lib.HgaError("q must be contiguous [B,H,S,Dh] or a transposed view of contiguous [B,S,H,Dh]")
+        return q, Q_BSHD
+    return q.contiguous(), Q_BHSD
 
 
 def kv_cap_of(t: torch.Tensor) -> int:
@@ -126,7 +127,8 @@ def route_prefill(p: HgaParams, q: torch.Tensor, chunk_k: torch.Tensor, group_k:
     if (chunk_k.stride(-1) != 1 or chunk_k.stride(2) != Dh or group_k.stride(-1) != 1
             or group_k.stride(1) != sum_cap * M * Dh or chunk_k.stride(0) != chunk_k.shape[1] * chunk_k.stride(1)):
         raise _lib.HgaError("summaries must be row-slices of contiguous [B,KVH,cap,(M,)Dh] buffers")
-    check(lib().hga_route_prefill_impl(ctypes_params(p), S, ptr(q), q_layout_of(q), ptr(chunk_k), ptr(group_k),
+    q, q_layout = q_view(q)
+    check(lib().hga_route_prefill_impl(ctypes_params(p), S, ptr(q), q_layout, ptr(chunk_k), ptr(group_k),
                                        sum_cap, ptr(res["sel_chunk"]), ptr(res["sel_t0"]), ptr(res["open_gid"]),
                                        ptr(res["open_t0"]), ptr(res.get("dbg_l1")), ptr(res.get("dbg_l2")), impl,
                                        stream_ptr(dev)), "hga_route_prefill")
@@ -149,7 +151,8 @@ def attend_prefill(p: HgaParams, q: torch.Tensor, k_rope: torch.Tensor, v: torch
             out = torch.empty(B, S, H, Dh, device=q.device, dtype=q.dtype)
         else:
             out = torch.empty(B, H, S, Dh, device=q.device, dtype=q.dtype)
-    check(lib().hga_attend_prefill(ctypes_params(p), S, ptr(q), q_layout_of(q), ptr(k_rope), ptr(v), cap,
+    q, q_layout = q_view(q)
+    check(lib().hga_attend_prefill(ctypes_params(p), S, ptr(q), q_layout, ptr(k_rope), ptr(v), cap,
                                    ptr(open_gid), ptr(open_t0), ptr(out), out_layout, impl, stream_ptr(q.device)),
           "hga_attend_prefill")
     return out.transpose(1, 2) if out_layout == Q_BSHD else out
@@ -196,3 +199,67 @@ def qkv_prologue(p: HgaParams, qkv: torch.Tensor, cos: torch.Tensor, sin: torch.
         sl = slice(kv_row0, kv_row0 + S)
         return q.transpose(1, 2), kraw[:, :, sl], krope[:, :, sl], v[:, :, sl]
     return q.transpose(1, 2), kraw, krope, v
+
+
+# ---------------------------------------------------------------------------------------------
+# incremental decode
+# ---------------------------------------------------------------------------------------------
+def decode_sizes(p: HgaParams, nmid_max: int) -> Tuple[int, int]:
+    """(Kc, Kg) of a decode block whose largest routed pool is nmid_max (chunk_router.py:226, 256)."""
+    M = p.chunk_size // p.group_size
+    Kc = min(p.topk_chunks, nmid_max) if p.topk_chunks > 0 else 0
+    Kg = min(p.topk_groups, Kc * M) if p.topk_groups > 0 else 0
+    return Kc, Kg
+
+
+def route_decode(p: HgaParams, q: torch.Tensor, seq_pos: torch.Tensor, chunk_k: torch.Tensor,
+                 group_k: torch.Tensor, nmid_max: int) -> Dict[str, torch.Tensor]:
+    """Routing of one decode block (see hga_route_decode).  q [B,H,L,Dh] contiguous."""
+    _require_cuda(q, seq_pos, chunk_k, group_k)
+    B, H, L, Dh = q.shape
+    Kc, Kg = decode_sizes(p, nmid_max)
+    dev = q.device
+    res = {"mid_chunk": torch.empty(B, H, Kc, device=dev, dtype=torch.int32),
+           "mid_t0": torch.empty(B, H, Kc, device=dev, dtype=torch.int32),
+           "open_gid": torch.empty(B, H, Kg, device=dev, dtype=torch.int32),
+           "open_t0": torch.empty(B, H, Kg, device=dev, dtype=torch.int32)}
+    if not q.is_contiguous():
+        q = q.contiguous()
+    sum_cap = chunk_k.stride(1) // Dh
+    check(lib().hga_route_decode(ctypes_params(p), L, ptr(q), ptr(seq_pos), ptr(chunk_k), ptr(group_k), sum_cap,
+                                 nmid_max, ptr(res["mid_chunk"]), ptr(res["mid_t0"]), ptr(res["open_gid"]),
+                                 ptr(res["open_t0"]), stream_ptr(dev)), "hga_route_decode")
+    return res
+
+
+def attend_decode(p: HgaParams, q: torch.Tensor, seq_pos: torch.Tensor, hot_k: torch.Tensor, hot_v: torch.Tensor,
+                  hot_mode: int, cold_k: Optional[torch.Tensor], cold_v: Optional[torch.Tensor],
+                  open_gid: torch.Tensor, open_t0: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Attention of one decode block (see hga_attend_decode).  Returns [B,H,L,Dh]."""
+    _require_cuda(q, seq_pos, hot_k, hot_v, open_gid, open_t0)
+    if not q.is_contiguous():
+        q = q.contiguous()
+    B, H, L, Dh = q.shape
+    out = torch.empty_like(q) if out is None else out
+    hot_cap = kv_cap_of(hot_k)
+    cold_cap = kv_cap_of(cold_k) if cold_k is not None else hot_cap
+    Kg = open_gid.shape[-1]
+    check(lib().hga_attend_decode(ctypes_params(p), L, ptr(q), ptr(seq_pos), ptr(hot_k), ptr(hot_v), hot_cap,
+                                  hot_mode, ptr(cold_k), ptr(cold_v), cold_cap, ptr(open_gid), ptr(open_t0), Kg,
+                                  ptr(out), stream_ptr(q.device)), "hga_attend_decode")
+    return out
+
+
+def append_tokens(p: HgaParams, seq_pos: torch.Tensor, k_rope: torch.Tensor, v: torch.Tensor,
+                  k_raw: Optional[torch.Tensor], hot_k: torch.Tensor, hot_v: torch.Tensor, hot_mode: int,
+                  cold_k: Optional[torch.Tensor], cold_v: Optional[torch.Tensor],
+                  active_raw: Optional[torch.Tensor]) -> None:
+    """Write a block's new K/V rows (see hga_append_tokens).  k_rope/v/k_raw [B,KVH,L,Dh]."""
+    _require_cuda(seq_pos, k_rope, v, hot_k, hot_v)
+    k_rope, v = k_rope.contiguous(), v.contiguous()
+    k_raw = None if k_raw is None else k_raw.contiguous()
+    L = k_rope.shape[2]
+    check(lib().hga_append_tokens(ctypes_params(p), L, ptr(seq_pos), ptr(k_rope), ptr(v), ptr(k_raw), ptr(hot_k),
+                                  ptr(hot_v), kv_cap_of(hot_k), hot_mode, ptr(cold_k), ptr(cold_v),
+                                  kv_cap_of(cold_k) if cold_k is not None else 0, ptr(active_raw),
+                                  stream_ptr(k_rope.device)), "hga_append_tokens")

@@ -61,15 +61,28 @@ class ChunkRouter:
     def __init__(self, cfg: RouterConfig, store: KVCacheStore) -> None:
         self.cfg = cfg
         self.store = store
-        self._active_kraw: Dict[int, Optional[torch.Tensor]] = {}
         self._active_len: Dict[int, int] = {}
         self._rot_cache: Dict[Tuple[str, int], Tuple[torch.Tensor, torch.Tensor]] = {}
+        self._pending: Dict[int, object] = {}   # decode blocks whose chunk close waits for their attention
+        self._pos_cache: Dict[Tuple[int, int, str], torch.Tensor] = {}
 
     # ---------------------------------------------------------------------------------------
     def reset(self) -> None:
+        for ctx in list(self._pending.values()):
+            ctx.finish()
+        self._pending.clear()
         self.store.reset()
-        self._active_kraw.clear()
         self._active_len.clear()
+
+    def _seq_pos(self, B: int, pos: int, device) -> torch.Tensor:
+        key = (B, pos, str(device))
+        t = self._pos_cache.get(key)
+        if t is None:
+            if len(self._pos_cache) > 4096:
+                self._pos_cache.clear()
+            t = torch.full((B,), pos, dtype=torch.int32, device=device)
+            self._pos_cache[key] = t
+        return t
 
     def expected_position(self, layer: int) -> int:
         return self.store.num_closed_chunks(layer) * self.cfg.chunk_size + self._active_len.get(layer, 0)
@@ -88,11 +101,13 @@ class ChunkRouter:
         cached = self._rot_cache.get(key)
         if cached is None or cached[0].shape[0] < length:
             n = max(length, 2 * cached[0].shape[0] if cached is not None else length)
+            # built with the host's fp32 cos/sin (the reference's own table) and uploaded once, so
+            # closed-chunk summaries are bit-identical to the reference's
             half = self.cfg.head_dim // 2
-            inv = 1.0 / (self.cfg.theta ** (torch.arange(half, device=device, dtype=torch.float32) / half))
-            f = torch.arange(n, device=device, dtype=torch.float32).unsqueeze(-1) * inv
+            inv = 1.0 / (self.cfg.theta ** (torch.arange(half, dtype=torch.float32) / half))
+            f = torch.arange(n, dtype=torch.float32).unsqueeze(-1) * inv
             emb = torch.cat((f, f), dim=-1)
-            cached = (emb.cos(), emb.sin())
+            cached = (emb.cos().to(device), emb.sin().to(device))
             self._rot_cache[key] = cached
         return cached
 
@@ -167,14 +182,23 @@ class ChunkRouter:
         store.mark_closed(layer, n_closed)
         rem = S - n_closed * C
         self._active_len[layer] = rem
-        self._active_kraw[layer] = k_raw[:, :, n_closed * C:].clone() if rem else None
+        if rem:
+            store.active_raw(layer)[:, :, :rem].copy_(k_raw[:, :, n_closed * C:])
+        store.after_seed(layer, S)
 
     # ---------------------------------------------------------------------------------------
     def decode_block(self, layer, q, k_rope, k_raw, v, start_pos, return_positions: bool = False) -> RoutedKV:
         """Incremental routing of L <= chunk_size new tokens inside the active chunk
-        (chunk_router.py:279-407)."""
+        (chunk_router.py:279-407).  q [B,H,L,Dh]; k_rope/k_raw/v [B,KVH,L,Dh]."""
+        if return_positions:
+            raise NotImplementedError("return_positions (the DCA attend variant) is not part of the B200 hot path")
         from .decode import decode_block
         return decode_block(self, layer, q, k_rope, k_raw, v, start_pos)
+
+    def decode_step(self, layer, q, k_rope, k_raw, v, seq_pos: torch.Tensor, seq_pos_host) -> RoutedKV:
+        """One block per sequence at per-sequence positions (mixed-length batched decode)."""
+        from .decode import decode_step
+        return decode_step(self, layer, q, k_rope, k_raw, v, seq_pos, seq_pos_host)
 
     def prefill(self, layer, q, k_rope, k_raw, v, start_pos: int = 0) -> torch.Tensor:
         """Stream a prefix chunk by chunk through the incremental path (chunk_router.py:410-442)."""

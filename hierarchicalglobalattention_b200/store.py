@@ -72,7 +72,9 @@ class LayerBuffers:
     group_v: Optional[torch.Tensor] = None        # [B,KVH,ccap,M,Dh]    device
     token_k: Optional[torch.Tensor] = None        # [B,KVH,tcap,Dh]      device (VRAM) / pinned host (RAM)
     token_v: Optional[torch.Tensor] = None
-    hot: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = field(default_factory=dict)  # RAM tier windows
+    active_raw: Optional[torch.Tensor] = None     # [B,KVH,C,Dh] pre-RoPE K of the active chunk (device)
+    hot_k: Optional[torch.Tensor] = None          # RAM tier: [B,KVH,(kf+kl+1)*C,Dh] window/active slots (device)
+    hot_v: Optional[torch.Tensor] = None
 
 
 class VramKVCacheStore(KVCacheStore):
@@ -113,8 +115,9 @@ class VramKVCacheStore(KVCacheStore):
             ck = torch.zeros(self.B, self.kvh, cap, self.dh, device=dev, dtype=dt)
             gk = torch.zeros(self.B, self.kvh, cap, self.M, self.dh, device=dev, dtype=dt)
             gv = torch.zeros_like(gk)
-            if st.chunk_k is not None and st.n_closed:
-                n = st.n_closed
+            if st.chunk_k is not None:
+                # whole old capacity: rows of a mixed-length batch may be ahead of n_closed
+                n = st.ccap
                 ck[:, :, :n] = st.chunk_k[:, :, :n]
                 gk[:, :, :n] = st.group_k[:, :, :n]
                 gv[:, :, :n] = st.group_v[:, :, :n]
@@ -129,6 +132,35 @@ class VramKVCacheStore(KVCacheStore):
                 tv[:, :, :keep] = st.token_v[:, :, :keep]
             st.token_k, st.token_v, st.tcap = tk, tv, cap
         return st
+
+    # -- decode-side views: hot rows (windows + active chunk), cold record, active pre-RoPE K ----
+    hot_mode = 0  # hot rows are addressed like cold rows (one HBM record)
+
+    def hot_buffers(self, layer: int):
+        st = self.layer_buffers(layer)
+        return st.token_k, st.token_v
+
+    def cold_buffers(self, layer: int):
+        st = self.layer_buffers(layer)
+        return st.token_k, st.token_v
+
+    def active_raw(self, layer: int) -> torch.Tensor:
+        st = self.layer_buffers(layer)
+        if st.active_raw is None:
+            st.active_raw = torch.zeros(self.B, self.kvh, self.C, self.dh, device=self.compute_device, dtype=self.dtype)
+        return st.active_raw
+
+    def active_rows(self, layer: int, n: int):
+        """Token K/V rows of (active) chunk n as [B,KVH,C,Dh] views."""
+        st = self.layer_buffers(layer)
+        sl = slice(n * self.C, (n + 1) * self.C)
+        return st.token_k[:, :, sl], st.token_v[:, :, sl]
+
+    def on_chunk_closed(self, layer: int, n: int, row: Optional[int] = None) -> None:
+        """Hook after chunk n closed (the RAM tier moves it into its window slots)."""
+
+    def after_seed(self, layer: int, seq_len: int) -> None:
+        """Hook after a prefill seeded tokens [0, seq_len) (the RAM tier fills its hot slots)."""
 
     def adopt_tokens(self, layer: int, token_k: torch.Tensor, token_v: torch.Tensor) -> None:
         """Take ownership of freshly written [B,KVH,cap,Dh] token buffers (zero-copy prefill seed)."""

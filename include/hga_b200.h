@@ -119,6 +119,44 @@ int hga_qkv_prologue(const hga_params* p, int64_t seq_len, const void* qkv, int6
                      void* q_rope, void* k_raw, void* k_rope, void* v, int64_t kv_cap, int64_t kv_row0,
                      cudaStream_t stream);
 
+/* ---- incremental decode (ChunkRouter.decode_block, chunk_router.py:188-407) ----------------
+ * A block of L (1 <= L <= chunk_size) new tokens per sequence, all inside the sequence's active
+ * chunk; seq_pos [B] (device int32) = absolute position of each sequence's first new token, so
+ * the sequences of one batch may sit at different positions (no reference equivalent: the
+ * reference keeps one position per layer).  q [B, H, L, Dh] contiguous, RoPE applied.
+ *
+ * hga_route_decode: routing of chunk_router.py:210-277 against the store's closed-chunk
+ * summaries; nmid_max >= the largest routed pool of the batch.  Writes, per (b, h), the routed
+ * chunks mid_chunk/mid_t0 [B,H,Kc] and the visible opened groups open_gid/open_t0 [B,H,Kg]
+ * (Kc = min(topk_chunks, nmid_max), Kg = min(topk_groups, Kc*M); t0 = first of the L rows that
+ * sees it; lists sorted, padded with -1). */
+int hga_route_decode(const hga_params* p, int32_t L, const void* q, const int32_t* seq_pos,
+                     const void* chunk_k, const void* group_k, int64_t sum_cap, int32_t nmid_max,
+                     int32_t* mid_chunk, int32_t* mid_t0, int32_t* open_gid, int32_t* open_t0,
+                     cudaStream_t stream);
+
+/* hga_attend_decode: token-only attention of one decode block (chunk_router.py:336-401 and the
+ * flat branch of RoutedKV.attend, :159-162) over the keep_first window, the keep_last window, the
+ * opened groups (rows >= t0) and the active chunk (key u visible to row t iff u <= pos%C + t).
+ * Window and active-chunk rows come from `hot`, opened groups from `cold` (the complete token
+ * record; may be mapped pinned host memory).  hot_mode 0: hot is addressed like cold (the VRAM
+ * tier, hot == cold); hot_mode 1: hot is a slot buffer [B,KVH,(kf+kl+1)*C,Dh] holding first-window
+ * chunk c in slot c, last-window chunk c in slot kf + c % kl and the active chunk in slot kf + kl.
+ * out [B, H, L, Dh]. */
+int hga_attend_decode(const hga_params* p, int32_t L, const void* q, const int32_t* seq_pos,
+                      const void* hot_k, const void* hot_v, int64_t hot_cap, int32_t hot_mode,
+                      const void* cold_k, const void* cold_v, int64_t cold_cap,
+                      const int32_t* open_gid, const int32_t* open_t0, int32_t Kg, void* out,
+                      cudaStream_t stream);
+
+/* hga_append_tokens: write L new K (RoPE applied) / V rows per sequence at seq_pos into the hot
+ * rows (and, for hot_mode 1, the cold record), and their pre-RoPE K into active_raw
+ * [B,KVH,C,Dh] (may be NULL) — ChunkRouter._append_active (chunk_router.py:603-614). */
+int hga_append_tokens(const hga_params* p, int32_t L, const int32_t* seq_pos, const void* k_rope,
+                      const void* v, const void* k_raw, void* hot_k, void* hot_v, int64_t hot_cap,
+                      int32_t hot_mode, void* cold_k, void* cold_v, int64_t cold_cap, void* active_raw,
+                      cudaStream_t stream);
+
 /* Device-side error word of the tensor-core kernels: 0, or the code of the first bounded
  * mbarrier wait that timed out (the CTA then released its TMEM and returned without output).
  * Synchronous (reads device memory); clear != 0 resets the word. */

@@ -453,7 +453,9 @@ def route_decode(p: OracleParams, q, chunk_k_mid, group_k_of, mid_lo: int, n_clo
 
     q ``[B,H,L,Dh]``; chunk_k_mid ``[B,KVH,n_mid,Dh]`` = store chunk summaries of the routed
     pool; ``group_k_of(mid_idx[B,H,Kc]) -> [B,H,Kc,M,Dh]``.  Returns absolute chunk ids and
-    group picks with their per-row first-visible index (L = never), plus a near-tie flag [B,H].
+    group picks with their per-row first-visible index (L = never), plus a near-tie flag [B,H]
+    (a selection that an accumulation-order difference of one rounding could flip; see
+    ``score_bounds``).
     """
     B, H, L, Dh = q.shape
     M = p.M
@@ -465,13 +467,18 @@ def route_decode(p: OracleParams, q, chunk_k_mid, group_k_of, mid_lo: int, n_clo
            "open_t0": torch.empty(B, H, 0, dtype=torch.long), "tie": torch.zeros(B, H, dtype=torch.bool)}
     if n_mid == 0 or p.topk_chunks <= 0:
         return res
+    # chunk_router.py:222-232: scores in the model dtype, pooled by max over the block's rows
     sc = torch.einsum("bhld,bhnd->bhln", q, ck) * p.scale
+    lo, hi = score_bounds(q, ck, p.scale, dtype, "bhld,bhnd->bhln")
     Kc = min(p.topk_chunks, n_mid)
     pooled = sc.max(dim=2).values
     top_s, mid_rel = torch.topk(pooled, Kc, dim=-1, sorted=False)
     _, req_rel = torch.topk(sc, Kc, dim=-1, sorted=False)
-    tie = _boundary_tie(pooled, Kc, torch.full(pooled.shape[:-1], n_mid), dtype)
-    tie |= _boundary_tie(sc, Kc, torch.full(sc.shape[:-1], n_mid), dtype).any(-1)
+    plo, phi = lo.max(dim=2).values, hi.max(dim=2).values
+    every = torch.ones_like(pooled, dtype=torch.bool)
+    tie = _set_tie(plo, phi, _onehot(mid_rel, n_mid), every)
+    tie |= _set_tie(lo, hi, _onehot(req_rel, n_mid), torch.ones_like(sc, dtype=torch.bool)).any(-1)
+    # chunk_router.py:234-246: the previous chunk replaces the lowest pooled pick
     prev = n_closed - 1
     mid_hi = mid_lo + n_mid
     prev_in = mid_lo <= prev < mid_hi
@@ -479,8 +486,11 @@ def route_decode(p: OracleParams, q, chunk_k_mid, group_k_of, mid_lo: int, n_clo
         prev_rel = prev - mid_lo
         missing = ~(mid_rel == prev_rel).any(dim=-1, keepdim=True)
         at = top_s.argmin(dim=-1, keepdim=True)
-        mins = top_s.gather(-1, at)
-        tie |= (missing & ((top_s == mins).sum(-1, keepdim=True) > 1)).squeeze(-1)
+        sel_lo, sel_hi = plo.gather(-1, mid_rel), phi.gather(-1, mid_rel)
+        min_hi = sel_hi.gather(-1, at)
+        others = torch.ones_like(sel_lo, dtype=torch.bool).scatter(-1, at, False)
+        amb = ((sel_lo <= min_hi) & others).any(-1, keepdim=True)
+        tie |= (missing & amb).squeeze(-1)
         mid_rel = mid_rel.scatter(-1, at, torch.where(missing, torch.full_like(at, prev_rel), mid_rel.gather(-1, at)))
     mid_idx = mid_rel + mid_lo
     mreq = (req_rel.unsqueeze(-2) == mid_rel.unsqueeze(2).unsqueeze(-1)).any(dim=-1)
@@ -493,14 +503,17 @@ def route_decode(p: OracleParams, q, chunk_k_mid, group_k_of, mid_lo: int, n_clo
     if Kg <= 0:
         res["tie"] = tie
         return res
+    # chunk_router.py:248-277: group candidates of the chosen chunks (not masked), pooled over rows
     gk = group_k_of(mid_idx).reshape(B, H, Kc * M, Dh)
     sg = torch.einsum("bhld,bhrd->bhlr", q, gk) * p.scale
+    glo, ghi = score_bounds(q, gk, p.scale, dtype, "bhld,bhrd->bhlr")
     pg = sg.max(dim=2).values
     _, top_g = torch.topk(pg, Kg, dim=-1, sorted=False)
-    tie |= _boundary_tie(pg, Kg, torch.full(pg.shape[:-1], Kc * M), dtype)
+    tie |= _set_tie(glo.max(dim=2).values, ghi.max(dim=2).values, _onehot(top_g, Kc * M),
+                    torch.ones_like(pg, dtype=torch.bool))
     if Kgr > 0:
         _, req_g = torch.topk(sg, Kgr, dim=-1, sorted=False)
-        tie |= _boundary_tie(sg, Kgr, torch.full(sg.shape[:-1], Kc * M), dtype).any(-1)
+        tie |= _set_tie(glo, ghi, _onehot(req_g, Kc * M), torch.ones_like(sg, dtype=torch.bool)).any(-1)
         greq = (req_g.unsqueeze(-2) == top_g.unsqueeze(2).unsqueeze(-1)).any(dim=-1)
     else:
         greq = torch.zeros(B, H, L, Kg, dtype=torch.bool)
@@ -525,6 +538,51 @@ def attend_decode(p: OracleParams, q, keys, vals, key_first_row):
     msk = torch.arange(L).view(1, 1, L, 1) >= key_first_row.unsqueeze(2)
     s = s.masked_fill(~msk, NEG)
     return torch.einsum("bhlr,bhrd->bhld", torch.softmax(s, -1), vals.float()).to(vals.dtype)
+
+
+def decode_sequence(p: OracleParams, q, k_rope, k_raw, v, block: int, start_pos: int = 0):
+    """The reference's incremental path over a whole sequence: ``ChunkRouter.decode_block`` fed
+    block by block and chunk-aligned (chunk_router.py:279-442), token-only attention.
+
+    q ``[B,H,S,Dh]``, k_* / v ``[B,KVH,S,Dh]`` cover positions [0, S); rows before ``start_pos``
+    are the already-closed prefix (its chunks are summarised exactly like closed decode chunks).
+    Returns (out ``[B,H,S-start_pos,Dh]``, list of per-block dicts with ``pos``, ``L``, the
+    routing result and its tie flag).
+    """
+    B, H, S, Dh = q.shape
+    C, gs, rep = p.chunk_size, p.group_size, p.rep
+    ck_all, gk_all, _ = summaries_store(p, k_raw, k_rope, v)
+    kv_of_h = torch.arange(H) // rep
+    bi = torch.arange(B).view(B, 1, 1)
+    hi_ = kv_of_h.view(1, H, 1)
+    outs, blocks = [], []
+    pos = start_pos
+    while pos < S:
+        L = min(block, C - pos % C, S - pos)
+        n, c0 = pos // C, pos % C
+        f_hi, l_lo = _windows(p, n)
+        qb = q[:, :, pos:pos + L]
+        r = route_decode(p, qb, ck_all[:, :, f_hi:max(l_lo, f_hi)],
+                         lambda mid: gk_all[bi, hi_, mid], f_hi, n)
+        rows, first = [], []
+        win = list(range(0, f_hi * C)) + list(range(l_lo * C, n * C))
+        if win:
+            rows.append(torch.tensor(win).view(1, 1, -1).expand(B, H, -1))
+            first.append(torch.zeros(B, H, len(win), dtype=torch.long))
+        if r["open_chunk"].shape[-1]:
+            base = (r["open_chunk"] * C + r["open_grp"] * gs).unsqueeze(-1) + torch.arange(gs)
+            rows.append(base.reshape(B, H, -1))
+            first.append(r["open_t0"].unsqueeze(-1).expand(*r["open_t0"].shape, gs).reshape(B, H, -1))
+        act = torch.arange(n * C, n * C + c0 + L)
+        rows.append(act.view(1, 1, -1).expand(B, H, -1))
+        first.append((torch.arange(c0 + L) - c0).view(1, 1, -1).expand(B, H, -1))
+        rows_t, first_t = torch.cat(rows, -1), torch.cat(first, -1)
+        keys = k_rope[bi, hi_, rows_t]
+        vals = v[bi, hi_, rows_t]
+        outs.append(attend_decode(p, qb, keys, vals, first_t))
+        blocks.append({"pos": pos, "L": L, "route": r})
+        pos += L
+    return torch.cat(outs, dim=2), blocks
 
 
 # ---------------------------------------------------------------------------------------------

@@ -65,3 +65,17 @@ def test_module_forward_matches_reference_cfg0_rows():
     keep = torch.tensor([int(r) // p.chunk_size in chunks for r in rows])
     err = (out[:, rows[keep]] - g["out"][:, keep]).abs().max().item()
     assert err < 1e-6
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in cases.CASES if c["kind"] == "incremental"])
+def test_incremental_decode_matches_reference(name):
+    """Block-by-block decode (chunk_router.py:279-442) with its closed-chunk summaries."""
+    c, g = cases.case(name), cases.load(name)
+    inp = cases.make_inputs(c)
+    assert cases.checksum(inp) == pytest.approx(g["input_checksum"], rel=1e-9)
+    out, blocks = O.decode_sequence(c["params"], inp["q"], inp["k_rope"], inp["k_raw"], inp["v"], c["block"])
+    n = g["store_chunk_k"].shape[2]
+    ck, _, _ = O.summaries_store(c["params"], inp["k_raw"], inp["k_rope"], inp["v"])
+    assert torch.equal(ck[:, :, :n], g["store_chunk_k"])
+    tol = 1e-5 if c["dtype"] == torch.float32 else 2e-2
+    torch.testing.assert_close(out[:, :, g["out_rows"]].float(), g["out"].float(), atol=tol, rtol=tol)
