@@ -53,6 +53,10 @@ _SIGNATURES = {
                                         _P]),
     "hga_attend_decode": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I32, _P, _P, _P, _P, _I64, _I32, _P, _P, _I64,
                                          _P, _P, _I32, _P, _P]),
+    "hga_route_decode_impl": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I32, _P, _P, _P, _P, _I64, _I32, _P, _P, _P,
+                                             _P, _I32, _P]),
+    "hga_attend_decode_impl": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I32, _P, _P, _P, _P, _I64, _I32, _P, _P,
+                                              _I64, _P, _P, _I32, _P, _I32, _P]),
     "hga_append_tokens": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I32, _P, _P, _P, _P, _P, _P, _I64, _I32, _P, _P,
                                          _I64, _P, _P]),
     "hga_device_status": (ctypes.c_int, [_P, _I32]),

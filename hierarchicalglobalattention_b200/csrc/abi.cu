@@ -38,6 +38,15 @@ cudaError_t launch_attend_decode(const hga_params& p, int L, const void* q, cons
                                  const void* hv, int64_t hot_cap, int hot_mode, const void* ckk, const void* cvv,
                                  int64_t cold_cap, const int32_t* og, const int32_t* ot, int Kg, void* out,
                                  cudaStream_t st);
+bool route_decode1_supported(const hga_params& p, int L);
+cudaError_t launch_route_decode1(const hga_params& p, const void* q, const int32_t* seq_pos, const void* ck,
+                                 const void* gk, int64_t sum_cap, int nmid_max, int Kcmax, int Kgmax, int32_t* mc,
+                                 int32_t* mt, int32_t* og, int32_t* ot, cudaStream_t st);
+bool attend_decode_fast_supported(const hga_params& p, int L);
+cudaError_t launch_attend_decode_fast(const hga_params& p, int L, const void* q, const int32_t* seq_pos,
+                                      const void* hk, const void* hv, int64_t hot_cap, int hot_mode, const void* ckk,
+                                      const void* cvv, int64_t cold_cap, const int32_t* og, const int32_t* ot, int Kg,
+                                      void* out, cudaStream_t st);
 cudaError_t launch_append(const hga_params& p, int L, const int32_t* seq_pos, const void* kr, const void* v,
                           const void* kraw, void* hk, void* hv, int64_t hot_cap, int hot_mode, void* ck, void* cv,
                           int64_t cold_cap, void* act_raw, cudaStream_t st);
@@ -199,20 +208,30 @@ static void decode_sizes(const hga_params* p, int nmid_max, int* Kc, int* Kg) {
 int hga_route_decode(const hga_params* p, int32_t L, const void* q, const int32_t* seq_pos, const void* chunk_k,
                      const void* group_k, int64_t sum_cap, int32_t nmid_max, int32_t* mid_chunk, int32_t* mid_t0,
                      int32_t* open_gid, int32_t* open_t0, cudaStream_t stream) {
+  return hga_route_decode_impl(p, L, q, seq_pos, chunk_k, group_k, sum_cap, nmid_max, mid_chunk, mid_t0, open_gid,
+                               open_t0, 0, stream);
+}
+
+int hga_route_decode_impl(const hga_params* p, int32_t L, const void* q, const int32_t* seq_pos, const void* chunk_k,
+                          const void* group_k, int64_t sum_cap, int32_t nmid_max, int32_t* mid_chunk, int32_t* mid_t0,
+                          int32_t* open_gid, int32_t* open_t0, int32_t impl, cudaStream_t stream) {
   int rc = check_params(p);
   if (rc) return rc;
   if (L <= 0 || L > p->chunk_size) return fail(HGA_E_INVALID, "hga_route_decode: 1 <= L <= chunk_size");
   if (!q || !seq_pos || !chunk_k || !group_k) return fail(HGA_E_INVALID, "hga_route_decode: NULL tensor");
   if (nmid_max < 0 || nmid_max > sum_cap) return fail(HGA_E_INVALID, "hga_route_decode: nmid_max outside [0, sum_cap]");
+  if (impl < 0 || impl > 2) return fail(HGA_E_INVALID, "hga_route_decode: impl must be 0, 1 or 2");
   int Kc, Kg;
   decode_sizes(p, nmid_max, &Kc, &Kg);
   if ((Kc && (!mid_chunk || !mid_t0)) || (Kg && (!open_gid || !open_t0)))
     return fail(HGA_E_INVALID, "hga_route_decode: NULL output list");
   if (Kc * (p->chunk_size / p->group_size) > 256) return fail(HGA_E_UNSUPPORTED, "hga_route_decode: topk_chunks * M > 256");
-  if (nmid_max == 0 || Kc == 0) {
-    // nothing to route: still write empty lists
-    (void)0;
-  }
+  const bool fast = hga::route_decode1_supported(*p, L);
+  if (impl == 2 && !fast) return fail(HGA_E_UNSUPPORTED, "hga_route_decode: the L = 1 kernel needs L == 1, head_dim 64 or 128");
+  if (fast && impl != 1)
+    return cuda_status(hga::launch_route_decode1(*p, q, seq_pos, chunk_k, group_k, sum_cap, nmid_max > 0 ? nmid_max : 1,
+                                                 Kc, Kg, mid_chunk, mid_t0, open_gid, open_t0, stream),
+                       "hga_route_decode");
   return cuda_status(hga::launch_route_decode(*p, L, q, seq_pos, chunk_k, group_k, sum_cap, nmid_max > 0 ? nmid_max : 1,
                                               Kc, Kg, mid_chunk, mid_t0, open_gid, open_t0, stream),
                      "hga_route_decode");
@@ -222,15 +241,32 @@ int hga_attend_decode(const hga_params* p, int32_t L, const void* q, const int32
                       const void* hot_v, int64_t hot_cap, int32_t hot_mode, const void* cold_k, const void* cold_v,
                       int64_t cold_cap, const int32_t* open_gid, const int32_t* open_t0, int32_t Kg, void* out,
                       cudaStream_t stream) {
+  return hga_attend_decode_impl(p, L, q, seq_pos, hot_k, hot_v, hot_cap, hot_mode, cold_k, cold_v, cold_cap, open_gid,
+                                open_t0, Kg, out, 0, stream);
+}
+
+int hga_attend_decode_impl(const hga_params* p, int32_t L, const void* q, const int32_t* seq_pos, const void* hot_k,
+                           const void* hot_v, int64_t hot_cap, int32_t hot_mode, const void* cold_k, const void* cold_v,
+                           int64_t cold_cap, const int32_t* open_gid, const int32_t* open_t0, int32_t Kg, void* out,
+                           int32_t impl, cudaStream_t stream) {
   int rc = check_params(p);
   if (rc) return rc;
   if (L <= 0 || L > p->chunk_size) return fail(HGA_E_INVALID, "hga_attend_decode: 1 <= L <= chunk_size");
   if (!q || !seq_pos || !hot_k || !hot_v || !out) return fail(HGA_E_INVALID, "hga_attend_decode: NULL tensor");
   if (Kg > 0 && (!open_gid || !open_t0 || !cold_k || !cold_v)) return fail(HGA_E_INVALID, "hga_attend_decode: NULL open lists / cold record");
   if (hot_mode != 0 && hot_mode != 1) return fail(HGA_E_INVALID, "hga_attend_decode: hot_mode must be 0 or 1");
-  return cuda_status(hga::launch_attend_decode(*p, L, q, seq_pos, hot_k, hot_v, hot_cap, hot_mode,
-                                               cold_k ? cold_k : hot_k, cold_v ? cold_v : hot_v, cold_cap, open_gid,
-                                               open_t0, Kg, out, stream),
+  if (impl < 0 || impl > 2) return fail(HGA_E_INVALID, "hga_attend_decode: impl must be 0, 1 or 2");
+  const bool fast = hga::attend_decode_fast_supported(*p, L);
+  if (impl == 2 && !fast)
+    return fail(HGA_E_UNSUPPORTED, "hga_attend_decode: the fast kernel needs bf16/fp16, group_size 16, head_dim 64/128, L <= 8");
+  const void* ck = cold_k ? cold_k : hot_k;
+  const void* cv = cold_v ? cold_v : hot_v;
+  if (fast && impl != 1)
+    return cuda_status(hga::launch_attend_decode_fast(*p, L, q, seq_pos, hot_k, hot_v, hot_cap, hot_mode, ck, cv,
+                                                      cold_cap, open_gid, open_t0, Kg, out, stream),
+                       "hga_attend_decode");
+  return cuda_status(hga::launch_attend_decode(*p, L, q, seq_pos, hot_k, hot_v, hot_cap, hot_mode, ck, cv, cold_cap,
+                                               open_gid, open_t0, Kg, out, stream),
                      "hga_attend_decode");
 }
 

@@ -213,8 +213,9 @@ def decode_sizes(p: HgaParams, nmid_max: int) -> Tuple[int, int]:
 
 
 def route_decode(p: HgaParams, q: torch.Tensor, seq_pos: torch.Tensor, chunk_k: torch.Tensor,
-                 group_k: torch.Tensor, nmid_max: int) -> Dict[str, torch.Tensor]:
-    """Routing of one decode block (see hga_route_decode).  q [B,H,L,Dh] contiguous."""
+                 group_k: torch.Tensor, nmid_max: int, impl: int = 0) -> Dict[str, torch.Tensor]:
+    """Routing of one decode block (see hga_route_decode_impl).  q [B,H,L,Dh] contiguous.
+    impl: 0 auto, 1 portable kernel, 2 single-token kernel."""
     _require_cuda(q, seq_pos, chunk_k, group_k)
     B, H, L, Dh = q.shape
     Kc, Kg = decode_sizes(p, nmid_max)
@@ -226,16 +227,19 @@ def route_decode(p: HgaParams, q: torch.Tensor, seq_pos: torch.Tensor, chunk_k: 
     if not q.is_contiguous():
         q = q.contiguous()
     sum_cap = chunk_k.stride(1) // Dh
-    check(lib().hga_route_decode(ctypes_params(p), L, ptr(q), ptr(seq_pos), ptr(chunk_k), ptr(group_k), sum_cap,
-                                 nmid_max, ptr(res["mid_chunk"]), ptr(res["mid_t0"]), ptr(res["open_gid"]),
-                                 ptr(res["open_t0"]), stream_ptr(dev)), "hga_route_decode")
+    check(lib().hga_route_decode_impl(ctypes_params(p), L, ptr(q), ptr(seq_pos), ptr(chunk_k), ptr(group_k),
+                                      sum_cap, nmid_max, ptr(res["mid_chunk"]), ptr(res["mid_t0"]),
+                                      ptr(res["open_gid"]), ptr(res["open_t0"]), impl, stream_ptr(dev)),
+          "hga_route_decode")
     return res
 
 
 def attend_decode(p: HgaParams, q: torch.Tensor, seq_pos: torch.Tensor, hot_k: torch.Tensor, hot_v: torch.Tensor,
                   hot_mode: int, cold_k: Optional[torch.Tensor], cold_v: Optional[torch.Tensor],
-                  open_gid: torch.Tensor, open_t0: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Attention of one decode block (see hga_attend_decode).  Returns [B,H,L,Dh]."""
+                  open_gid: torch.Tensor, open_t0: torch.Tensor, out: Optional[torch.Tensor] = None,
+                  impl: int = 0) -> torch.Tensor:
+    """Attention of one decode block (see hga_attend_decode_impl).  Returns [B,H,L,Dh].
+    impl: 0 auto, 1 portable kernel, 2 short-block kernel."""
     _require_cuda(q, seq_pos, hot_k, hot_v, open_gid, open_t0)
     if not q.is_contiguous():
         q = q.contiguous()
@@ -244,9 +248,9 @@ def attend_decode(p: HgaParams, q: torch.Tensor, seq_pos: torch.Tensor, hot_k: t
     hot_cap = kv_cap_of(hot_k)
     cold_cap = kv_cap_of(cold_k) if cold_k is not None else hot_cap
     Kg = open_gid.shape[-1]
-    check(lib().hga_attend_decode(ctypes_params(p), L, ptr(q), ptr(seq_pos), ptr(hot_k), ptr(hot_v), hot_cap,
-                                  hot_mode, ptr(cold_k), ptr(cold_v), cold_cap, ptr(open_gid), ptr(open_t0), Kg,
-                                  ptr(out), stream_ptr(q.device)), "hga_attend_decode")
+    check(lib().hga_attend_decode_impl(ctypes_params(p), L, ptr(q), ptr(seq_pos), ptr(hot_k), ptr(hot_v), hot_cap,
+                                       hot_mode, ptr(cold_k), ptr(cold_v), cold_cap, ptr(open_gid), ptr(open_t0), Kg,
+                                       ptr(out), impl, stream_ptr(q.device)), "hga_attend_decode")
     return out
 
 

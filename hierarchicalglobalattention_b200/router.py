@@ -166,6 +166,13 @@ class ChunkRouter:
         return RoutedKV(params=hp, seq_len=S, token_k=k_rope, token_v=v, routing=routing, scale=cfg.scale,
                         chunked=True, chunk_size=C, out=out)
 
+    def seed(self, layer: int, k_rope: torch.Tensor, k_raw: torch.Tensor, v: torch.Tensor) -> None:
+        """Load a fresh context [0, S) into the store without attending over it (the store side of
+        ``route_query_block(start_pos=0, populate_store=True)``); k_* / v [B,KVH,S,Dh]."""
+        B = k_rope.shape[0]
+        hp = self.cfg.hga_params(self.store.policy, B, k_rope.dtype)
+        self._seed_store(layer, hp, k_rope, k_raw, v, k_rope.shape[2])
+
     def _seed_store(self, layer, hp, k_rope, k_raw, v, S):
         """Store seed of a fresh prefill (chunk_router.py:553-599): summaries of the closed chunks with
         fixed anchors and fp32 rotary rows, token rows, and the partial active chunk."""

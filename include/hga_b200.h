@@ -149,6 +149,20 @@ int hga_attend_decode(const hga_params* p, int32_t L, const void* q, const int32
                       const int32_t* open_gid, const int32_t* open_t0, int32_t Kg, void* out,
                       cudaStream_t stream);
 
+/* The two decode entry points above with an explicit kernel choice: impl 0 = automatic (the
+ * fast kernels when the shape allows), 1 = the portable kernels, 2 = the fast kernels (routing:
+ * L == 1 and head_dim 64/128; attention: bf16/fp16, group_size 16, head_dim 64/128, L <= 8;
+ * HGA_E_UNSUPPORTED otherwise).  Both choices compute the same routing rules and attention. */
+int hga_route_decode_impl(const hga_params* p, int32_t L, const void* q, const int32_t* seq_pos,
+                          const void* chunk_k, const void* group_k, int64_t sum_cap, int32_t nmid_max,
+                          int32_t* mid_chunk, int32_t* mid_t0, int32_t* open_gid, int32_t* open_t0,
+                          int32_t impl, cudaStream_t stream);
+int hga_attend_decode_impl(const hga_params* p, int32_t L, const void* q, const int32_t* seq_pos,
+                           const void* hot_k, const void* hot_v, int64_t hot_cap, int32_t hot_mode,
+                           const void* cold_k, const void* cold_v, int64_t cold_cap,
+                           const int32_t* open_gid, const int32_t* open_t0, int32_t Kg, void* out,
+                           int32_t impl, cudaStream_t stream);
+
 /* hga_append_tokens: write L new K (RoPE applied) / V rows per sequence at seq_pos into the hot
  * rows (and, for hot_mode 1, the cold record), and their pre-RoPE K into active_raw
  * [B,KVH,C,Dh] (may be NULL) — ChunkRouter._append_active (chunk_router.py:603-614). */

@@ -247,3 +247,37 @@ def _seed_mixed(router, pre, starts, c):
             st.hot_v[b] = s1.hot_v[0]
     st.n_closed = min(s // C for s in starts)
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("tier", TIERS)
+@pytest.mark.parametrize("L", [1, 3, 8])
+def test_fast_decode_kernels_equal_portable_kernels(cuda, tier, L):
+    """The single-token router is bit-identical to the portable router; the short-block attention
+    matches the portable attention to fp32 rounding."""
+    from hierarchicalglobalattention_b200 import ops
+    c, inp = _synthetic(DECODE_SHAPES[0], seed=21)
+    p = c["params"]
+    B = 3
+    g = {k: t.expand(B, *t.shape[1:]).contiguous().to(cuda) for k, t in inp.items() if k != "cos" and k != "sin"}
+    router = _router(p, B, c["dtype"], cuda, tier)
+    S0 = 1900
+    router.seed(0, g["k_rope"][:, :, :S0], g["k_raw"][:, :, :S0], g["v"][:, :, :S0])
+    hp = router.cfg.hga_params(router.store.policy, B, c["dtype"])
+    st = router.store.layer_buffers(0)
+    seq = torch.tensor([S0, S0 - 37, S0 - 64 * 5 - 3], dtype=torch.int32, device=cuda)
+    q = torch.randn(B, p.nhead, L, p.head_dim, generator=torch.Generator().manual_seed(L)).to(c["dtype"]).to(cuda)
+    nmid = S0 // 64
+    if L == 1:
+        a = ops.route_decode(hp, q, seq, st.chunk_k, st.group_k, nmid, impl=1)
+        b = ops.route_decode(hp, q, seq, st.chunk_k, st.group_k, nmid, impl=2)
+        for k in a:
+            assert torch.equal(a[k], b[k]), k
+    else:
+        a = ops.route_decode(hp, q, seq, st.chunk_k, st.group_k, nmid, impl=1)
+    hk, hv = router.store.hot_buffers(0)
+    ck, cv = router.store.cold_buffers(0)
+    seq_att = torch.tensor([S0 - L, S0 - 37 - L, S0 - 64 * 5 - 3 - L], dtype=torch.int32, device=cuda)
+    seq_att = torch.where(seq_att % 64 + L > 64, seq_att - L, seq_att)
+    o1 = ops.attend_decode(hp, q, seq_att, hk, hv, router.store.hot_mode, ck, cv, a["open_gid"], a["open_t0"], impl=1)
+    o2 = ops.attend_decode(hp, q, seq_att, hk, hv, router.store.hot_mode, ck, cv, a["open_gid"], a["open_t0"], impl=2)
+    torch.testing.assert_close(o2.float(), o1.float(), atol=1e-2, rtol=1e-2)
