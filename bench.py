@@ -38,20 +38,54 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock and throttle-reason samples taken every 10 ms during the timed region (NVML reads
+    only; falls back to ``nvidia-smi -lms 200`` when the NVML binding is unavailable)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, device: torch.device):
+        self.device = device
         self.proc = None
         self.lines = []
+        self.samples = []      # (sm_mhz, reason bits)
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._nvml = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(self.device)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
+
+    def _poll(self):
+        nv, h = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+            except Exception:
+                pass
+            self._stop.wait(0.01)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+            self._nvml = self._nvml_handle()
+            nv, h = self._nvml
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self._nvml = None
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device.index or 0}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
@@ -65,6 +99,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *a):
+        if self._nvml is not None:
+            self._stop.set()
+            self.t.join(timeout=2)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -73,6 +110,16 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        if self._nvml is not None:
+            nv = self._nvml[0]
+            bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+            reasons = sorted(k for k, bit in bits.items() if any(r & bit for _, r in self.samples))
+            sm = [c for c, _ in self.samples]
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(sm), "source": "nvml 10 ms"}
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
@@ -88,7 +135,7 @@ class ClockSampler:
                 if val.lower().startswith("active"):
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi 200 ms"}
 
 
 def build_module(device, dtype, seed=0):
@@ -154,7 +201,7 @@ def run_ours(args, rank, world, device):
             torch.distributed.barrier()
         torch.cuda.synchronize()
         st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(device.index or 0) as clk:
+        with ClockSampler(device) as clk:
             st.record()
             for _ in range(args.steps):
                 m(x)
@@ -232,6 +279,83 @@ def cpu_sample(seconds_hint: float = 20.0, S: int = 32768, n_sample_chunks: int 
             "measured_s": t2 - t0}
 
 
+CFG2 = dict(batch=16, ctx=32768, nhead=32, kv_heads=4, head_dim=128, chunk_size=64, group_size=16, keep_first=2,
+            keep_last=8, topk_chunks=16, topk_groups=64, theta=1e6)
+
+
+def decode_bench(device, steps: int = 64, warmup: int = 8):
+    """batched decode step (B=16 sequences, 32768 cached tokens each, one new token per
+    sequence), one layer, through ChunkRouter.decode_block + RoutedKV.attend.  Timed per tier:
+    RAM (cold record in pinned host memory, windows in HBM; the config's tier) and VRAM."""
+    from hierarchicalglobalattention_b200 import ChunkPlacementPolicy, ChunkRouter, RouterConfig, VramKVCacheStore
+    from hierarchicalglobalattention_b200.store_ram import RamKVCacheStore
+    c = CFG2
+    B, H, KVH, Dh, S, C, gs = c["batch"], c["nhead"], c["kv_heads"], c["head_dim"], c["ctx"], c["chunk_size"], c["group_size"]
+    dt = torch.bfloat16
+    g = torch.Generator(device=device).manual_seed(2)
+    res = {}
+    # host-link reference: one pinned host -> device copy of 256 MB
+    hbuf = torch.empty(256 << 20, dtype=torch.uint8).pin_memory()
+    dbuf = torch.empty_like(hbuf, device=device)
+    for _ in range(2):
+        dbuf.copy_(hbuf, non_blocking=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(4):
+        dbuf.copy_(hbuf, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    res["h2d_copy_GBps"] = 4 * hbuf.numel() / (e0.elapsed_time(e1) / 1e3) / 1e9
+    del hbuf, dbuf
+    for tier in ("ram", "vram"):
+        cfg = RouterConfig(nhead=H, kv_heads=KVH, head_dim=Dh, chunk_size=C, group_size=gs,
+                           topk_chunks=c["topk_chunks"], topk_groups=c["topk_groups"], theta=c["theta"])
+        pol = ChunkPlacementPolicy(keep_first=c["keep_first"], keep_last=c["keep_last"], first_token_level=True)
+        cls = RamKVCacheStore if tier == "ram" else VramKVCacheStore
+        store = cls(compute_device=device, policy=pol, kv_heads=KVH, head_dim=Dh, chunk_size=C,
+                    groups_per_chunk=C // gs, batch_size=B, dtype=dt, initial_capacity=(S + 4 * C) // C)
+        router = ChunkRouter(cfg, store)
+        k_raw = torch.randn(B, KVH, S, Dh, device=device, dtype=dt, generator=g)
+        v = torch.randn(B, KVH, S, Dh, device=device, dtype=dt, generator=g)
+        cos, sin = router.rotary_table(0, S, device)
+        half = Dh // 2
+        kf = k_raw.float()
+        k_rope = (kf * cos[0, 0] + torch.cat((-kf[..., half:], kf[..., :half]), -1) * sin[0, 0]).to(dt)
+        del kf
+        router.seed(0, k_rope, k_raw, v)
+        del k_raw, v, k_rope
+        n = warmup + steps
+        qs = torch.randn(n, B, H, 1, Dh, device=device, dtype=dt, generator=g)
+        ks = torch.randn(n, B, KVH, 1, Dh, device=device, dtype=dt, generator=g)
+        torch.cuda.synchronize()
+        pos = S
+        vis_groups = 0
+        for i in range(n):
+            if i == warmup:
+                torch.cuda.synchronize()
+                t_wall = time.perf_counter()
+                e0.record()
+            rk = router.decode_block(0, qs[i], ks[i], ks[i], ks[i], pos)
+            rk.attend(qs[i])
+            if i == warmup:
+                vis_groups = int((rk.routing["open_t0"] >= 0).sum())
+            pos += 1
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / steps
+        wall_us = (time.perf_counter() - t_wall) * 1e6 / steps
+        cold = vis_groups * gs * Dh * 2 * 2                       # opened K+V rows read per step
+        hot = B * H * ((c["keep_first"] + c["keep_last"]) * C + (S % C) + 1) * Dh * 2 * 2
+        summ = B * KVH * (S // C) * Dh * 2 + B * H * c["topk_chunks"] * (C // gs) * Dh * 2
+        res[tier] = {"us_per_layer_step": us, "wall_us_per_step": wall_us, "cold_bytes_per_step": cold,
+                     "hbm_bytes_per_step": hot + summ + (0 if tier == "ram" else cold)}
+        if tier == "ram":
+            res[tier]["host_link_GBps"] = cold / (us / 1e6) / 1e9
+        del router, store
+        torch.cuda.empty_cache()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -240,6 +364,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq", type=int, default=32768)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the configs[2] decode measurement")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -309,6 +434,14 @@ def main():
                          "peak_kind": f"{kind} bf16 sustained", "attention_ms": r["att_ms"],
                          "visible_pairs": r["pairs"]},
             "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["launches_per_step"] * args.steps}
+    if not args.no_decode:
+        try:
+            d = decode_bench(device)
+            line["decode"] = {"workload": "configs[2]: batched decode step, B=16 x 32768 cached tokens, one layer",
+                              "unit": "us/layer-step", "value": d["ram"]["us_per_layer_step"],
+                              "tier": "ram (cold K/V in pinned host memory)", **d}
+        except Exception as e:
+            line["decode"] = {"error": str(e)[:300]}
     print(json.dumps(line))
     if world > 1:
         torch.distributed.destroy_process_group()

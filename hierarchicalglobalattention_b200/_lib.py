@@ -132,7 +132,8 @@ def make_params(*, batch, nhead, kv_heads, head_dim, chunk_size, group_size, top
 
 
 def device_status(clear: bool = True) -> int:
-    """Error word of the tensor-core kernels (0 = no bounded wait timed out)."""
+    """First device error code of the kernels (0 = none): a bounded tensor-core wait that timed out,
+    or a decode bounds check (0x101 routing, 0x102 attention, 0x103 append)."""
     code = ctypes.c_int32(0)
     check(lib().hga_device_status(ctypes.byref(code), 1 if clear else 0), "hga_device_status")
     return int(code.value)

@@ -38,6 +38,8 @@ cudaError_t launch_attend_decode(const hga_params& p, int L, const void* q, cons
                                  const void* hv, int64_t hot_cap, int hot_mode, const void* ckk, const void* cvv,
                                  int64_t cold_cap, const int32_t* og, const int32_t* ot, int Kg, void* out,
                                  cudaStream_t st);
+int decode_error_status(bool clear);
+int decode_fast_error_status(bool clear);
 bool route_decode1_supported(const hga_params& p, int L);
 cudaError_t launch_route_decode1(const hga_params& p, const void* q, const int32_t* seq_pos, const void* ck,
                                  const void* gk, int64_t sum_cap, int nmid_max, int Kcmax, int Kgmax, int32_t* mc,
@@ -285,10 +287,14 @@ int hga_append_tokens(const hga_params* p, int32_t L, const int32_t* seq_pos, co
 }
 
 int hga_device_status(int32_t* code, int32_t clear) {
-  const int v = hga::tc_error_status(clear != 0);
-  const int w = hga::route_tc_error_status(clear != 0);
-  if (v < 0 || w < 0) return fail(HGA_E_CUDA, "hga_device_status: cannot read the device error word");
-  if (code) *code = v ? v : w;
+  const int words[4] = {hga::tc_error_status(clear != 0), hga::route_tc_error_status(clear != 0),
+                        hga::decode_error_status(clear != 0), hga::decode_fast_error_status(clear != 0)};
+  int first = 0;
+  for (int w : words) {
+    if (w < 0) return fail(HGA_E_CUDA, "hga_device_status: cannot read the device error word");
+    if (!first) first = w;
+  }
+  if (code) *code = first;
   return HGA_OK;
 }
 

@@ -19,6 +19,8 @@
 
 namespace hga {
 
+HGA_DEVICE_ERROR_WORD(g_decode_error, decode_error_status)
+
 constexpr int kDecThreads = 256;
 constexpr int kDecTile = 64;
 
@@ -41,6 +43,10 @@ __global__ void __launch_bounds__(kDecThreads) route_decode_kernel(
   for (int i = tid; i < Kcmax; i += blockDim.x) { mid_chunk[bh * Kcmax + i] = -1; mid_t0[bh * Kcmax + i] = -1; }
   for (int i = tid; i < Kgmax; i += blockDim.x) { open_gid[bh * Kgmax + i] = -1; open_t0[bh * Kgmax + i] = -1; }
   if (n_mid == 0 || p.topk_chunks <= 0) return;
+  if ((int64_t)l_lo > sum_cap || n_mid > nmid_max) {
+    if (tid == 0) atomicCAS(&g_decode_error, 0, kErrBoundsRouteDecode);
+    return;
+  }
   const int Kc = p.topk_chunks < n_mid ? p.topk_chunks : n_mid;
   const int G = Kc * M;
   const int Kg = p.topk_groups > 0 ? (p.topk_groups < G ? p.topk_groups : G) : 0;
@@ -221,6 +227,12 @@ __global__ void __launch_bounds__(128) attend_decode_kernel(
   int f_hi, l_lo;
   windows(n_closed, kf, kl, f_hi, l_lo);
   const size_t bh = (size_t)b * H + h;
+  const bool hot_oob = hot_mode == 0 ? (int64_t)(n_closed + 1) * C > hot_cap : (int64_t)(kf + kl + 1) * C > hot_cap;
+  if (hot_oob || (int64_t)n_closed * C > cold_cap) {
+    if (tid == 0) atomicCAS(&g_decode_error, 0, kErrBoundsAttendDecode);
+    for (int i = tid; i < L * Dh; i += blockDim.x) out[bh * L * Dh + i] = Num<T>::from_f(0.f);
+    return;
+  }
   // key segments: (source 0 hot / 1 cold, chunk, first row, length, tmin, causal offset)
   const int ld = Dh + 1;
   float* qs = (float*)smem;                 // [L][ld]
@@ -257,6 +269,10 @@ __global__ void __launch_bounds__(128) attend_decode_kernel(
           // the opened entries are a prefix of the list
           const int j = kk / gs;
           row = (int64_t)open_gid[bh * Kg + j] * gs + kk % gs; tmin = open_t0[bh * Kg + j]; src = 1;
+          if (row >= cold_cap) {  // a list entry past the record: skipped (never visible)
+            atomicCAS(&g_decode_error, 0, kErrBoundsAttendDecode);
+            row = 0; tmin = 1 << 30;
+          }
         } else {
           const int u = k - nfirst - nlast - nopen * gs;
           row = hot_row(n_closed, u, C, hot_mode, kf, kl, true); tmin = u - c0;
@@ -345,6 +361,10 @@ __global__ void append_kernel(hga_params p, int L, const int32_t* __restrict__ s
     const int n = pos / C, u = pos % C;
     const T kr = k_rope[i], vv = v[i];
     const int64_t hr = hot_row(n, u, C, hot_mode, kf, kl, true);
+    if (hr >= hot_cap || (hot_mode != 0 && cold_k && pos >= cold_cap)) {
+      atomicCAS(&g_decode_error, 0, kErrBoundsAppend);
+      continue;
+    }
     hot_k[((int64_t)bk * hot_cap + hr) * Dh + d] = kr;
     hot_v[((int64_t)bk * hot_cap + hr) * Dh + d] = vv;
     if (hot_mode != 0 && cold_k) {

@@ -8,13 +8,17 @@
 //    and the visible groups are the row's top-Kg_request among the chosen chunks' groups (a
 //    subset of the pooled top-Kg).  One thread scores one summary row with 16-byte loads.
 //  * attention: one warp streams one 16-token unit at a time (a window group, an opened group or
-//    a group of the active chunk).  A lane pair holds one key (each lane half of head_dim, eight
-//    16-byte loads), every lane holds head_dim/32 columns of all 16 values, and the warp keeps an
+//    a group of the active chunk).  The unit's K rows are read as whole lines (consecutive lanes,
+//    consecutive 16-byte pieces) and staged in shared memory, a lane pair then scores one key
+//    (each lane half of head_dim), every lane holds head_dim/32 columns of all 16 values (also read
+//    as whole lines), and the warp keeps an
 //    fp32 online-softmax state per query row; the 8 warps' states are merged at the end.  Opened
 //    groups are read from the cold record, which for the RAM tier is pinned host memory.
 #include "select.cuh"
 
 namespace hga {
+
+HGA_DEVICE_ERROR_WORD(g_decode_fast_error, decode_fast_error_status)
 
 template <typename T>
 __device__ __forceinline__ void unpack16(const uint4& u, float* f) {
@@ -77,6 +81,10 @@ __global__ void __launch_bounds__(256) route_decode1_kernel(
   for (int i = tid; i < Kcmax; i += blockDim.x) { mid_chunk[bh * Kcmax + i] = -1; mid_t0[bh * Kcmax + i] = -1; }
   for (int i = tid; i < Kgmax; i += blockDim.x) { open_gid[bh * Kgmax + i] = -1; open_t0[bh * Kgmax + i] = -1; }
   if (n_mid == 0 || p.topk_chunks <= 0) return;
+  if ((int64_t)l_lo > sum_cap || n_mid > nkey_max) {
+    if (tid == 0) atomicCAS(&g_decode_fast_error, 0, kErrBoundsRouteDecode);
+    return;
+  }
   const int Kc = p.topk_chunks < n_mid ? p.topk_chunks : n_mid;
   const int G = Kc * M;
   const int Kg = p.topk_groups > 0 ? (p.topk_groups < G ? p.topk_groups : G) : 0;
@@ -95,11 +103,12 @@ __global__ void __launch_bounds__(256) route_decode1_kernel(
   for (int i = tid; i < n_mid; i += blockDim.x)
     keys[i] = ord_f32(ref_score<T>(dot_row<T, DH>(qs, ckb + (size_t)(f_hi + i) * DH), p.scale));
   __syncthreads();
-  block_select(keys, n_mid, Kc, flag, sred);
-  // the previous chunk replaces the lowest chosen one (ties: the highest index) when in the pool
-  const int prev = n_closed - 1;
-  if (prev >= f_hi && prev < l_lo && !flag[prev - f_hi]) {
-    if (warp == 0) {
+  // selection runs in warp 0 alone (shuffle reductions, no block barriers)
+  if (warp == 0) {
+    warp_select(keys, n_mid, Kc, flag);
+    // the previous chunk replaces the lowest chosen one (ties: the highest index) when in the pool
+    const int prev = n_closed - 1;
+    if (prev >= f_hi && prev < l_lo && !flag[prev - f_hi]) {
       unsigned long long worst = ~0ull;
       for (int i = lane; i < n_mid; i += 32)
         if (flag[i]) {
@@ -114,21 +123,19 @@ __global__ void __launch_bounds__(256) route_decode1_kernel(
         flag[0xffffffffu - (uint32_t)(worst & 0xffffffffull)] = 0;
         flag[prev - f_hi] = 1;
       }
+      __syncwarp();
     }
-    __syncthreads();
-  }
-  if (warp == 0) {
     const int k = warp_compact(flag, n_mid, idx);
+    __syncwarp();
+    for (int i = lane; i < k; i += 32) {
+      idx[i] += f_hi;
+      mid_chunk[bh * Kcmax + i] = idx[i];
+      mid_t0[bh * Kcmax + i] = 0;
+    }
     if (lane == 0) sred[8] = k;
   }
   __syncthreads();
   const int ksel = sred[8];
-  for (int i = tid; i < ksel; i += blockDim.x) {
-    idx[i] += f_hi;
-    mid_chunk[bh * Kcmax + i] = idx[i];
-    mid_t0[bh * Kcmax + i] = 0;
-  }
-  __syncthreads();
   if (Kg <= 0 || Kgr <= 0) return;
   // ---- level 2: one thread per candidate group of the chosen chunks ----------------------------
   const int Gs = ksel * M;
@@ -136,8 +143,8 @@ __global__ void __launch_bounds__(256) route_decode1_kernel(
   for (int j = tid; j < Gs; j += blockDim.x)
     keys[j] = ord_f32(ref_score<T>(dot_row<T, DH>(qs, gkb + ((size_t)idx[j / M] * M + (j % M)) * DH), p.scale));
   __syncthreads();
-  block_select(keys, Gs, Kgr < Gs ? Kgr : Gs, flag, sred);
   if (warp == 0) {
+    warp_select(keys, Gs, Kgr < Gs ? Kgr : Gs, flag);
     int k = 0;
     for (int base = 0; base < Gs; base += 32) {
       const int j = base + lane;
@@ -224,11 +231,15 @@ __global__ void __launch_bounds__(kAttWarps * 32, (LM == 1 ? 2 : 1)) attend_deco
   constexpr int KLD = HALF / 8;   // 16-byte loads per lane for its half key row
   constexpr int VD = DH / 32;     // value columns per lane
   using VT = typename VCols<DH>::type;
+  constexpr int CPK = DH * 2 / 16;        // 16-byte pieces per key row
+  constexpr int RS = DH * 2 + 32;         // staged row stride (bytes): conflict-free lane-pair reads
+  constexpr int HO = HALF * 2 + 16;       // offset of a staged row's second half
   extern __shared__ __align__(16) unsigned char smem[];
   float* qs = (float*)smem;                               // [LM][DH]
   float* so = qs + LM * DH;                               // [warps][LM][DH]
   float* sm = so + kAttWarps * LM * DH;                   // [warps][LM]
   float* sl = sm + kAttWarps * LM;                        // [warps][LM]
+  unsigned char* kst = (unsigned char*)(sl + kAttWarps * LM) + (size_t)(threadIdx.x >> 5) * kUnit * RS;
 
   const int h = blockIdx.x, b = blockIdx.y;
   const int H = p.nhead, KVH = p.kv_heads, C = p.chunk_size, M = C / kUnit;
@@ -240,6 +251,12 @@ __global__ void __launch_bounds__(kAttWarps * 32, (LM == 1 ? 2 : 1)) attend_deco
   int f_hi, l_lo;
   windows(n_closed, kf, kl, f_hi, l_lo);
   const size_t bh = (size_t)b * H + h;
+  const bool hot_oob = hot_mode == 0 ? (int64_t)(n_closed + 1) * C > hot_cap : (int64_t)(kf + kl + 1) * C > hot_cap;
+  if (hot_oob || (int64_t)n_closed * C > cold_cap) {
+    if (tid == 0) atomicCAS(&g_decode_fast_error, 0, kErrBoundsAttendDecode);
+    for (int i = tid; i < L * DH; i += blockDim.x) out[bh * L * DH + i] = Num<T>::from_f(0.f);
+    return;
+  }
 
   // the opened entries are a prefix of the list (entries that no row sees are not written)
   int nopen = 0;
@@ -282,7 +299,12 @@ __global__ void __launch_bounds__(kAttWarps * 32, (LM == 1 ? 2 : 1)) attend_deco
       kb = hot_k; vb = hot_v;
     } else if (u < nfirst_u + nlast_u + nopen) {
       const int j = u - nfirst_u - nlast_u;
-      row = cold_base + (int64_t)open_gid[bh * Kg + j] * kUnit;
+      const int gid = open_gid[bh * Kg + j];
+      if ((int64_t)(gid + 1) * kUnit > cold_cap) {  // warp-uniform
+        if (lane == 0) atomicCAS(&g_decode_fast_error, 0, kErrBoundsAttendDecode);
+        continue;
+      }
+      row = cold_base + (int64_t)gid * kUnit;
       t0 = open_t0[bh * Kg + j];
       kb = cold_k; vb = cold_v;
     } else {
@@ -290,14 +312,28 @@ __global__ void __launch_bounds__(kAttWarps * 32, (LM == 1 ? 2 : 1)) attend_deco
       row = hot_base + slot_row(n_closed, act0, C, hot_mode, kf, kl, true);
       kb = hot_k; vb = hot_v;
     }
+    // K: the unit's 16 rows are one contiguous block; lanes read consecutive 16-byte pieces (whole
+    // lines per instruction, which matters most for rows in host memory) and stage them in shared
+    // memory, from which each lane pair reads its key.
     uint4 kr[KLD];
-    const uint4* kp = reinterpret_cast<const uint4*>(kb + (row + key) * DH + half * HALF);
+    const uint4* kp = reinterpret_cast<const uint4*>(kb + row * DH);
 #pragma unroll
-    for (int i = 0; i < KLD; ++i) kr[i] = kp[i];
+    for (int i = 0; i < KLD; ++i) kr[i] = kp[i * 32 + lane];
     VT vr[kUnit];
     const T* vp = vb + row * DH + lane * VD;
 #pragma unroll
     for (int j = 0; j < kUnit; ++j) vr[j] = *reinterpret_cast<const VT*>(vp + (size_t)j * DH);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < KLD; ++i) {
+      const int c = i * 32 + lane;
+      const int w = (c % CPK) * 16;
+      *reinterpret_cast<uint4*>(kst + (c / CPK) * RS + w + (w >= HALF * 2 ? 16 : 0)) = kr[i];
+    }
+    __syncwarp();
+    const uint4* kmine = reinterpret_cast<const uint4*>(kst + key * RS + half * HO);
+#pragma unroll
+    for (int i = 0; i < KLD; ++i) kr[i] = kmine[i];
 
 #pragma unroll
     for (int t = 0; t < LM; ++t) {
@@ -374,7 +410,8 @@ static cudaError_t launch_att_fast(const hga_params& p, int L, const void* q, co
                                    const void* hv, int64_t hot_cap, int hot_mode, const void* ckk, const void* cvv,
                                    int64_t cold_cap, const int32_t* og, const int32_t* ot, int Kg, void* out,
                                    cudaStream_t st) {
-  const size_t smem = ((size_t)LM * DH + (size_t)kAttWarps * LM * DH + 2 * kAttWarps * LM) * 4;
+  const size_t smem = ((size_t)LM * DH + (size_t)kAttWarps * LM * DH + 2 * kAttWarps * LM) * 4 +
+                      (size_t)kAttWarps * kUnit * (DH * 2 + 32);
   auto kern = attend_decode_fast_kernel<T, DH, LM>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

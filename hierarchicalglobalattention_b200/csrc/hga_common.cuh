@@ -70,4 +70,25 @@ __host__ __device__ __forceinline__ void windows(int n, int keep_first, int keep
   }
 }
 
+// Device error word of one translation unit's kernels (a file-scope variable, so each .cu file
+// that uses the macro gets its own word) and its host-side reader: 0, or the first error code.
+#define HGA_DEVICE_ERROR_WORD(word, reader)                              \
+  static __device__ int word = 0;                                        \
+  int reader(bool clear) {                                               \
+    int v = 0;                                                           \
+    if (cudaMemcpyFromSymbol(&v, word, sizeof(int)) != cudaSuccess)      \
+      return -1;                                                         \
+    if (clear && v) {                                                    \
+      int z = 0;                                                         \
+      cudaMemcpyToSymbol(word, &z, sizeof(int));                         \
+    }                                                                    \
+    return v;                                                            \
+  }
+
+// Codes of the decode kernels' bounds checks: a position or list entry whose rows lie past a
+// buffer's capacity.  The kernel skips those rows (its output for the (b, h) is then zero).
+constexpr int kErrBoundsRouteDecode = 0x101;
+constexpr int kErrBoundsAttendDecode = 0x102;
+constexpr int kErrBoundsAppend = 0x103;
+
 }  // namespace hga

@@ -61,11 +61,11 @@ def close_chunk(router, layer: int, hp, n, rows=None) -> None:
     act = store.active_raw(layer)
     if rows is None:
         k_act, v_act = store.active_rows(layer, n)
-        cos, sin = router._rotary(act.device, (n + 1) * C)
+        cos, sin = router.chunk_rotary(n, act.device)
         store.ensure_capacity(layer, n + 1)
         st = store.layer_buffers(layer)
         ops.summaries(hp, act, k_act.contiguous(), v_act.contiguous(), cos, sin, seq_len=C, pos0=n * C,
-                      out=(st.chunk_k, st.group_k, st.group_v), out_chunk0=n)
+                      rot_row0=n * C, out=(st.chunk_k, st.group_k, st.group_v), out_chunk0=n)
         store.on_chunk_closed(layer, n)
         store.mark_closed(layer, n + 1)
         return
@@ -75,11 +75,11 @@ def close_chunk(router, layer: int, hp, n, rows=None) -> None:
     hp1.batch = 1
     for b, nb in zip(rows, n):
         k_act, v_act = store.active_rows(layer, nb)
-        cos, sin = router._rotary(act.device, (nb + 1) * C)
+        cos, sin = router.chunk_rotary(nb, act.device)
         store.ensure_capacity(layer, nb + 1)
         st = store.layer_buffers(layer)
         ops.summaries(hp1, act[b:b + 1], k_act[b:b + 1].contiguous(), v_act[b:b + 1].contiguous(), cos, sin,
-                      seq_len=C, pos0=nb * C,
+                      seq_len=C, pos0=nb * C, rot_row0=nb * C,
                       out=(st.chunk_k[b:b + 1], st.group_k[b:b + 1], st.group_v[b:b + 1]), out_chunk0=nb)
         store.on_chunk_closed(layer, nb, row=b)
 

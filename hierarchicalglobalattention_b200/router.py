@@ -63,6 +63,7 @@ class ChunkRouter:
         self.store = store
         self._active_len: Dict[int, int] = {}
         self._rot_cache: Dict[Tuple[str, int], Tuple[torch.Tensor, torch.Tensor]] = {}
+        self._close_rot: Dict[Tuple[str, int], Tuple[torch.Tensor, torch.Tensor]] = {}
         self._pending: Dict[int, object] = {}   # decode blocks whose chunk close waits for their attention
         self._pos_cache: Dict[Tuple[int, int, str], torch.Tensor] = {}
 
@@ -94,7 +95,8 @@ class ChunkRouter:
         """fp32 cos/sin ``[1, 1, length, Dh]`` for positions [start_pos, start_pos+length)
         (chunk_router.py:457-461, 702-709)."""
         cos, sin = self._rotary(device, start_pos + length)
-        return cos[start_pos:].view(1, 1, length, -1), sin[start_pos:].view(1, 1, length, -1)
+        e = start_pos + length
+        return cos[start_pos:e].view(1, 1, length, -1), sin[start_pos:e].view(1, 1, length, -1)
 
     def _rotary(self, device, length: int) -> Tuple[torch.Tensor, torch.Tensor]:
         key = (str(device), 0)
@@ -110,6 +112,24 @@ class ChunkRouter:
             cached = (emb.cos().to(device), emb.sin().to(device))
             self._rot_cache[key] = cached
         return cached
+
+    def chunk_rotary(self, n: int, device) -> Tuple[torch.Tensor, torch.Tensor]:
+        """fp32 cos/sin ``[C, Dh]`` for the positions of chunk n (rows [n*C, n*C + C)), as the
+        chunk-close summaries read them (their anchors, chunk_router.py:702-709).  Built on the host
+        for a few KB per chunk and kept for the layers that close the same chunk."""
+        key = (str(device), n)
+        t = self._close_rot.get(key)
+        if t is None:
+            if len(self._close_rot) > 256:
+                self._close_rot.clear()
+            C, half = self.cfg.chunk_size, self.cfg.head_dim // 2
+            inv = 1.0 / (self.cfg.theta ** (torch.arange(half, dtype=torch.float32) / half))
+            f = torch.arange(n * C, n * C + C, dtype=torch.float32).unsqueeze(-1) * inv
+            emb = torch.cat((f, f), dim=-1)
+            t = (emb.cos().pin_memory().to(device, non_blocking=True),
+                 emb.sin().pin_memory().to(device, non_blocking=True))
+            self._close_rot[key] = t
+        return t
 
     # ---------------------------------------------------------------------------------------
     def route_query_block(self, layer: int, q: torch.Tensor, k_rope: torch.Tensor, k_raw: torch.Tensor,

@@ -171,9 +171,12 @@ int hga_append_tokens(const hga_params* p, int32_t L, const int32_t* seq_pos, co
                       int32_t hot_mode, void* cold_k, void* cold_v, int64_t cold_cap, void* active_raw,
                       cudaStream_t stream);
 
-/* Device-side error word of the tensor-core kernels: 0, or the code of the first bounded
- * mbarrier wait that timed out (the CTA then released its TMEM and returned without output).
- * Synchronous (reads device memory); clear != 0 resets the word. */
+/* Device-side error words: 0, or the first code recorded.  The tensor-core kernels record a
+ * bounded mbarrier wait that timed out (the CTA then released its TMEM and returned without
+ * output); the decode kernels record 0x101 / 0x102 / 0x103 (routing / attention / append) when a
+ * sequence position or a list entry addresses rows past a buffer's capacity (those rows are
+ * skipped; a (b, h) whose position is past the capacity gets a zero output).
+ * Synchronous (reads device memory); clear != 0 resets the words. */
 int hga_device_status(int32_t* code, int32_t clear);
 
 #ifdef __cplusplus

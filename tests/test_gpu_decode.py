@@ -281,3 +281,36 @@ def test_fast_decode_kernels_equal_portable_kernels(cuda, tier, L):
     o1 = ops.attend_decode(hp, q, seq_att, hk, hv, router.store.hot_mode, ck, cv, a["open_gid"], a["open_t0"], impl=1)
     o2 = ops.attend_decode(hp, q, seq_att, hk, hv, router.store.hot_mode, ck, cv, a["open_gid"], a["open_t0"], impl=2)
     torch.testing.assert_close(o2.float(), o1.float(), atol=1e-2, rtol=1e-2)
+
+
+def test_positions_past_capacity_are_reported_not_read(cuda):
+    """A sequence position whose rows lie past the buffers is skipped by the kernels, reported in
+    the device error word, and leaves the context usable."""
+    from hierarchicalglobalattention_b200 import _lib, ops
+    c, inp = _synthetic(DECODE_SHAPES[0], seed=4)
+    p = c["params"]
+    g = {k: t.to(cuda) for k, t in inp.items() if k not in ("cos", "sin")}
+    router = _router(p, 1, c["dtype"], cuda, "vram")
+    S0 = 640
+    router.seed(0, g["k_rope"][:, :, :S0], g["k_raw"][:, :, :S0], g["v"][:, :, :S0])
+    hp = router.cfg.hga_params(router.store.policy, 1, c["dtype"])
+    st = router.store.layer_buffers(0)
+    _lib.device_status(clear=True)
+    far = torch.tensor([st.tcap + 64 * 3], dtype=torch.int32, device=cuda)      # rows past the token buffers
+    q = g["q"][:, :, :1].contiguous()
+    empty = torch.empty(1, p.nhead, 0, dtype=torch.int32, device=cuda)
+    for impl in (1, 2):
+        out = ops.attend_decode(hp, q, far, st.token_k, st.token_v, 0, st.token_k, st.token_v, empty, empty, impl=impl)
+        torch.cuda.synchronize()
+        assert _lib.device_status(clear=True) == 0x102
+        assert torch.count_nonzero(out) == 0
+    for impl in (1, 2):
+        ops.route_decode(hp, q, far, st.chunk_k[:, :, :10], st.group_k[:, :, :10], 10, impl=impl)
+        torch.cuda.synchronize()
+        assert _lib.device_status(clear=True) == 0x101
+    # the context still works
+    ok = torch.tensor([S0], dtype=torch.int32, device=cuda)
+    r = ops.route_decode(hp, q, ok, st.chunk_k, st.group_k, S0 // 64)
+    ops.attend_decode(hp, q, ok, st.token_k, st.token_v, 0, st.token_k, st.token_v, r["open_gid"], r["open_t0"])
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
