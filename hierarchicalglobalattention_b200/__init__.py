@@ -10,7 +10,10 @@ from . import _lib, ops  # noqa: F401
 from .config import ChunkPlacementPolicy, RouterConfig
 from .module import HierarchicalGlobalAttentionRouted
 from .router import ChunkRouter, RoutedKV
+from .qwen import QwenRoutedAttention, replace_qwen_attention_with_router, restore_original_attention
 from .store import KVCacheStore, VramKVCacheStore
+from .store_ram import RamKVCacheStore
 
 __all__ = ["ChunkPlacementPolicy", "RouterConfig", "HierarchicalGlobalAttentionRouted", "ChunkRouter",
-           "RoutedKV", "KVCacheStore", "VramKVCacheStore", "ops"]
+           "RoutedKV", "KVCacheStore", "VramKVCacheStore", "RamKVCacheStore", "QwenRoutedAttention",
+           "replace_qwen_attention_with_router", "restore_original_attention", "ops"]

@@ -23,6 +23,42 @@ from .router import ChunkRouter
 from .store import VramKVCacheStore
 
 
+def routed_attention(router: ChunkRouter, layer: int, hp, qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                     rot_row0: int, start_pos: int, q_norm_w: Optional[torch.Tensor], k_norm_w: Optional[torch.Tensor],
+                     eps: float, *, norm_mode: int, rope_mode: int, round_table: bool) -> torch.Tensor:
+    """Attention core shared by the routed module and the Qwen3 wrapper: q/k RMSNorm + RoPE
+    prologue on the fused projection output ``qkv`` [B,S,(H+2KVH)*Dh], routing through ``router``
+    and the routed attention kernels.  Returns the heads' output [B,S,H,Dh] (o_proj input layout).
+
+    ``cos``/``sin`` [R, Dh] hold the rotary rows of positions [rot_row0, rot_row0 + R): fp32 for
+    rope_mode 0, the model dtype for rope_mode 1.  A fresh multi-chunk prefill into a VRAM store
+    writes K/V straight into the store's token rows (no seed copy)."""
+    B, S, _ = qkv.shape
+    H, KVH, Dh, C = hp.nhead, hp.kv_heads, hp.head_dim, hp.chunk_size
+    multi_chunk = start_pos // C != (start_pos + S - 1) // C
+    store = router.store
+    kv_out = None
+    if start_pos == 0 and multi_chunk and not getattr(store, "cold_on_host", False):
+        # k_raw gets a scratch buffer with the token rows' capacity
+        st = store.ensure_capacity(layer, max(S // C, 1), S)
+        kraw_buf = torch.empty(B, KVH, st.tcap, Dh, device=qkv.device, dtype=qkv.dtype)
+        kv_out = (kraw_buf, st.token_k, st.token_v)
+    q_rope, k_raw, k_rope, v = ops.qkv_prologue(hp, qkv, cos, sin, q_norm_w=q_norm_w, k_norm_w=k_norm_w, eps=eps,
+                                                norm_mode=norm_mode, rope_mode=rope_mode, rot_row0=rot_row0,
+                                                pos0=start_pos, kv_out=kv_out, kv_row0=0)
+    out_heads = torch.empty(B, S, H, Dh, device=qkv.device, dtype=qkv.dtype)
+    r0 = start_pos - rot_row0
+    segments = router.route_query_block(layer, q_rope, k_rope, k_raw, v, start_pos,
+                                        cos=cos[r0:r0 + S].view(1, 1, S, Dh), sin=sin[r0:r0 + S].view(1, 1, S, Dh),
+                                        _round_table=round_table, _out=out_heads)
+    for routed, lo, hi in segments:
+        if routed.chunked and lo == 0 and hi == S:
+            routed.attend(q_rope, use_summaries=False)
+        else:
+            out_heads[:, lo:hi] = routed.attend(q_rope[:, :, lo:hi], use_summaries=False).transpose(1, 2)
+    return out_heads
+
+
 class RMSNorm(nn.Module):
     """RMSNorm with the reference's parameter name and fp32 arithmetic (HierarchicalGlobalAttentionRouted.py:56-67)."""
 
@@ -149,27 +185,7 @@ class HierarchicalGlobalAttentionRouted(nn.Module):
         kn = self.k_norm.weight if isinstance(self.k_norm, RMSNorm) else None
         qn = None if qn is None else qn.detach().to(x.dtype).contiguous()
         kn = None if kn is None else kn.detach().to(x.dtype).contiguous()
-        multi_chunk = start_pos // C != (start_pos + S - 1) // C
-        store = router.store
-        kv_out = None
-        if start_pos == 0 and multi_chunk and not getattr(store, "cold_on_host", False):
-            # the prologue writes K/V straight into the store's token rows (zero-copy seed); k_raw
-            # gets a scratch buffer with the same row capacity
-            st = store.ensure_capacity(self.layer_idx, max(S // C, 1), S)
-            kraw_buf = torch.empty(B, KVH, st.tcap, Dh, device=x.device, dtype=x.dtype)
-            kv_out = (kraw_buf, st.token_k, st.token_v)
-        q_rope, k_raw, k_rope, v = ops.qkv_prologue(hp, qkv, cos, sin, q_norm_w=qn, k_norm_w=kn, eps=self.norm_eps,
-                                                    norm_mode=0, rope_mode=0, rot_row0=rot_row0, pos0=start_pos,
-                                                    kv_out=kv_out, kv_row0=0)
-        out_heads = torch.empty(B, S, H, Dh, device=x.device, dtype=x.dtype)
-        r0 = start_pos - rot_row0
-        segments = router.route_query_block(self.layer_idx, q_rope, k_rope, k_raw, v, start_pos,
-                                            cos=cos[r0:r0 + S].view(1, 1, S, Dh), sin=sin[r0:r0 + S].view(1, 1, S, Dh),
-                                            _round_table=True, _out=out_heads)
-        for routed, lo, hi in segments:
-            if routed.chunked and lo == 0 and hi == S:
-                routed.attend(q_rope, use_summaries=False)
-            else:
-                out_heads[:, lo:hi] = routed.attend(q_rope[:, :, lo:hi], use_summaries=False).transpose(1, 2)
+        out_heads = routed_attention(router, self.layer_idx, hp, qkv, cos, sin, rot_row0, start_pos, qn, kn,
+                                     self.norm_eps, norm_mode=0, rope_mode=0, round_table=True)
         out = self.o_proj(out_heads.view(B, S, H * Dh))
         return out, {}

@@ -39,6 +39,7 @@ class RoutedKV:
     chunk_size: int = 0
     decode: Optional[object] = None
     out: Optional[torch.Tensor] = field(default=None, repr=False)  # optional [B,S,H,Dh] destination
+    result: Optional[torch.Tensor] = field(default=None, repr=False)  # attention already computed
 
     def attend(self, q: torch.Tensor, use_summaries: bool = False) -> torch.Tensor:
         """Token-only attention over the routed keys: ``q`` [B,H,L,Dh] -> [B,H,L,Dh].
@@ -49,6 +50,10 @@ class RoutedKV:
         if use_summaries:
             raise NotImplementedError("summary-attending attention is not part of the B200 hot path; "
                                       "call attend(q, use_summaries=False)")
+        if self.result is not None:
+            if self.result.shape != q.shape:
+                raise ValueError("attend(q): q does not match the block this segment was routed for")
+            return self.result
         if self.chunked:
             return ops.attend_prefill(self.params, q, self.token_k, self.token_v, self.routing["open_gid"],
                                       self.routing["open_t0"], seq_len=self.seq_len, out=self.out)
@@ -155,13 +160,17 @@ class ChunkRouter:
         if start_pos == 0:
             return [(self._prefill_chunk_parallel(layer, q, k_rope, k_raw, v, cos, sin, populate_store,
                                                   _round_table, _out), 0, S)]
+        # one incremental segment per chunk.  Each segment is attended before the next one is
+        # routed: closing a chunk recycles store rows (the RAM tier's window and active slots) that
+        # the previous segment's attention reads, so the attention cannot wait for the caller.
         segs = []
         p, done = start_pos, 0
         while done < S:
             take = min(C - (p % C), S - done)
             sl = slice(done, done + take)
-            segs.append((self.decode_block(layer, q[:, :, sl], k_rope[:, :, sl], k_raw[:, :, sl], v[:, :, sl], p),
-                         done, done + take))
+            rk = self.decode_block(layer, q[:, :, sl], k_rope[:, :, sl], k_raw[:, :, sl], v[:, :, sl], p)
+            rk.result = rk.attend(q[:, :, sl])
+            segs.append((rk, done, done + take))
             p += take
             done += take
         return segs

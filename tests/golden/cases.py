@@ -52,6 +52,13 @@ CASES = [
     dict(name="mod_cfg0", kind="module", dtype=F32, seed=20, B=1, S=4096, row_step=8, d_model=512,
          params=_p(nhead=8, kv_heads=2, head_dim=64, chunk_size=64, group_size=16, topk_chunks=16,
                    topk_groups=64, keep_first=2, keep_last=8, theta=1e4)),
+    # Qwen3 wrapper over HF Qwen3MoeAttention: a chunk-parallel prefill of `prefix` tokens, then
+    # blocks of `block` tokens through the incremental path (the reference's serving schedule).
+    # theta 1e6: the reference reads config.rope_theta, absent under transformers 5, and falls back
+    # to 1e6, so the routed summaries agree only when the model's theta is 1e6 as well.
+    dict(name="qwen_wrap_fp32", kind="qwen", dtype=F32, seed=21, B=1, S=1100, prefix=1024, block=19, row_step=3,
+         d_model=512, params=_p(nhead=8, kv_heads=2, head_dim=64, chunk_size=64, group_size=16, topk_chunks=4,
+                                topk_groups=8, keep_first=1, keep_last=2, theta=1e6)),
 ]
 
 
@@ -91,6 +98,51 @@ def make_module_inputs(c):
             "wq": w(H * Dh, D), "wk": w(KVH * Dh, D), "wv": w(KVH * Dh, D), "wo": w(D, H * Dh)}
 
 
+def make_qwen_inputs(c):
+    """x N(0, 1), projections N(0, 0.02), q/k RMSNorm weights 1 + N(0, 0.1).  (Input checksums are
+    fp32 sums whose order follows the host thread count: compare them at rel 1e-6.)"""
+    p, B, S, dtype, D = c["params"], c["B"], c["S"], c["dtype"], c["d_model"]
+    g = torch.Generator().manual_seed(c["seed"])
+    H, KVH, Dh = p.nhead, p.kv_heads, p.head_dim
+    w = lambda o, i: (torch.randn(o, i, generator=g) * 0.02).to(dtype)  # noqa: E731
+    return {"x": torch.randn(B, S, D, generator=g).to(dtype),
+            "wq": w(H * Dh, D), "wk": w(KVH * Dh, D), "wv": w(KVH * Dh, D), "wo": w(D, H * Dh),
+            "qn": (1 + 0.1 * torch.randn(Dh, generator=g)).to(dtype),
+            "kn": (1 + 0.1 * torch.randn(Dh, generator=g)).to(dtype)}
+
+
+def qwen_config(c):
+    """The HF Qwen3-MoE config of a qwen case (eager attention)."""
+    from transformers import Qwen3MoeConfig
+    p = c["params"]
+    cfg = Qwen3MoeConfig(hidden_size=c["d_model"], num_attention_heads=p.nhead, num_key_value_heads=p.kv_heads,
+                         head_dim=p.head_dim, num_hidden_layers=1, num_experts=4, num_experts_per_tok=2,
+                         rms_norm_eps=1e-6, rope_theta=p.theta, attention_bias=False,
+                         max_position_embeddings=max(4096, c["S"]))
+    cfg._attn_implementation = "eager"
+    return cfg
+
+
+def load_qwen_weights(attn, inp):
+    with torch.no_grad():
+        attn.q_proj.weight.copy_(inp["wq"])
+        attn.k_proj.weight.copy_(inp["wk"])
+        attn.v_proj.weight.copy_(inp["wv"])
+        attn.o_proj.weight.copy_(inp["wo"])
+        attn.q_norm.weight.copy_(inp["qn"])
+        attn.k_norm.weight.copy_(inp["kn"])
+
+
+def qwen_schedule(c):
+    """(lo, hi) blocks of a qwen case's forward calls."""
+    blocks = [(0, c["prefix"])]
+    s = c["prefix"]
+    while s < c["S"]:
+        blocks.append((s, min(s + c["block"], c["S"])))
+        s = blocks[-1][1]
+    return blocks
+
+
 def load_module_weights(m, inp):
     with torch.no_grad():
         m.q_proj.weight.copy_(inp["wq"])
@@ -123,5 +175,6 @@ def load(name):
     return torch.load(fixture_path(name), weights_only=False)
 
 
-__all__ = ["CASES", "case", "make_inputs", "make_module_inputs", "output_rows", "checksum", "load",
+__all__ = ["CASES", "case", "make_inputs", "make_module_inputs", "make_qwen_inputs", "qwen_config",
+           "load_qwen_weights", "qwen_schedule", "output_rows", "checksum", "load",
            "rope_apply", "math"]

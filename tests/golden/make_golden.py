@@ -36,6 +36,9 @@ def _import_reference(ref_root: str):
     from KvRouter import ChunkRouter, RouterConfig, VramKVCacheStore, RamKVCacheStore  # type: ignore
     from KvRouter.cache_store import ChunkPlacementPolicy  # type: ignore
     import HierarchicalGlobalAttentionRouted as hgar  # type: ignore
+    sys.path.insert(0, os.path.join(eft, "Qwen3LongContext"))
+    import qwen_routed_attention as qra  # type: ignore
+    hgar.__qwen__ = qra
     return vec, ChunkRouter, RouterConfig, VramKVCacheStore, RamKVCacheStore, ChunkPlacementPolicy, hgar
 
 
@@ -186,6 +189,37 @@ def run_module_case(ref, case):
             "out": out[:, rows].clone()}
 
 
+def run_qwen_case(ref, case):
+    """The reference's QwenRoutedAttention over HF Qwen3MoeAttention on the case's schedule."""
+    import types
+    from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeAttention, Qwen3MoeRotaryEmbedding
+    qra = ref[-1].__qwen__
+    p = case["params"]
+    inp = cases.make_qwen_inputs(case)
+    cfg = cases.qwen_config(case)
+    attn = Qwen3MoeAttention(cfg, layer_idx=0).to(inp["x"].dtype).eval()
+    cases.load_qwen_weights(attn, inp)
+    rot = Qwen3MoeRotaryEmbedding(cfg)
+    x = inp["x"]
+    S = x.shape[1]
+    pos = torch.arange(S).unsqueeze(0)
+    cos, sin = rot(x, pos)
+    w = qra.QwenRoutedAttention(attn, cfg, keep_first=p.keep_first, keep_last=p.keep_last,
+                                topk_chunks=p.topk_chunks, topk_groups=p.topk_groups, chunk_size=p.chunk_size,
+                                group_size=p.group_size)
+    pkv = types.SimpleNamespace()
+    outs = []
+    with torch.no_grad():
+        for lo, hi in cases.qwen_schedule(case):
+            o, _ = w(x[:, lo:hi], position_embeddings=(cos[:, lo:hi], sin[:, lo:hi]), attention_mask=None,
+                     past_key_values=pkv, position_ids=pos[:, lo:hi])
+            outs.append(o)
+    out = torch.cat(outs, dim=1)
+    rows = cases.output_rows(case, S)
+    return {"name": case["name"], "input_checksum": cases.checksum(inp), "out_rows": rows,
+            "out": out[:, rows].clone()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("HGA_REFERENCE_ROOT", "/root/reference"))
@@ -198,7 +232,7 @@ def main():
             continue
         kind = case["kind"]
         fn = {"prefill": run_prefill_case, "summary": run_summary_case,
-              "incremental": run_incremental_case, "module": run_module_case}[kind]
+              "incremental": run_incremental_case, "module": run_module_case, "qwen": run_qwen_case}[kind]
         gold = fn(ref, case)
         path = os.path.join(HERE, f"{case['name']}.pt")
         torch.save(gold, path)

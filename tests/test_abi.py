@@ -63,3 +63,40 @@ def test_module_fails_loudly_on_cpu():
     m = hga.HierarchicalGlobalAttentionRouted(d_model=64, nhead=4, kv_heads=2)
     with pytest.raises(Exception, match="CUDA"):
         m(torch.randn(1, 130, 64))
+
+
+def test_qwen_patch_host_side():
+    """rope theta from both HF config styles; replace/restore bookkeeping (no kernels run)."""
+    import types
+    import torch.nn as nn
+    from hierarchicalglobalattention_b200.qwen import (QwenRoutedAttention, replace_qwen_attention_with_router,
+                                                       restore_original_attention, rope_theta_of)
+    assert rope_theta_of(types.SimpleNamespace(rope_parameters={"rope_theta": 5e5})) == 5e5
+    assert rope_theta_of(types.SimpleNamespace(rope_theta=1e4)) == 1e4
+    assert rope_theta_of(types.SimpleNamespace()) == 1e6
+    cfg = types.SimpleNamespace(num_attention_heads=4, num_key_value_heads=2, head_dim=16, hidden_size=64,
+                                num_hidden_layers=2, rope_parameters={"rope_theta": 1e4})
+
+    class Attn(nn.Module):
+        def __init__(self, i):
+            super().__init__()
+            self.layer_idx = i
+            self.q_proj, self.k_proj = nn.Linear(64, 64, bias=False), nn.Linear(64, 32, bias=False)
+            self.v_proj, self.o_proj = nn.Linear(64, 32, bias=False), nn.Linear(64, 64, bias=False)
+
+    model = nn.Module()
+    model.config = cfg
+    model.model = nn.Module()
+    model.model.layers = nn.ModuleList()
+    for i in range(2):
+        layer = nn.Module()
+        layer.self_attn = Attn(i)
+        model.model.layers.append(layer)
+    n_params = sum(p.numel() for p in model.parameters())
+    assert replace_qwen_attention_with_router(model, topk_chunks=3) == 2
+    assert replace_qwen_attention_with_router(model, topk_chunks=3) == 2          # idempotent
+    w = model.model.layers[1].self_attn
+    assert isinstance(w, QwenRoutedAttention) and w.layer_idx == 1 and w._cfg.theta == 1e4
+    assert sum(p.numel() for p in model.parameters()) == n_params                 # no new parameters
+    assert restore_original_attention(model) == 2
+    assert isinstance(model.model.layers[0].self_attn, Attn)

@@ -30,7 +30,7 @@ def _sets_from_gold(g, C, M, B, H, N):
 def test_summaries_match_reference(name):
     c, g = cases.case(name), cases.load(name)
     inp = cases.make_inputs(c)
-    assert cases.checksum(inp) == pytest.approx(g["input_checksum"], rel=1e-9)
+    assert cases.checksum(inp) == pytest.approx(g["input_checksum"], rel=1e-6)
     ck, gk, _ = O.summaries_prefill(c["params"], inp["k_raw"], inp["k_rope"], inp["v"], inp["cos"], inp["sin"])
     assert torch.equal(ck, g["chunk_k"]) and torch.equal(gk, g["group_k"])
 
@@ -41,7 +41,7 @@ def test_prefill_routing_and_output_match_reference(name):
     c, g = cases.case(name), cases.load(name)
     p, S = c["params"], c["S"]
     inp = cases.make_inputs(c)
-    assert cases.checksum(inp) == pytest.approx(g["input_checksum"], rel=1e-9)
+    assert cases.checksum(inp) == pytest.approx(g["input_checksum"], rel=1e-6)
     ck, gk, _ = O.summaries_prefill(p, inp["k_raw"], inp["k_rope"], inp["v"], inp["cos"], inp["sin"])
     r = O.route_prefill(p, inp["q"], ck, gk, S)
     B, H = inp["q"].shape[:2]
@@ -72,7 +72,7 @@ def test_incremental_decode_matches_reference(name):
     """Block-by-block decode (chunk_router.py:279-442) with its closed-chunk summaries."""
     c, g = cases.case(name), cases.load(name)
     inp = cases.make_inputs(c)
-    assert cases.checksum(inp) == pytest.approx(g["input_checksum"], rel=1e-9)
+    assert cases.checksum(inp) == pytest.approx(g["input_checksum"], rel=1e-6)
     out, blocks = O.decode_sequence(c["params"], inp["q"], inp["k_rope"], inp["k_raw"], inp["v"], c["block"])
     n = g["store_chunk_k"].shape[2]
     ck, _, _ = O.summaries_store(c["params"], inp["k_raw"], inp["k_rope"], inp["v"])
