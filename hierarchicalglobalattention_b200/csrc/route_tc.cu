@@ -23,6 +23,7 @@ constexpr int kThreads = 192;
 
 struct Args {
   int S, H, KVH, N, Kc, Kg, Kgr, keep_first, keep_last, q_layout;
+  int NP;  // per-head length of the pooled / t0 / flag arrays: max(N, Kc * M) (reused by level 2)
   int64_t sum_cap;
   float scale;
   const __nv_bfloat16* group_k;
@@ -107,11 +108,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   constexpr int C = 64, M = 4;
   const int row0 = n * C;
   const int nvalid = (a.S - row0) < C ? (a.S - row0) : C;
-  const int N = a.N;
-  uint32_t* pooled = reinterpret_cast<uint32_t*>(smem + L::kFixed);     // [2][N]
-  uint32_t* t0c = pooled + 2 * N;                                        // [2][N]
-  unsigned char* flags = reinterpret_cast<unsigned char*>(t0c + 2 * N);  // [2][N]
-  Misc* ms = reinterpret_cast<Misc*>(flags + ((2 * N + 15) & ~15));
+  const int N = a.N, NP = a.NP;
+  uint32_t* pooled = reinterpret_cast<uint32_t*>(smem + L::kFixed);      // [2][NP]
+  uint32_t* t0c = pooled + 2 * NP;                                        // [2][NP]
+  unsigned char* flags = reinterpret_cast<unsigned char*>(t0c + 2 * NP);  // [2][NP]
+  Misc* ms = reinterpret_cast<Misc*>(flags + ((2 * NP + 15) & ~15));
   volatile int* abort_flag = &ms->abort;
   uint64_t* q_full = ms->bars + 0;
   uint64_t* ck_full = ms->bars + 1;   // [2]
@@ -151,8 +152,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     ms->abort = 0;
   }
   for (int i = tid; i < 2 * npool; i += kThreads) {
-    pooled[(i / npool) * N + i % npool] = 0u;
-    t0c[(i / npool) * N + i % npool] = 0xffffffffu;
+    pooled[(i / npool) * NP + i % npool] = 0u;
+    t0c[(i / npool) * NP + i % npool] = 0xffffffffu;
   }
   for (int i = tid; i < 2 * 128; i += kThreads) {
     ms->gpool[i / 128][i % 128] = 0u;
@@ -261,8 +262,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int j = 0; j < KL; ++j) {
         if (j < k1 && lst[j] != 0u) {
           const int c = 0xffff - (int)(lst[j] & 0xffffu);
-          atomicMax(&pooled[hs * N + c], lst[j] >> 16);
-          atomicMin(&t0c[hs * N + c], (uint32_t)t);
+          atomicMax(&pooled[hs * NP + c], lst[j] >> 16);
+          atomicMin(&t0c[hs * NP + c], (uint32_t)t);
         }
       }
     }
@@ -272,8 +273,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   // ================================ chunk choice (one warp per head) ==========================
   if (warp == 2 || warp == 3) {
     const int hs = warp - 2;
-    uint32_t* keys = pooled + hs * N;
-    unsigned char* fl = flags + hs * N;
+    uint32_t* keys = pooled + hs * NP;
+    unsigned char* fl = flags + hs * NP;
     for (int c = lane; c < npool; c += 32) keys[c] = keys[c] ? ((keys[c] << 16) | (0xffffu - c)) : 0u;
     __syncwarp();
     warp_select_u32(keys, npool, a.Kc, fl);
@@ -297,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (lane == 0) fl[pr] = 1;
       }
       __syncwarp();
-      if (lane == 0) t0c[hs * N + pr] = 0;
+      if (lane == 0) t0c[hs * NP + pr] = 0;
       __syncwarp();
     }
     int k = 0;
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const unsigned bal = __ballot_sync(0xffffffffu, s);
       if (s) {
         const int slot = k + __popc(bal & ((1u << lane) - 1u));
-        const int t0 = (int)t0c[hs * N + c];
+        const int t0 = (int)t0c[hs * NP + c];
         ms->sel[hs][slot] = pool_lo + c;
         ms->selt0[hs][slot] = t0;
         a.sel_chunk[o + slot] = pool_lo + c;
@@ -422,8 +423,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (warp == 2 || warp == 3) {
       const int hs = warp - 2;
       const int th = 4 * ms->ksel[hs];
-      unsigned char* fl = flags + hs * N;
-      uint32_t* keys = pooled + hs * N;  // reused as 32-bit unique keys of the groups
+      unsigned char* fl = flags + hs * NP;
+      uint32_t* keys = pooled + hs * NP;  // reused as 32-bit unique keys of the groups
       for (int j = lane; j < th; j += 32) {
         const uint32_t g = ms->gpool[hs][j];
         keys[j] = (ms->gt0[hs][j] != 0xffffffffu) ? ((g << 16) | (0xffffu - j)) : 0u;
@@ -496,11 +497,13 @@ cudaError_t launch_route_tc(const hga_params& p, int64_t S, const void* q, int q
   }
   rtc::Args a;
   a.S = (int)S; a.H = p.nhead; a.KVH = p.kv_heads; a.N = N; a.Kc = Kc; a.Kg = Kg; a.Kgr = Kgr;
+  const int NP = N > Tg ? N : Tg;
+  a.NP = NP;
   a.keep_first = p.keep_first; a.keep_last = p.keep_last; a.q_layout = q_layout; a.sum_cap = sum_cap;
   a.scale = p.scale; a.group_k = (const __nv_bfloat16*)gk;
   a.sel_chunk = sel_chunk; a.sel_t0 = sel_t0; a.open_gid = open_gid; a.open_t0 = open_t0;
   a.dbg_l1 = dbg1; a.dbg_l2 = dbg2;
-  const int smem = rtc::L::kFixed + 2 * N * 4 * 2 + ((2 * N + 15) & ~15) + (int)sizeof(rtc::Misc) + 1024;
+  const int smem = rtc::L::kFixed + 2 * NP * 4 * 2 + ((2 * NP + 15) & ~15) + (int)sizeof(rtc::Misc) + 1024;
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
   dim3 grid(N, p.nhead / 2, p.batch);
   cudaError_t e;

@@ -68,3 +68,22 @@ def test_tc_router_matches_portable_router_on_its_scores(cuda):
     eq &= (r1["open_gid"] == r2["open_gid"]).all(-1) & (r1["open_t0"] == r2["open_t0"]).all(-1)
     assert bool(eq[same].all())
     assert same.float().mean().item() > 0.5
+
+
+@pytest.mark.parametrize("S,H,KVH,kf,kl,tc_,tg", [(700, 4, 1, 1, 1, 3, 4), (600, 2, 1, 0, 0, 3, 6), (200, 2, 1, 0, 1, 3, 12)])
+def test_tc_router_is_deterministic_when_groups_outnumber_chunks(cuda, S, H, KVH, kf, kl, tc_, tg):
+    """Level 2 reuses the level-1 per-chunk arrays for topk_chunks * M group keys, which can exceed
+    the number of chunks on short sequences; repeated calls must give identical lists."""
+    from hierarchicalglobalattention_b200 import _lib, ops
+    p = O.OracleParams(nhead=H, kv_heads=KVH, head_dim=128, chunk_size=64, group_size=16, topk_chunks=tc_,
+                       topk_groups=tg, keep_first=kf, keep_last=kl, theta=1e6)
+    c = dict(dtype=torch.bfloat16, seed=5, B=1, S=S, params=p)
+    inp = {k: v.to(cuda) for k, v in cases.make_inputs(c).items()}
+    hp = _lib.make_params(batch=1, nhead=H, kv_heads=KVH, head_dim=128, chunk_size=64, group_size=16,
+                          topk_chunks=tc_, topk_groups=tg, keep_first=kf, keep_last=kl, theta=1e6,
+                          dtype=torch.bfloat16)
+    ck, gk, _ = ops.summaries(hp, inp["k_raw"], inp["k_rope"], inp["v"], inp["cos"], inp["sin"])
+    runs = [ops.route_prefill(hp, inp["q"], ck, gk, impl=2) for _ in range(6)]
+    for r in runs:
+        for k in r:
+            assert torch.equal(r[k], runs[0][k]), k
