@@ -10,11 +10,11 @@ cudaError_t launch_summaries(const hga_params& p, int64_t S, int64_t pos0, const
                              const void* v, int64_t kv_cap, const void* cos, const void* sin, int rot_dtype,
                              int64_t rot_row0, void* ck, void* gk, void* gv, int64_t sum_cap, int64_t out_chunk0,
                              cudaStream_t st);
-cudaError_t launch_route_prefill(const hga_params& p, int64_t S, const void* q, int q_layout, const void* ck,
+cudaError_t launch_route_prefill(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout, const void* ck,
                                  const void* gk, int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0,
                                  int32_t* open_gid, int32_t* open_t0, float* dbg1, float* dbg2, cudaStream_t st,
                                  int* smem_bytes_out);
-cudaError_t launch_attend_simt(const hga_params& p, int64_t S, const void* q, int q_layout, const void* k_rope,
+cudaError_t launch_attend_simt(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout, const void* k_rope,
                                const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0,
                                int Kg, void* out, int out_layout, cudaStream_t st);
 cudaError_t launch_prologue(const hga_params& p, int64_t S, const void* qkv, int64_t row_stride, const void* qw,
@@ -22,13 +22,13 @@ cudaError_t launch_prologue(const hga_params& p, int64_t S, const void* qkv, int
                             int rope_mode, int64_t rot_row0, int64_t pos0, void* q_out, void* kraw_out,
                             void* krope_out, void* v_out, int64_t kv_cap, int64_t kv_row0, cudaStream_t st);
 bool attend_tc_supported(const hga_params& p);
-cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const void* q, int q_layout, const void* k_rope,
+cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout, const void* k_rope,
                              const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0,
                              int Kg, void* out, int out_layout, cudaStream_t st);
 int tc_error_status(bool clear);
 int route_tc_error_status(bool clear);
 bool route_tc_supported(const hga_params& p, int64_t S);
-cudaError_t launch_route_tc(const hga_params& p, int64_t S, const void* q, int q_layout, const void* ck, const void* gk,
+cudaError_t launch_route_tc(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout, const void* ck, const void* gk,
                             int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid, int32_t* open_t0,
                             float* dbg1, float* dbg2, cudaStream_t st);
 cudaError_t launch_route_decode(const hga_params& p, int L, const void* q, const int32_t* seq_pos, const void* ck,
@@ -104,6 +104,15 @@ int hga_route_prefill_impl(const hga_params* p, int64_t seq_len, const void* q, 
                            int32_t* open_gid, int32_t* open_t0, float* dbg_l1, float* dbg_l2, int32_t impl,
                            cudaStream_t stream);
 
+int hga_route_prefill_range(const hga_params* p, int64_t seq_len, int64_t chunk_lo, int64_t chunk_hi, const void* q,
+                            int32_t q_layout, const void* chunk_k, const void* group_k, int64_t sum_cap,
+                            int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid, int32_t* open_t0, float* dbg_l1,
+                            float* dbg_l2, int32_t impl, cudaStream_t stream);
+int hga_attend_prefill_range(const hga_params* p, int64_t seq_len, int64_t chunk_lo, int64_t chunk_hi, const void* q,
+                             int32_t q_layout, const void* k_rope, const void* v, int64_t kv_cap,
+                             const int32_t* open_gid, const int32_t* open_t0, void* out, int32_t out_layout,
+                             int32_t impl, cudaStream_t stream);
+
 const char* hga_version(void) { return "hga_b200 0.1 (sm_100a)"; }
 const char* hga_last_error(void) { return g_err; }
 
@@ -142,6 +151,18 @@ int hga_route_prefill_impl(const hga_params* p, int64_t seq_len, const void* q, 
   int rc = check_params(p);
   if (rc) return rc;
   if (seq_len <= 0) return HGA_OK;
+  const int64_t N = (seq_len + p->chunk_size - 1) / p->chunk_size;
+  return hga_route_prefill_range(p, seq_len, 0, N, q, q_layout, chunk_k, group_k, sum_cap, sel_chunk, sel_t0,
+                                 open_gid, open_t0, dbg_l1, dbg_l2, impl, stream);
+}
+
+int hga_route_prefill_range(const hga_params* p, int64_t seq_len, int64_t chunk_lo, int64_t chunk_hi, const void* q,
+                            int32_t q_layout, const void* chunk_k, const void* group_k, int64_t sum_cap,
+                            int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid, int32_t* open_t0, float* dbg_l1,
+                            float* dbg_l2, int32_t impl, cudaStream_t stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (seq_len <= 0) return HGA_OK;
   int Kc, Kg;
   route_sizes(p, seq_len, &Kc, &Kg);
   if (!q || !chunk_k || !group_k) return fail(HGA_E_INVALID, "hga_route_prefill: NULL tensor");
@@ -149,29 +170,45 @@ int hga_route_prefill_impl(const hga_params* p, int64_t seq_len, const void* q, 
     return fail(HGA_E_INVALID, "hga_route_prefill: NULL output list");
   if (q_layout != 0 && q_layout != 1) return fail(HGA_E_INVALID, "q_layout must be 0 or 1");
   const int64_t N = (seq_len + p->chunk_size - 1) / p->chunk_size;
+  if (chunk_lo < 0 || chunk_hi > N || chunk_lo >= chunk_hi)
+    return fail(HGA_E_INVALID, "hga_route_prefill: query chunk range outside [0, N) or empty");
   if (sum_cap < N) return fail(HGA_E_INVALID, "hga_route_prefill: sum_cap < number of chunks");
   if ((int64_t)Kc * (p->chunk_size / p->group_size) > 256)
     return fail(HGA_E_UNSUPPORTED, "hga_route_prefill: topk_chunks * groups_per_chunk > 256");
+  const int64_t row_hi = chunk_hi * p->chunk_size < seq_len ? chunk_hi * p->chunk_size : seq_len;
+  const hga::QRange qr{(int)chunk_lo, (int)(chunk_hi - chunk_lo), row_hi - chunk_lo * p->chunk_size};
   const bool tc_ok = hga::route_tc_supported(*p, seq_len);
   if (impl == 2 && !tc_ok)
     return fail(HGA_E_UNSUPPORTED, "tensor-core router needs bf16, head_dim 128, chunk 64, group 16, topk_chunks <= 32");
   if ((impl == 0 && tc_ok) || impl == 2) {
-    const cudaError_t e = hga::launch_route_tc(*p, seq_len, q, q_layout, chunk_k, group_k, sum_cap, sel_chunk, sel_t0,
-                                               open_gid, open_t0, dbg_l1, dbg_l2, stream);
+    const cudaError_t e = hga::launch_route_tc(*p, seq_len, qr, q, q_layout, chunk_k, group_k, sum_cap, sel_chunk,
+                                               sel_t0, open_gid, open_t0, dbg_l1, dbg_l2, stream);
     if (!(impl == 0 && (e == cudaErrorMisalignedAddress || e == cudaErrorInvalidConfiguration)))
       return cuda_status(e, "hga_route_prefill(tcgen05)");
     (void)cudaGetLastError();
   }
   if (impl != 0 && impl != 1) return fail(HGA_E_INVALID, "impl must be 0, 1 or 2");
   int smem = 0;
-  return cuda_status(hga::launch_route_prefill(*p, seq_len, q, q_layout, chunk_k, group_k, sum_cap, sel_chunk, sel_t0,
-                                               open_gid, open_t0, dbg_l1, dbg_l2, stream, &smem),
+  return cuda_status(hga::launch_route_prefill(*p, seq_len, qr, q, q_layout, chunk_k, group_k, sum_cap, sel_chunk,
+                                               sel_t0, open_gid, open_t0, dbg_l1, dbg_l2, stream, &smem),
                      "hga_route_prefill");
 }
 
 int hga_attend_prefill(const hga_params* p, int64_t seq_len, const void* q, int32_t q_layout, const void* k_rope,
                        const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0, void* out,
                        int32_t out_layout, int32_t impl, cudaStream_t stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (seq_len <= 0) return HGA_OK;
+  const int64_t N = (seq_len + p->chunk_size - 1) / p->chunk_size;
+  return hga_attend_prefill_range(p, seq_len, 0, N, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, out,
+                                  out_layout, impl, stream);
+}
+
+int hga_attend_prefill_range(const hga_params* p, int64_t seq_len, int64_t chunk_lo, int64_t chunk_hi, const void* q,
+                             int32_t q_layout, const void* k_rope, const void* v, int64_t kv_cap,
+                             const int32_t* open_gid, const int32_t* open_t0, void* out, int32_t out_layout,
+                             int32_t impl, cudaStream_t stream) {
   int rc = check_params(p);
   if (rc) return rc;
   if (seq_len <= 0) return HGA_OK;
@@ -182,12 +219,17 @@ int hga_attend_prefill(const hga_params* p, int64_t seq_len, const void* q, int3
   if (kv_cap < seq_len) return fail(HGA_E_INVALID, "hga_attend_prefill: kv_cap < seq_len");
   if (q_layout != 0 && q_layout != 1) return fail(HGA_E_INVALID, "q_layout must be 0 or 1");
   if (out_layout != 0 && out_layout != 1) return fail(HGA_E_INVALID, "out_layout must be 0 or 1");
+  const int64_t N = (seq_len + p->chunk_size - 1) / p->chunk_size;
+  if (chunk_lo < 0 || chunk_hi > N || chunk_lo >= chunk_hi)
+    return fail(HGA_E_INVALID, "hga_attend_prefill: query chunk range outside [0, N) or empty");
+  const int64_t row_hi = chunk_hi * p->chunk_size < seq_len ? chunk_hi * p->chunk_size : seq_len;
+  const hga::QRange qr{(int)chunk_lo, (int)(chunk_hi - chunk_lo), row_hi - chunk_lo * p->chunk_size};
   const bool tc_ok = hga::attend_tc_supported(*p);
   if (impl == 2 && !tc_ok)
     return fail(HGA_E_UNSUPPORTED, "tensor-core attention needs bf16, head_dim 128, chunk 64, group 16");
   if ((impl == 0 && tc_ok) || impl == 2) {
-    const cudaError_t e = hga::launch_attend_tc(*p, seq_len, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg,
-                                                out, out_layout, stream);
+    const cudaError_t e = hga::launch_attend_tc(*p, seq_len, qr, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0,
+                                                Kg, out, out_layout, stream);
     // windows wider than the tensor-core kernel's unit table (or misaligned pointers) go to the
     // portable kernel when the caller let us choose
     if (!(impl == 0 && (e == cudaErrorNotSupported || e == cudaErrorMisalignedAddress)))
@@ -195,8 +237,8 @@ int hga_attend_prefill(const hga_params* p, int64_t seq_len, const void* q, int3
     (void)cudaGetLastError();
   }
   if (impl != 0 && impl != 1) return fail(HGA_E_INVALID, "impl must be 0, 1 or 2");
-  return cuda_status(hga::launch_attend_simt(*p, seq_len, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg, out,
-                                             out_layout, stream),
+  return cuda_status(hga::launch_attend_simt(*p, seq_len, qr, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg,
+                                             out, out_layout, stream),
                      "hga_attend_prefill");
 }
 

@@ -19,11 +19,12 @@ constexpr int kKeyTile = 32;
 
 template <typename T>
 __global__ void __launch_bounds__(kAttThreads) attend_simt_kernel(
-    hga_params p, int64_t S, const T* __restrict__ q, int q_layout, const T* __restrict__ k_rope,
+    hga_params p, int64_t S, QRange qr, const T* __restrict__ q, int q_layout, const T* __restrict__ k_rope,
     const T* __restrict__ v, int64_t kv_cap, const int32_t* __restrict__ open_gid,
     const int32_t* __restrict__ open_t0, int Kg, int N, T* __restrict__ out, int out_layout) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int ln = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int n = qr.chunk0 + ln;
   const int H = p.nhead, KVH = p.kv_heads, Dh = p.head_dim, C = p.chunk_size, gs = p.group_size;
   const int kvh = h / (H / KVH);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -53,7 +54,7 @@ __global__ void __launch_bounds__(kAttThreads) attend_simt_kernel(
     seg_start[ns] = (int)row0; seg_tmin[ns] = -1; seg_off[ns] = off; off += nvalid; ++ns;
     if (n > l_lo) { seg_start[ns] = l_lo * C; seg_tmin[ns] = 0; seg_off[ns] = off; off += (n - l_lo) * C; ++ns; }
     if (f_hi > 0) { seg_start[ns] = 0; seg_tmin[ns] = 0; seg_off[ns] = off; off += f_hi * C; ++ns; }
-    const size_t tile = ((size_t)b * H + h) * N + n;
+    const size_t tile = ((size_t)b * H + h) * qr.count + ln;
     for (int j = 0; j < Kg; ++j) {
       const int g = open_gid[tile * Kg + j];
       const int t0 = open_t0[tile * Kg + j];
@@ -67,8 +68,9 @@ __global__ void __launch_bounds__(kAttThreads) attend_simt_kernel(
     const int t = i / Dh, d = i % Dh;
     float x = 0.f;
     if (t < nvalid) {
-      const int64_t tt = row0 + t;
-      const T* src = q_layout == 0 ? q + (((int64_t)b * H + h) * S + tt) * Dh : q + (((int64_t)b * S + tt) * H + h) * Dh;
+      const int64_t tt = (int64_t)ln * C + t;  // local q row
+      const T* src = q_layout == 0 ? q + (((int64_t)b * H + h) * qr.sq + tt) * Dh
+                                   : q + (((int64_t)b * qr.sq + tt) * H + h) * Dh;
       x = Num<T>::to_f(src[d]);
     }
     qs[t * ld + d] = x;
@@ -141,8 +143,9 @@ __global__ void __launch_bounds__(kAttThreads) attend_simt_kernel(
   for (int i = tid; i < nvalid * Dh; i += blockDim.x) {
     const int t = i / Dh, d = i % Dh;
     const float val = os[i] / ls[t];
-    const int64_t tt = row0 + t;
-    T* dst = out_layout == 0 ? out + (((int64_t)b * H + h) * S + tt) * Dh : out + (((int64_t)b * S + tt) * H + h) * Dh;
+    const int64_t tt = (int64_t)ln * C + t;  // local output row
+    T* dst = out_layout == 0 ? out + (((int64_t)b * H + h) * qr.sq + tt) * Dh
+                             : out + (((int64_t)b * qr.sq + tt) * H + h) * Dh;
     dst[d] = Num<T>::from_f(val);
   }
 }
@@ -155,7 +158,7 @@ static size_t attend_simt_smem(const hga_params& p, int Kg) {
 }
 
 template <typename T>
-static cudaError_t launch_attend_simt_t(const hga_params& p, int64_t S, const void* q, int q_layout,
+static cudaError_t launch_attend_simt_t(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout,
                                         const void* k_rope, const void* v, int64_t kv_cap,
                                         const int32_t* open_gid, const int32_t* open_t0, int Kg, void* out,
                                         int out_layout, cudaStream_t st) {
@@ -165,24 +168,24 @@ static cudaError_t launch_attend_simt_t(const hga_params& p, int64_t S, const vo
   auto kern = attend_simt_kernel<T>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(N, p.nhead, p.batch);
-  kern<<<grid, kAttThreads, smem, st>>>(p, S, (const T*)q, q_layout, (const T*)k_rope, (const T*)v, kv_cap, open_gid,
+  dim3 grid(qr.count, p.nhead, p.batch);
+  kern<<<grid, kAttThreads, smem, st>>>(p, S, qr, (const T*)q, q_layout, (const T*)k_rope, (const T*)v, kv_cap, open_gid,
                                         open_t0, Kg, N, (T*)out, out_layout);
   return cudaGetLastError();
 }
 
-cudaError_t launch_attend_simt(const hga_params& p, int64_t S, const void* q, int q_layout, const void* k_rope,
+cudaError_t launch_attend_simt(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout, const void* k_rope,
                                const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0,
                                int Kg, void* out, int out_layout, cudaStream_t st) {
   switch (p.dtype) {
     case HGA_DTYPE_F32:
-      return launch_attend_simt_t<float>(p, S, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg, out,
+      return launch_attend_simt_t<float>(p, S, qr, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg, out,
                                          out_layout, st);
     case HGA_DTYPE_BF16:
-      return launch_attend_simt_t<__nv_bfloat16>(p, S, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg,
+      return launch_attend_simt_t<__nv_bfloat16>(p, S, qr, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg,
                                                  out, out_layout, st);
     case HGA_DTYPE_F16:
-      return launch_attend_simt_t<__half>(p, S, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg, out,
+      return launch_attend_simt_t<__half>(p, S, qr, q, q_layout, k_rope, v, kv_cap, open_gid, open_t0, Kg, out,
                                           out_layout, st);
   }
   return cudaErrorInvalidValue;

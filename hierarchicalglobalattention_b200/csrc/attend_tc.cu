@@ -51,6 +51,7 @@ struct SmemLayout {
 
 struct Args {
   int S, H, KVH, N, Kg, keep_first, keep_last, out_layout, q_layout;
+  int chunk0, nl, sq;  // query chunks [chunk0, chunk0 + nl); q / out hold sq rows per batch entry
   int64_t kv_cap;
   float scale_log2;
   const int32_t* open_gid;
@@ -74,12 +75,14 @@ __global__ void __launch_bounds__(kThreads, 2)
                      const __grid_constant__ CUtensorMap tm_v, const Args a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  const int n = blockIdx.x, hp = blockIdx.y, b = blockIdx.z;
+  const int ln = blockIdx.x, hp = blockIdx.y, b = blockIdx.z;
+  const int n = a.chunk0 + ln;
   const int h0 = 2 * hp, h1 = h0 + 1;
   const int kvh = h0 / (a.H / a.KVH);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int C = 64, gs = 16;
-  const int row0 = n * C;
+  const int row0 = n * C;       // absolute first row (keys, causality)
+  const int lrow0 = ln * C;     // first row in q / out
   const int nvalid = (a.S - row0) < C ? (a.S - row0) : C;
 
   Unit* units = reinterpret_cast<Unit*>(smem + SmemLayout::kUnits);
@@ -126,8 +129,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   // stage both heads' open lists in smem (coalesced); visible entries are a prefix of each list
-  const size_t tile0 = (((size_t)b * a.H + h0) * a.N + n) * a.Kg;
-  const size_t tile1 = (((size_t)b * a.H + h1) * a.N + n) * a.Kg;
+  const size_t tile0 = (((size_t)b * a.H + h0) * a.nl + ln) * a.Kg;
+  const size_t tile1 = (((size_t)b * a.H + h1) * a.nl + ln) * a.Kg;
   for (int i = tid; i < a.Kg; i += kThreads) {
     gidA[i] = a.open_gid[tile0 + i];
     t0A[i] = a.open_t0[tile0 + i];
@@ -221,8 +224,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int hh = 0; hh < 2; ++hh)
         for (int kb = 0; kb < 2; ++kb) {
           unsigned char* dst = q_s + kb * 16384 + hh * 8192;
-          if (a.q_layout == 1) tma_load_3d(dst, &tm_q, kb * 64, h0 + hh, b * a.S + row0, q_full);
-          else tma_load_2d(dst, &tm_q, kb * 64, (b * a.H + h0 + hh) * a.S + row0, q_full);
+          if (a.q_layout == 1) tma_load_3d(dst, &tm_q, kb * 64, h0 + hh, b * a.sq + lrow0, q_full);
+          else tma_load_2d(dst, &tm_q, kb * 64, (b * a.H + h0 + hh) * a.sq + lrow0, q_full);
         }
       const int64_t kvrow = ((int64_t)b * a.KVH + kvh) * a.kv_cap;
       for (int i = 0; i < ntiles; ++i) {
@@ -392,9 +395,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t o_addr = tmem + lane_addr + kColO;
       __nv_bfloat16* dst = nullptr;
       if (rvalid) {
-        const int64_t tt = row0 + t;
-        dst = a.out_layout == 1 ? a.out + (((int64_t)b * a.S + tt) * a.H + h) * 128
-                                : a.out + (((int64_t)b * a.H + h) * a.S + tt) * 128;
+        const int64_t tt = lrow0 + t;
+        dst = a.out_layout == 1 ? a.out + (((int64_t)b * a.sq + tt) * a.H + h) * 128
+                                : a.out + (((int64_t)b * a.H + h) * a.sq + tt) * 128;
       }
       for (int c0 = 0; c0 < 128; c0 += 32) {
         uint32_t o[32];
@@ -427,7 +430,7 @@ bool attend_tc_supported(const hga_params& p) {
          (p.nhead / p.kv_heads) % 2 == 0 && p.keep_last <= 1 << 20 && p.keep_first <= 1 << 20;
 }
 
-cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const void* q, int q_layout, const void* k_rope,
+cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout, const void* k_rope,
                              const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0, int Kg,
                              void* out, int out_layout, cudaStream_t st) {
   using namespace tc;
@@ -443,17 +446,18 @@ cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const void* q, int 
   const cuuint32_t bkv[2] = {64, 16};
   if (!make_map(&mk, k_rope, 2, dkv, skv, bkv) || !make_map(&mv, v, 2, dkv, skv, bkv)) return cudaErrorInvalidValue;
   if (q_layout == 1) {
-    const cuuint64_t dq[3] = {128, (cuuint64_t)p.nhead, (cuuint64_t)(p.batch * S)};
+    const cuuint64_t dq[3] = {128, (cuuint64_t)p.nhead, (cuuint64_t)(p.batch * qr.sq)};
     const cuuint64_t sq[2] = {256, (cuuint64_t)p.nhead * 256};
     const cuuint32_t bq[3] = {64, 1, 64};
     if (!make_map(&mq, q, 3, dq, sq, bq)) return cudaErrorInvalidValue;
   } else {
-    const cuuint64_t dq[2] = {128, (cuuint64_t)p.batch * p.nhead * S};
+    const cuuint64_t dq[2] = {128, (cuuint64_t)p.batch * p.nhead * qr.sq};
     const cuuint64_t sq[1] = {256};
     const cuuint32_t bq[2] = {64, 64};
     if (!make_map(&mq, q, 2, dq, sq, bq)) return cudaErrorInvalidValue;
   }
   Args a;
+  a.chunk0 = qr.chunk0; a.nl = qr.count; a.sq = (int)qr.sq;
   a.S = (int)S; a.H = p.nhead; a.KVH = p.kv_heads; a.N = N; a.Kg = Kg;
   a.keep_first = p.keep_first; a.keep_last = p.keep_last; a.out_layout = out_layout; a.q_layout = q_layout;
   a.kv_cap = kv_cap;
@@ -463,7 +467,7 @@ cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const void* q, int 
   const int smem = SmemLayout::kTotal + 1024;
   cudaError_t e = cudaFuncSetAttribute(attend_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(N, p.nhead / 2, p.batch);
+  dim3 grid(qr.count, p.nhead / 2, p.batch);
   attend_tc_kernel<<<grid, kThreads, smem, st>>>(mq, mk, mv, a);
   return cudaGetLastError();
 }

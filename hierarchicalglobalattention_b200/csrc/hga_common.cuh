@@ -56,6 +56,16 @@ __device__ __forceinline__ uint32_t rank_idx(unsigned long long k) {
 }
 __device__ __forceinline__ float rank_score(unsigned long long k) { return unord_f32((uint32_t)(k >> 32)); }
 
+// The query chunks one prefill launch processes: chunks [chunk0, chunk0 + count) of a sequence of
+// S tokens.  q and the per-chunk outputs hold only those chunks (rows, tiles) — sq query rows per
+// batch entry, local chunk i = chunk chunk0 + i — while keys, summaries and all routing rules use
+// the absolute chunk index.  A whole-sequence launch is {0, N, S}.
+struct QRange {
+  int chunk0;
+  int count;
+  int64_t sq;
+};
+
 // Windows of query chunk n (vectorized.py:242-253; chunk_placement_policy.py:27-38).
 __host__ __device__ __forceinline__ void windows(int n, int keep_first, int keep_last, int& f_hi, int& l_lo) {
   int kf = keep_first > 0 ? keep_first : 0;

@@ -67,12 +67,13 @@ __device__ __forceinline__ const T* q_row_ptr(const T* q, int q_layout, int b, i
 
 template <typename T>
 __global__ void __launch_bounds__(kRouteThreads) route_prefill_kernel(
-    hga_params p, int64_t S, const T* __restrict__ q, int q_layout, const T* __restrict__ chunk_k,
+    hga_params p, int64_t S, QRange qr, const T* __restrict__ q, int q_layout, const T* __restrict__ chunk_k,
     const T* __restrict__ group_k, int64_t sum_cap, int N, int Kc, int Kg, int Kgr, int nsub,
     int32_t* __restrict__ sel_chunk, int32_t* __restrict__ sel_t0, int32_t* __restrict__ open_gid,
     int32_t* __restrict__ open_t0, float* __restrict__ dbg_l1, float* __restrict__ dbg_l2) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int ln = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int n = qr.chunk0 + ln;
   const int H = p.nhead, KVH = p.kv_heads, Dh = p.head_dim, C = p.chunk_size, M = C / p.group_size;
   const int kvh = h / (H / KVH);
   const int tid = threadIdx.x;
@@ -94,7 +95,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_prefill_kernel(
   int* red = (int*)(smem + L.red);
   const int ldq = Dh + 2;
 
-  const size_t tile_out = (((size_t)b * H + h) * N + n);
+  const size_t tile_out = (((size_t)b * H + h) * qr.count + ln);
   // default outputs: empty lists
   for (int i = tid; i < Kc; i += blockDim.x) {
     sel_chunk[tile_out * Kc + i] = -1;
@@ -117,7 +118,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_prefill_kernel(
   for (int i = tid; i < C * Dh; i += blockDim.x) {
     const int t = i / Dh, d = i % Dh;
     T x = Num<T>::from_f(0.f);
-    if (t < nvalid) x = q_row_ptr(q, q_layout, b, h, row0 + t, H, S, Dh)[d];
+    if (t < nvalid) x = q_row_ptr(q, q_layout, b, h, (int64_t)ln * C + t, H, qr.sq, Dh)[d];
     qs[t * ldq + d] = x;
   }
   for (int i = tid; i < npool; i += blockDim.x) {
@@ -286,7 +287,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_prefill_kernel(
 }
 
 template <typename T>
-static cudaError_t launch_route_t(const hga_params& p, int64_t S, const void* q, int q_layout,
+static cudaError_t launch_route_t(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout,
                                   const void* ck, const void* gk, int64_t sum_cap, int32_t* sel_chunk,
                                   int32_t* sel_t0, int32_t* open_gid, int32_t* open_t0, float* dbg1,
                                   float* dbg2, cudaStream_t st, int* smem_bytes_out) {
@@ -307,26 +308,26 @@ static cudaError_t launch_route_t(const hga_params& p, int64_t S, const void* q,
   auto kern = route_prefill_kernel<T>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
   if (e != cudaSuccess) return e;
-  dim3 grid(N, p.nhead, p.batch);
-  kern<<<grid, kRouteThreads, L.total, st>>>(p, S, (const T*)q, q_layout, (const T*)ck, (const T*)gk, sum_cap, N,
+  dim3 grid(qr.count, p.nhead, p.batch);
+  kern<<<grid, kRouteThreads, L.total, st>>>(p, S, qr, (const T*)q, q_layout, (const T*)ck, (const T*)gk, sum_cap, N,
                                              Kc, Kg, Kgr, nsub, sel_chunk, sel_t0, open_gid, open_t0, dbg1,
                                              dbg2);
   return cudaGetLastError();
 }
 
-cudaError_t launch_route_prefill(const hga_params& p, int64_t S, const void* q, int q_layout, const void* ck,
+cudaError_t launch_route_prefill(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout, const void* ck,
                                  const void* gk, int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0,
                                  int32_t* open_gid, int32_t* open_t0, float* dbg1, float* dbg2,
                                  cudaStream_t st, int* smem_bytes_out) {
   switch (p.dtype) {
     case HGA_DTYPE_F32:
-      return launch_route_t<float>(p, S, q, q_layout, ck, gk, sum_cap, sel_chunk, sel_t0, open_gid, open_t0,
+      return launch_route_t<float>(p, S, qr, q, q_layout, ck, gk, sum_cap, sel_chunk, sel_t0, open_gid, open_t0,
                                    dbg1, dbg2, st, smem_bytes_out);
     case HGA_DTYPE_BF16:
-      return launch_route_t<__nv_bfloat16>(p, S, q, q_layout, ck, gk, sum_cap, sel_chunk, sel_t0, open_gid,
+      return launch_route_t<__nv_bfloat16>(p, S, qr, q, q_layout, ck, gk, sum_cap, sel_chunk, sel_t0, open_gid,
                                            open_t0, dbg1, dbg2, st, smem_bytes_out);
     case HGA_DTYPE_F16:
-      return launch_route_t<__half>(p, S, q, q_layout, ck, gk, sum_cap, sel_chunk, sel_t0, open_gid, open_t0,
+      return launch_route_t<__half>(p, S, qr, q, q_layout, ck, gk, sum_cap, sel_chunk, sel_t0, open_gid, open_t0,
                                     dbg1, dbg2, st, smem_bytes_out);
   }
   return cudaErrorInvalidValue;

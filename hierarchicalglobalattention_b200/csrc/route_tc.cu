@@ -23,6 +23,7 @@ constexpr int kThreads = 192;
 
 struct Args {
   int S, H, KVH, N, Kc, Kg, Kgr, keep_first, keep_last, q_layout;
+  int chunk0, nl, sq;  // query chunks [chunk0, chunk0 + nl); q and the lists hold only those
   int NP;  // per-head length of the pooled / t0 / flag arrays: max(N, Kc * M) (reused by level 2)
   int64_t sum_cap;
   float scale;
@@ -101,7 +102,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     route_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ck, const Args a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  const int n = blockIdx.x, hp = blockIdx.y, b = blockIdx.z;
+  const int ln = blockIdx.x, hp = blockIdx.y, b = blockIdx.z;
+  const int n = a.chunk0 + ln;
   const int h0 = 2 * hp;
   const int kvh = h0 / (a.H / a.KVH);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -124,8 +126,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   int f_hi, l_lo;
   windows(n, a.keep_first, a.keep_last, f_hi, l_lo);
   const int pool_lo = f_hi, npool = l_lo > f_hi ? l_lo - f_hi : 0;
-  const size_t out0 = (((size_t)b * a.H + h0) * N + n);
-  const size_t out1 = out0 + N;  // head h0+1
+  const size_t out0 = (((size_t)b * a.H + h0) * a.nl + ln);
+  const size_t out1 = out0 + a.nl;  // head h0+1
   for (int i = tid; i < 2 * a.Kc; i += kThreads) {
     const size_t o = (i < a.Kc ? out0 : out1) * a.Kc + (i % a.Kc);
     a.sel_chunk[o] = -1;
@@ -178,8 +180,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int hh = 0; hh < 2; ++hh)
         for (int kb = 0; kb < 2; ++kb) {
           unsigned char* dst = q_s + kb * 16384 + hh * 8192;
-          if (a.q_layout == 1) tma_load_3d(dst, &tm_q, kb * 64, h0 + hh, b * a.S + row0, q_full);
-          else tma_load_2d(dst, &tm_q, kb * 64, (b * a.H + h0 + hh) * a.S + row0, q_full);
+          if (a.q_layout == 1) tma_load_3d(dst, &tm_q, kb * 64, h0 + hh, b * a.sq + ln * C, q_full);
+          else tma_load_2d(dst, &tm_q, kb * 64, (b * a.H + h0 + hh) * a.sq + ln * C, q_full);
         }
       const int64_t ckrow = ((int64_t)b * a.KVH + kvh) * a.sum_cap + pool_lo;
       for (int i = 0; i < ntile; ++i) {
@@ -468,7 +470,7 @@ bool route_tc_supported(const hga_params& p, int64_t S) {
          (p.nhead / p.kv_heads) % 2 == 0 && Kc <= 32 && N < 65536 && S * p.batch < (1ll << 31);
 }
 
-cudaError_t launch_route_tc(const hga_params& p, int64_t S, const void* q, int q_layout, const void* ck, const void* gk,
+cudaError_t launch_route_tc(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout, const void* ck, const void* gk,
                             int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid, int32_t* open_t0,
                             float* dbg1, float* dbg2, cudaStream_t st) {
   using namespace tc;
@@ -485,17 +487,18 @@ cudaError_t launch_route_tc(const hga_params& p, int64_t S, const void* q, int q
   const cuuint32_t bck[2] = {64, 128};
   if (!make_map(&mck, ck, 2, dck, sck, bck)) return cudaErrorInvalidValue;
   if (q_layout == 1) {
-    const cuuint64_t dq[3] = {128, (cuuint64_t)p.nhead, (cuuint64_t)(p.batch * S)};
+    const cuuint64_t dq[3] = {128, (cuuint64_t)p.nhead, (cuuint64_t)(p.batch * qr.sq)};
     const cuuint64_t sq[2] = {256, (cuuint64_t)p.nhead * 256};
     const cuuint32_t bq[3] = {64, 1, 64};
     if (!make_map(&mq, q, 3, dq, sq, bq)) return cudaErrorInvalidValue;
   } else {
-    const cuuint64_t dq[2] = {128, (cuuint64_t)p.batch * p.nhead * S};
+    const cuuint64_t dq[2] = {128, (cuuint64_t)p.batch * p.nhead * qr.sq};
     const cuuint64_t sq[1] = {256};
     const cuuint32_t bq[2] = {64, 64};
     if (!make_map(&mq, q, 2, dq, sq, bq)) return cudaErrorInvalidValue;
   }
   rtc::Args a;
+  a.chunk0 = qr.chunk0; a.nl = qr.count; a.sq = (int)qr.sq;
   a.S = (int)S; a.H = p.nhead; a.KVH = p.kv_heads; a.N = N; a.Kc = Kc; a.Kg = Kg; a.Kgr = Kgr;
   const int NP = N > Tg ? N : Tg;
   a.NP = NP;
@@ -505,7 +508,7 @@ cudaError_t launch_route_tc(const hga_params& p, int64_t S, const void* q, int q
   a.dbg_l1 = dbg1; a.dbg_l2 = dbg2;
   const int smem = rtc::L::kFixed + 2 * NP * 4 * 2 + ((2 * NP + 15) & ~15) + (int)sizeof(rtc::Misc) + 1024;
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
-  dim3 grid(N, p.nhead / 2, p.batch);
+  dim3 grid(qr.count, p.nhead / 2, p.batch);
   cudaError_t e;
   if (Kc <= 16) {
     e = cudaFuncSetAttribute(rtc::route_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -104,57 +104,67 @@ def ctypes_params(p: HgaParams):
 
 
 def route_prefill(p: HgaParams, q: torch.Tensor, chunk_k: torch.Tensor, group_k: torch.Tensor,
-                  seq_len: Optional[int] = None, debug: bool = False, impl: int = 0) -> Dict[str, torch.Tensor]:
+                  seq_len: Optional[int] = None, debug: bool = False, impl: int = 0,
+                  chunk_range: Optional[Tuple[int, int]] = None) -> Dict[str, torch.Tensor]:
     """Two-level prefill routing (see hga_route_prefill_impl).  q [B,H,S,Dh] (or a BSHD view).
-    impl: 0 auto, 1 portable SIMT router, 2 tcgen05 router."""
+    impl: 0 auto, 1 portable SIMT router, 2 tcgen05 router.  ``chunk_range=(lo, hi)`` routes only
+    query chunks [lo, hi) of a ``seq_len``-token sequence: q then holds just those chunks' rows and
+    the lists are [B,H,hi-lo,K] (hga_route_prefill_range)."""
     _require_cuda(q, chunk_k, group_k)
     B, H, S, Dh = q.shape
     S = S if seq_len is None else seq_len
     N, Kc, Kg, _ = route_sizes(p, S)
+    lo, hi = (0, N) if chunk_range is None else chunk_range
+    NL = hi - lo
     dev = q.device
     C = p.chunk_size
     M = C // p.group_size
     res = {
-        "sel_chunk": torch.empty(B, H, N, Kc, device=dev, dtype=torch.int32),
-        "sel_t0": torch.empty(B, H, N, Kc, device=dev, dtype=torch.int32),
-        "open_gid": torch.empty(B, H, N, Kg, device=dev, dtype=torch.int32),
-        "open_t0": torch.empty(B, H, N, Kg, device=dev, dtype=torch.int32),
+        "sel_chunk": torch.empty(B, H, NL, Kc, device=dev, dtype=torch.int32),
+        "sel_t0": torch.empty(B, H, NL, Kc, device=dev, dtype=torch.int32),
+        "open_gid": torch.empty(B, H, NL, Kg, device=dev, dtype=torch.int32),
+        "open_t0": torch.empty(B, H, NL, Kg, device=dev, dtype=torch.int32),
     }
     if debug:
-        res["dbg_l1"] = torch.full((B, H, N, C, N), float("nan"), device=dev, dtype=torch.float32)
-        res["dbg_l2"] = torch.full((B, H, N, C, Kc * M), float("nan"), device=dev, dtype=torch.float32)
+        res["dbg_l1"] = torch.full((B, H, NL, C, N), float("nan"), device=dev, dtype=torch.float32)
+        res["dbg_l2"] = torch.full((B, H, NL, C, Kc * M), float("nan"), device=dev, dtype=torch.float32)
     sum_cap = chunk_k.stride(1) // Dh
     if (chunk_k.stride(-1) != 1 or chunk_k.stride(2) != Dh or group_k.stride(-1) != 1
             or group_k.stride(1) != sum_cap * M * Dh or chunk_k.stride(0) != chunk_k.shape[1] * chunk_k.stride(1)):
         raise _lib.HgaError("summaries must be row-slices of contiguous [B,KVH,cap,(M,)Dh] buffers")
     q, q_layout = q_view(q)
-    check(lib().hga_route_prefill_impl(ctypes_params(p), S, ptr(q), q_layout, ptr(chunk_k), ptr(group_k),
-                                       sum_cap, ptr(res["sel_chunk"]), ptr(res["sel_t0"]), ptr(res["open_gid"]),
-                                       ptr(res["open_t0"]), ptr(res.get("dbg_l1")), ptr(res.get("dbg_l2")), impl,
-                                       stream_ptr(dev)), "hga_route_prefill")
+    check(lib().hga_route_prefill_range(ctypes_params(p), S, lo, hi, ptr(q), q_layout, ptr(chunk_k), ptr(group_k),
+                                        sum_cap, ptr(res["sel_chunk"]), ptr(res["sel_t0"]), ptr(res["open_gid"]),
+                                        ptr(res["open_t0"]), ptr(res.get("dbg_l1")), ptr(res.get("dbg_l2")), impl,
+                                        stream_ptr(dev)), "hga_route_prefill")
     return res
 
 
 def attend_prefill(p: HgaParams, q: torch.Tensor, k_rope: torch.Tensor, v: torch.Tensor,
                    open_gid: torch.Tensor, open_t0: torch.Tensor, seq_len: Optional[int] = None,
-                   out_layout: int = Q_BSHD, impl: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                   out_layout: int = Q_BSHD, impl: int = 0, out: Optional[torch.Tensor] = None,
+                   chunk_range: Optional[Tuple[int, int]] = None) -> torch.Tensor:
     """Working-set attention (see hga_attend_prefill).  Returns [B,H,S,Dh] (a view of a BSHD
-    buffer when out_layout == 1)."""
+    buffer when out_layout == 1).  ``chunk_range=(lo, hi)`` attends only query chunks [lo, hi) of
+    a ``seq_len``-token sequence (q, lists and out hold just those chunks; hga_attend_prefill_range)."""
     _require_cuda(q, k_rope, v, open_gid, open_t0)
-    B, H, S, Dh = q.shape
-    S = S if seq_len is None else seq_len
+    B, H, SQ, Dh = q.shape
+    S = SQ if seq_len is None else seq_len
+    C = p.chunk_size
+    lo, hi = (0, (S + C - 1) // C) if chunk_range is None else chunk_range
+    SQ = min(S, hi * C) - lo * C
     cap = kv_cap_of(k_rope)
     if kv_cap_of(v) != cap:
         raise _lib.HgaError("k_rope and v must share one capacity layout")
     if out is None:
         if out_layout == Q_BSHD:
-            out = torch.empty(B, S, H, Dh, device=q.device, dtype=q.dtype)
+            out = torch.empty(B, SQ, H, Dh, device=q.device, dtype=q.dtype)
         else:
-            out = torch.empty(B, H, S, Dh, device=q.device, dtype=q.dtype)
+            out = torch.empty(B, H, SQ, Dh, device=q.device, dtype=q.dtype)
     q, q_layout = q_view(q)
-    check(lib().hga_attend_prefill(ctypes_params(p), S, ptr(q), q_layout, ptr(k_rope), ptr(v), cap,
-                                   ptr(open_gid), ptr(open_t0), ptr(out), out_layout, impl, stream_ptr(q.device)),
-          "hga_attend_prefill")
+    check(lib().hga_attend_prefill_range(ctypes_params(p), S, lo, hi, ptr(q), q_layout, ptr(k_rope), ptr(v), cap,
+                                         ptr(open_gid), ptr(open_t0), ptr(out), out_layout, impl,
+                                         stream_ptr(q.device)), "hga_attend_prefill")
     return out.transpose(1, 2) if out_layout == Q_BSHD else out
 
 

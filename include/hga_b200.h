@@ -103,6 +103,22 @@ int hga_attend_prefill(const hga_params* p, int64_t seq_len, const void* q, int3
                        const int32_t* open_gid, const int32_t* open_t0,
                        void* out, int32_t out_layout, int32_t impl, cudaStream_t stream);
 
+/* Query-chunk ranges of the two prefill steps (the unit a multi-GPU prefill shards): routing /
+ * attention of query chunks [chunk_lo, chunk_hi) of a sequence of seq_len tokens, whose keys,
+ * summaries and K/V rows cover the whole prefix [0, seq_len).  q holds only the range's rows
+ * (sq = min(seq_len, chunk_hi*C) - chunk_lo*C rows per batch entry, same layouts as above); the
+ * routing lists are [B, H, chunk_hi - chunk_lo, K] and out holds the range's sq rows.  No
+ * counterpart in the reference, which routes a whole block on one device; each chunk's result
+ * equals that of the whole-sequence calls. */
+int hga_route_prefill_range(const hga_params* p, int64_t seq_len, int64_t chunk_lo, int64_t chunk_hi,
+                            const void* q, int32_t q_layout, const void* chunk_k, const void* group_k,
+                            int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0, int32_t* open_gid,
+                            int32_t* open_t0, float* dbg_l1, float* dbg_l2, int32_t impl, cudaStream_t stream);
+int hga_attend_prefill_range(const hga_params* p, int64_t seq_len, int64_t chunk_lo, int64_t chunk_hi,
+                             const void* q, int32_t q_layout, const void* k_rope, const void* v, int64_t kv_cap,
+                             const int32_t* open_gid, const int32_t* open_t0, void* out, int32_t out_layout,
+                             int32_t impl, cudaStream_t stream);
+
 /* Projection epilogue of the routed module: q/k RMSNorm + RoPE + KV-store layout in one pass.
  * Replaces the eager prologue of HierarchicalGlobalAttentionRouted.forward
  * (HierarchicalGlobalAttentionRouted.py:151-157) and QwenRoutedAttention.forward
