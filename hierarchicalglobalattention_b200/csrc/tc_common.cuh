@@ -1,5 +1,5 @@
 // PTX helpers shared by the tcgen05 / TMA kernels (sm_100a): mbarriers with bounded waits,
-// TMA tile loads (no cluster multicast anywhere), UMMA descriptors, tcgen05 MMA / TMEM access,
+// TMA tile loads (each CTA loads its own tiles), UMMA descriptors, tcgen05 MMA / TMEM access,
 // tensor-map encoding through the driver entry point.
 #pragma once
 
