@@ -9,11 +9,11 @@ independent once every rank holds the whole sequence's summaries and K/V
   1. projects its own token rows (fused QKV GEMM) and runs the q/k RMSNorm + RoPE prologue, writing
      its K (RoPE'd) and V rows straight into its slice of a flat send buffer;
   2. builds the routing summaries of its own chunks into the same send buffer;
-  3. one all-gather of the send buffers (K, V, chunk_k, group_k: group V summaries are not read by
-     the token-only path) over NCCL, then one permuting copy per tensor into the [B, KVH, S, Dh]
-     row layout the kernels address;
-  4. routes and attends its own chunks (hga_route_prefill_range / hga_attend_prefill_range) and
-     applies o_proj to its rows.
+  3. all-gathers the routing summaries (chunk_k, group_k; group V summaries are not read by the
+     token-only path) over NCCL and routes its own chunks (hga_route_prefill_range) while a second,
+     asynchronous all-gather moves the K / V rows; each gathered tensor is put into the
+     [B, KVH, S, Dh] row layout the kernels address by one permuting copy;
+  4. attends its own chunks (hga_attend_prefill_range) and applies o_proj to its rows.
 
 Partition: rank r owns chunks [r*P, min((r+1)*P, N)), P = ceil(N / world) — equal row counts, so
 the all-gather needs no size exchange and the unpack is one strided copy per tensor.  The output
@@ -40,7 +40,8 @@ def prefill_partition(seq_len: int, chunk_size: int, world: int) -> List[Tuple[i
 
 @dataclass
 class ShardLayout:
-    """Element layout of one rank's send buffer: K rows, V rows, chunk_k, group_k (model dtype)."""
+    """Element layout of one rank's send buffer: [chunk_k | group_k] (the routing part, gathered
+    first) then [K rows | V rows] (the attention part, gathered while the router runs)."""
     B: int
     KVH: int
     Dh: int
@@ -50,63 +51,79 @@ class ShardLayout:
     dtype: torch.dtype
 
     @property
-    def elems(self) -> Tuple[int, int, int, int]:
-        kv = self.B * self.KVH * self.rows * self.Dh
-        ck = self.B * self.KVH * self.chunks * self.Dh
-        return kv, kv, ck, ck * self.M
+    def sum_numel(self) -> int:
+        return self.B * self.KVH * self.chunks * self.Dh * (1 + self.M)
+
+    @property
+    def kv_numel(self) -> int:
+        return 2 * self.B * self.KVH * self.rows * self.Dh
 
     @property
     def numel(self) -> int:
-        return sum(self.elems)
+        return self.sum_numel + self.kv_numel
 
     def views(self, flat: torch.Tensor):
-        """(k_rope [B,KVH,rows,Dh], v, chunk_k [B,KVH,chunks,Dh], group_k [B,KVH,chunks,M,Dh]) views."""
-        a, b, c, d = self.elems
-        shapes = ((self.B, self.KVH, self.rows, self.Dh), (self.B, self.KVH, self.rows, self.Dh),
-                  (self.B, self.KVH, self.chunks, self.Dh), (self.B, self.KVH, self.chunks, self.M, self.Dh))
+        """(chunk_k [B,KVH,chunks,Dh], group_k [B,KVH,chunks,M,Dh], k_rope [B,KVH,rows,Dh], v) views."""
+        ck = self.B * self.KVH * self.chunks * self.Dh
+        kv = self.B * self.KVH * self.rows * self.Dh
+        shapes = ((self.B, self.KVH, self.chunks, self.Dh), (self.B, self.KVH, self.chunks, self.M, self.Dh),
+                  (self.B, self.KVH, self.rows, self.Dh), (self.B, self.KVH, self.rows, self.Dh))
         out, o = [], 0
-        for n, shape in zip((a, b, c, d), shapes):
+        for n, shape in zip((ck, ck * self.M, kv, kv), shapes):
             out.append(flat[o:o + n].view(shape))
             o += n
         return tuple(out)
 
 
-def unpack_gathered(lay: ShardLayout, recv: torch.Tensor, world: int, k_rope: torch.Tensor, v: torch.Tensor,
-                    chunk_k: torch.Tensor, group_k: torch.Tensor) -> None:
-    """Scatter the all-gathered buffers [world * numel] into whole-sequence tensors
-    (k_rope / v [B,KVH,world*rows,Dh], chunk_k [B,KVH,world*chunks,Dh], group_k [...,M,Dh]):
-    one permuting copy per tensor (rank r's rows land at r*rows)."""
-    B, KVH, Dh, M = lay.B, lay.KVH, lay.Dh, lay.M
-    stacked = recv.view(world, lay.numel)
-    a, b, c, d = lay.elems
-    offs = [0, a, a + b, a + b + c, a + b + c + d]
-    shapes = [(lay.rows, Dh), (lay.rows, Dh), (lay.chunks, Dh), (lay.chunks, M * Dh)]
-    for i, dst in enumerate((k_rope, v, chunk_k, group_k)):
-        src = stacked[:, offs[i]:offs[i + 1]].view(world, B, KVH, *shapes[i])
-        dst.view(B, KVH, world, *shapes[i]).copy_(src.permute(1, 2, 0, 3, 4))
+def _scatter(stacked: torch.Tensor, world: int, parts) -> None:
+    """stacked [world, part elements...]: copy part i of every rank into dst_i (rank-major rows)."""
+    o = 0
+    for dst, n, shape in parts:
+        src = stacked[:, o:o + n].view(world, *shape[:2], *shape[2:])
+        B, KVH = shape[:2]
+        dst.view(B, KVH, world, *shape[2:]).copy_(src.permute(1, 2, 0, 3, 4))
+        o += n
+
+
+def unpack_summaries(lay: ShardLayout, recv: torch.Tensor, world: int, chunk_k: torch.Tensor,
+                     group_k: torch.Tensor) -> None:
+    """Gathered routing parts [world * sum_numel] -> chunk_k [B,KVH,world*chunks,Dh] and group_k
+    [B,KVH,world*chunks,M,Dh] (rank r's chunks land at r*chunks)."""
+    ck = lay.B * lay.KVH * lay.chunks * lay.Dh
+    _scatter(recv.view(world, lay.sum_numel), world,
+             [(chunk_k, ck, (lay.B, lay.KVH, lay.chunks, lay.Dh)),
+              (group_k, ck * lay.M, (lay.B, lay.KVH, lay.chunks, lay.M * lay.Dh))])
+
+
+def unpack_kv(lay: ShardLayout, recv: torch.Tensor, world: int, k_rope: torch.Tensor, v: torch.Tensor) -> None:
+    """Gathered attention parts [world * kv_numel] -> k_rope / v [B,KVH,world*rows,Dh]."""
+    kv = lay.B * lay.KVH * lay.rows * lay.Dh
+    shape = (lay.B, lay.KVH, lay.rows, lay.Dh)
+    _scatter(recv.view(world, lay.kv_numel), world, [(k_rope, kv, shape), (v, kv, shape)])
 
 
 class ShardedPrefill:
     """Sharded prefill of ``HierarchicalGlobalAttentionRouted`` layers over ``world`` ranks.
 
-    ``exchange(send) -> recv`` performs the all-gather (default: ``torch.distributed`` on the
-    default group: ``all_gather_into_tensor`` over NCCL); tests substitute an in-process exchange.
-    Buffers are kept between calls of the same shape.
+    ``exchange(send) -> recv`` replaces the collective (tests emulate the ranks in one process);
+    by default the routing parts are all-gathered first and the K/V parts are all-gathered
+    asynchronously over NCCL while the router runs.  Buffers are kept between calls of the same
+    shape.
     """
 
     def __init__(self, world: int, rank: int, exchange: Optional[Callable[[torch.Tensor], torch.Tensor]] = None):
         self.world, self.rank = world, rank
-        self.exchange = exchange if exchange is not None else self._dist_exchange
+        self.exchange = exchange
         self._bufs = {}
 
-    def _dist_exchange(self, send: torch.Tensor) -> torch.Tensor:
+    def _gather(self, name, send: torch.Tensor, async_op: bool):
         import torch.distributed as dist
-        recv = self._buf("recv", (self.world * send.numel(),), send.dtype, send.device)
+        recv = self._buf(name, (self.world * send.numel(),), send.dtype, send.device)
         if dist.get_backend() == "nccl":
-            dist.all_gather_into_tensor(recv, send)
+            h = dist.all_gather_into_tensor(recv, send, async_op=async_op)
         else:
-            dist.all_gather(list(recv.view(self.world, -1).unbind(0)), send)
-        return recv
+            h = dist.all_gather(list(recv.view(self.world, -1).unbind(0)), send, async_op=async_op)
+        return recv, h
 
     def _buf(self, name, shape, dtype, device, zero=False):
         key = (name, tuple(shape), dtype, str(device))
@@ -129,7 +146,7 @@ class ShardedPrefill:
         dev = x_local.device
         # zero-filled once: rows past the sequence end stay finite (the kernels stream whole units)
         send = self._buf("send", (lay.numel,), x_local.dtype, dev, zero=True)
-        kr_s, v_s, ck_s, gk_s = lay.views(send)
+        ck_s, gk_s, kr_s, v_s = lay.views(send)
         hp = m._cfg.hga_params(m._policy, B, x_local.dtype)
         state = {"lay": lay, "lo": lo, "hi": hi, "hp": hp, "S": seq_len}
         if hi <= lo:
@@ -151,32 +168,44 @@ class ShardedPrefill:
         state["q"] = q
         return state, send
 
-    def global_phase(self, m, state, recv: torch.Tensor) -> Optional[torch.Tensor]:
-        """Steps 3-4: unpack the gathered K/V and summaries, route + attend own chunks, o_proj.
-        Returns this rank's output rows [B, SQ, d_model] (None for a rank with no chunks)."""
+    def global_phase(self, m, state, recv_sum: torch.Tensor, recv_kv: torch.Tensor, kv_handle=None):
+        """Steps 3-4: unpack the gathered summaries, route own chunks, (wait for the K/V gather)
+        unpack K/V, attend, o_proj.  Returns this rank's output rows [B, SQ, d_model] (None for a
+        rank with no chunks)."""
         lay = state["lay"]
-        dev = recv.device
+        dev = recv_sum.device
         W = self.world
         rows, chunks = W * lay.rows, W * lay.chunks
-        k_rope = self._buf("k_rope", (lay.B, lay.KVH, rows, lay.Dh), lay.dtype, dev)
-        v = self._buf("v", (lay.B, lay.KVH, rows, lay.Dh), lay.dtype, dev)
         ck = self._buf("ck", (lay.B, lay.KVH, chunks, lay.Dh), lay.dtype, dev)
         gk = self._buf("gk", (lay.B, lay.KVH, chunks, lay.M, lay.Dh), lay.dtype, dev)
-        unpack_gathered(lay, recv, W, k_rope, v, ck, gk)
+        unpack_summaries(lay, recv_sum, W, ck, gk)
         lo, hi = state["lo"], state["hi"]
-        if hi <= lo:
+        routing = None
+        if hi > lo:
+            routing = ops.route_prefill(state["hp"], state["q"], ck, gk, seq_len=state["S"], chunk_range=(lo, hi))
+        if kv_handle is not None:
+            kv_handle.wait()
+        k_rope = self._buf("k_rope", (lay.B, lay.KVH, rows, lay.Dh), lay.dtype, dev)
+        v = self._buf("v", (lay.B, lay.KVH, rows, lay.Dh), lay.dtype, dev)
+        unpack_kv(lay, recv_kv, W, k_rope, v)
+        if routing is None:
             return None
-        S, hp, q = state["S"], state["hp"], state["q"]
-        routing = ops.route_prefill(hp, q, ck, gk, seq_len=S, chunk_range=(lo, hi))
-        out_heads = ops.attend_prefill(hp, q, k_rope, v, routing["open_gid"], routing["open_t0"], seq_len=S,
-                                       chunk_range=(lo, hi))            # [B,H,SQ,Dh] view of [B,SQ,H,Dh]
+        q = state["q"]
+        out_heads = ops.attend_prefill(state["hp"], q, k_rope, v, routing["open_gid"], routing["open_t0"],
+                                       seq_len=state["S"], chunk_range=(lo, hi))   # [B,H,SQ,Dh] of [B,SQ,H,Dh]
         B, SQ = q.shape[0], q.shape[2]
         return m.o_proj(out_heads.transpose(1, 2).reshape(B, SQ, m.nhead * m.head_dim))
 
     def forward(self, m, x_local: torch.Tensor, seq_len: int) -> Optional[torch.Tensor]:
         state, send = self.local_phase(m, x_local, seq_len)
-        recv = self.exchange(send)
-        return self.global_phase(m, state, recv)
+        lay = state["lay"]
+        if self.exchange is not None:
+            recv = self.exchange(send).view(self.world, lay.numel)
+            return self.global_phase(m, state, recv[:, :lay.sum_numel].contiguous(),
+                                     recv[:, lay.sum_numel:].contiguous())
+        recv_sum, _ = self._gather("recv_sum", send[:lay.sum_numel], async_op=False)
+        recv_kv, h = self._gather("recv_kv", send[lay.sum_numel:], async_op=True)
+        return self.global_phase(m, state, recv_sum, recv_kv, h)
 
 
-__all__ = ["ShardedPrefill", "ShardLayout", "prefill_partition", "unpack_gathered"]
+__all__ = ["ShardedPrefill", "ShardLayout", "prefill_partition", "unpack_summaries", "unpack_kv"]

@@ -29,8 +29,10 @@ def emulate(m, x, S, W):
         st, send = shards[r].local_phase(m, x[:, lo * 64:min(S, hi * 64)], S)
         states.append(st)
         sends.append(send.clone())
-    recv = torch.cat(sends)
-    return [shards[r].global_phase(m, states[r], recv) for r in range(W)]
+    lay = states[0]["lay"]
+    recv = torch.stack(sends)
+    rs, rk = recv[:, :lay.sum_numel].contiguous().view(-1), recv[:, lay.sum_numel:].contiguous().view(-1)
+    return [shards[r].global_phase(m, states[r], rs, rk) for r in range(W)]
 
 
 @pytest.mark.parametrize("S,W", [(1000, 3), (4096, 8), (2048, 2), (200, 8)])

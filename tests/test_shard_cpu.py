@@ -7,7 +7,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from hierarchicalglobalattention_b200.shard import ShardedPrefill, ShardLayout, prefill_partition, unpack_gathered
+from hierarchicalglobalattention_b200.shard import ShardedPrefill, ShardLayout, prefill_partition, unpack_kv, unpack_summaries
 
 
 def test_partition_covers_every_chunk_once():
@@ -31,19 +31,24 @@ def _worker(rank, world, port, out):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         lay = ShardLayout(B=2, KVH=3, Dh=4, M=2, rows=8, chunks=2, dtype=torch.float32)
-        recv = ShardedPrefill(world, rank).exchange(_fill(lay, rank))
-        k = torch.empty(lay.B, lay.KVH, world * lay.rows, lay.Dh)
-        v = torch.empty_like(k)
+        sp = ShardedPrefill(world, rank)
+        send = _fill(lay, rank)
+        rs, _ = sp._gather("rs", send[:lay.sum_numel], async_op=False)
+        rk, h = sp._gather("rk", send[lay.sum_numel:], async_op=True)
+        h.wait()
         ck = torch.empty(lay.B, lay.KVH, world * lay.chunks, lay.Dh)
         gk = torch.empty(lay.B, lay.KVH, world * lay.chunks, lay.M, lay.Dh)
-        unpack_gathered(lay, recv, world, k, v, ck, gk)
+        k = torch.empty(lay.B, lay.KVH, world * lay.rows, lay.Dh)
+        v = torch.empty_like(k)
+        unpack_summaries(lay, rs, world, ck, gk)
+        unpack_kv(lay, rk, world, k, v)
         ok = True
         for r in range(world):
             ref = lay.views(_fill(lay, r))
-            ok &= torch.equal(k[:, :, r * lay.rows:(r + 1) * lay.rows], ref[0])
-            ok &= torch.equal(v[:, :, r * lay.rows:(r + 1) * lay.rows], ref[1])
-            ok &= torch.equal(ck[:, :, r * lay.chunks:(r + 1) * lay.chunks], ref[2])
-            ok &= torch.equal(gk[:, :, r * lay.chunks:(r + 1) * lay.chunks], ref[3])
+            ok &= torch.equal(ck[:, :, r * lay.chunks:(r + 1) * lay.chunks], ref[0])
+            ok &= torch.equal(gk[:, :, r * lay.chunks:(r + 1) * lay.chunks], ref[1])
+            ok &= torch.equal(k[:, :, r * lay.rows:(r + 1) * lay.rows], ref[2])
+            ok &= torch.equal(v[:, :, r * lay.rows:(r + 1) * lay.rows], ref[3])
         out[rank] = bool(ok)
     finally:
         dist.destroy_process_group()
