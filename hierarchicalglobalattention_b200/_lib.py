@@ -57,6 +57,7 @@ _SIGNATURES = {
                                                _P, _P, _P, _P, _P, _P, _I32, _P]),
     "hga_attend_prefill_range": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _I64, _I64, _P, _I32, _P, _P, _I64,
                                                 _P, _P, _P, _I32, _I32, _P]),
+    "hga_shard_unpack": (ctypes.c_int, [_P, _I64, _I64, _I32, _I32, _P, _I64, _I64, _I64, _P, _P]),
     "hga_route_decode_impl": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I32, _P, _P, _P, _P, _I64, _I32, _P, _P, _P,
                                              _P, _I32, _P]),
     "hga_attend_decode_impl": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I32, _P, _P, _P, _P, _I64, _I32, _P, _P,

@@ -38,6 +38,9 @@ cudaError_t launch_attend_decode(const hga_params& p, int L, const void* q, cons
                                  const void* hv, int64_t hot_cap, int hot_mode, const void* ckk, const void* cvv,
                                  int64_t cold_cap, const int32_t* og, const int32_t* ot, int Kg, void* out,
                                  cudaStream_t st);
+cudaError_t launch_shard_unpack(const void* recv, int64_t rank_stride, int64_t part_offset, int world, int pieces,
+                                const int32_t* dst_block, int64_t bk, int64_t rows, int64_t row_bytes, void* dst,
+                                cudaStream_t st);
 int decode_error_status(bool clear);
 int decode_fast_error_status(bool clear);
 bool route_decode1_supported(const hga_params& p, int L);
@@ -326,6 +329,23 @@ int hga_append_tokens(const hga_params* p, int32_t L, const int32_t* seq_pos, co
   return cuda_status(hga::launch_append(*p, L, seq_pos, k_rope, v, k_raw, hot_k, hot_v, hot_cap, hot_mode, cold_k,
                                         cold_v, cold_cap, active_raw, stream),
                      "hga_append_tokens");
+}
+
+int hga_shard_unpack(const void* recv, int64_t rank_stride, int64_t part_offset, int32_t world, int32_t pieces,
+                     const int32_t* dst_block, int64_t bk, int64_t rows, int64_t row_bytes, void* dst,
+                     cudaStream_t stream) {
+  if (!recv || !dst || !dst_block) return fail(HGA_E_INVALID, "hga_shard_unpack: NULL pointer");
+  if (world < 1 || pieces < 1 || (int64_t)world * pieces > 128)
+    return fail(HGA_E_INVALID, "hga_shard_unpack: world * pieces must be in [1, 128]");
+  if (bk < 0 || rows < 0 || row_bytes <= 0 || row_bytes % 16 || rank_stride % 16 || part_offset % 16 ||
+      ((uintptr_t)recv | (uintptr_t)dst) & 15)
+    return fail(HGA_E_INVALID, "hga_shard_unpack: rows, strides and pointers must be 16-byte aligned");
+  for (int i = 0; i < world * pieces; ++i)
+    if (dst_block[i] < 0 || dst_block[i] >= world * pieces)
+      return fail(HGA_E_INVALID, "hga_shard_unpack: destination block %d out of range", dst_block[i]);
+  return cuda_status(hga::launch_shard_unpack(recv, rank_stride, part_offset, world, pieces, dst_block, bk, rows,
+                                              row_bytes, dst, stream),
+                     "hga_shard_unpack");
 }
 
 int hga_device_status(int32_t* code, int32_t clear) {

@@ -180,7 +180,7 @@ def qkv_prologue(p: HgaParams, qkv: torch.Tensor, cos: torch.Tensor, sin: torch.
     _require_cuda(qkv, cos, sin)
     B, S, W = qkv.shape
     H, KVH, Dh = p.nhead, p.kv_heads, p.head_dim
-    if qkv.stride(2) != 1 or qkv.stride(0) != S * qkv.stride(1):
+    if qkv.stride(2) != 1 or (B > 1 and qkv.stride(0) != S * qkv.stride(1)):
         raise _lib.HgaError("qkv must be contiguous in its token rows")
     row_stride = qkv.stride(1)
     if W < (H + 2 * KVH) * Dh:
@@ -277,3 +277,15 @@ def append_tokens(p: HgaParams, seq_pos: torch.Tensor, k_rope: torch.Tensor, v: 
                                   ptr(hot_v), kv_cap_of(hot_k), hot_mode, ptr(cold_k), ptr(cold_v),
                                   kv_cap_of(cold_k) if cold_k is not None else 0, ptr(active_raw),
                                   stream_ptr(k_rope.device)), "hga_append_tokens")
+
+
+def shard_unpack(recv: torch.Tensor, rank_stride: int, part_offset: int, world: int, pieces: int,
+                 dst_block, bk: int, rows: int, row_bytes: int, dst: torch.Tensor) -> None:
+    """Scatter one part of an all-gathered multi-GPU prefill buffer into sequence order (see
+    hga_shard_unpack; strides and offsets in bytes, ``dst_block`` a list of world*pieces ints)."""
+    import ctypes
+    _require_cuda(recv, dst)
+    table = (ctypes.c_int32 * len(dst_block))(*dst_block)
+    check(lib().hga_shard_unpack(ptr(recv), rank_stride, part_offset, world, pieces,
+                                 ctypes.cast(table, ctypes.c_void_p), bk, rows, row_bytes,
+                                 ptr(dst), stream_ptr(dst.device)), "hga_shard_unpack")

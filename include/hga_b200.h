@@ -187,6 +187,16 @@ int hga_append_tokens(const hga_params* p, int32_t L, const int32_t* seq_pos, co
                       int32_t hot_mode, void* cold_k, void* cold_v, int64_t cold_cap, void* active_raw,
                       cudaStream_t stream);
 
+/* Unpack of a multi-GPU prefill's all-gathered buffer (no counterpart in the reference, which
+ * runs on one device).  Rank r's data starts at recv + r * rank_stride (bytes); one part of it
+ * starts part_offset bytes further and holds `pieces` blocks of [bk][rows][row_bytes], piece j of
+ * rank r being block dst_block[r * pieces + j] (a host array) of the sequence.  dst receives
+ * [bk][world * pieces][rows][row_bytes].  row_bytes, the strides and both pointers must be 16-byte
+ * aligned; world * pieces <= 128. */
+int hga_shard_unpack(const void* recv, int64_t rank_stride, int64_t part_offset, int32_t world, int32_t pieces,
+                     const int32_t* dst_block, int64_t bk, int64_t rows, int64_t row_bytes, void* dst,
+                     cudaStream_t stream);
+
 /* Device-side error words: 0, or the first code recorded.  The tensor-core kernels record a
  * bounded mbarrier wait that timed out (the CTA then released its TMEM and returned without
  * output); the decode kernels record 0x101 / 0x102 / 0x103 (routing / attention / append) when a

@@ -1,9 +1,11 @@
 """Sharded prefill (query chunks split across ranks, K/V + summaries all-gathered) equals the
 single-device module forward.  The ranks are emulated in one process: every rank's local phase
-runs, the send buffers are concatenated (what the all-gather produces), then every rank's global
-phase runs — no kernel waits on another rank."""
+runs, the send buffers are stacked (what the all-gather produces), then every rank's global phase
+runs — no kernel waits on another rank."""
 import pytest
 import torch
+
+from test_shard_cpu import unpack_reference
 
 pytestmark = pytest.mark.gpu
 
@@ -21,18 +23,27 @@ def _module(dev, d_model=1024, nhead=8, kv_heads=2, head_dim=128, seed=0):
 
 
 def emulate(m, x, S, W):
-    from hierarchicalglobalattention_b200.shard import ShardedPrefill, prefill_partition
-    parts = prefill_partition(S, 64, W)
-    shards = [ShardedPrefill(W, r, exchange=lambda s: s) for r in range(W)]
+    """Output rows of every rank, put back in sequence order."""
+    from hierarchicalglobalattention_b200.shard import ShardedPrefill, rank_rows
+    shards = [ShardedPrefill(W, r) for r in range(W)]
     states, sends = [], []
-    for r, (lo, hi) in enumerate(parts):
-        st, send = shards[r].local_phase(m, x[:, lo * 64:min(S, hi * 64)], S)
+    for r in range(W):
+        pieces = [x[:, lo:hi] for lo, hi in rank_rows(S, 64, W, r)]
+        xr = torch.cat(pieces, dim=1) if pieces else x[:, :0]
+        st, send = shards[r].local_phase(m, xr, S)
         states.append(st)
         sends.append(send.clone())
     lay = states[0]["lay"]
     recv = torch.stack(sends)
     rs, rk = recv[:, :lay.sum_numel].contiguous().view(-1), recv[:, lay.sum_numel:].contiguous().view(-1)
-    return [shards[r].global_phase(m, states[r], rs, rk) for r in range(W)]
+    out = torch.empty(1, S, m.d_model, device=x.device, dtype=x.dtype)
+    for r in range(W):
+        o = shards[r].global_phase(m, states[r], rs, rk)
+        at = 0
+        for lo, hi in rank_rows(S, 64, W, r):
+            out[:, lo:hi] = o[:, at:at + hi - lo]
+            at += hi - lo
+    return out
 
 
 @pytest.mark.parametrize("S,W", [(1000, 3), (4096, 8), (2048, 2), (200, 8)])
@@ -41,11 +52,27 @@ def test_sharded_prefill_equals_single_device(cuda, S, W):
     x = torch.randn(1, S, m.d_model, device=cuda, dtype=torch.bfloat16, generator=torch.Generator(cuda).manual_seed(1))
     with torch.no_grad():
         ref, _ = m(x)
-        outs = emulate(m, x, S, W)
-    out = torch.cat([o for o in outs if o is not None], dim=1)
-    assert out.shape == ref.shape
+        out = emulate(m, x, S, W)
     d = (out.float() - ref.float()).abs()
     # the only difference is the QKV GEMM over a row subset (cuBLAS may pick another tiling), which
     # can move a score across a bf16 rounding boundary: nearly all rows are identical
     assert (d.amax(-1) == 0).float().mean() > 0.9
     assert d.max() < 5e-2
+
+
+@pytest.mark.parametrize("W", [1, 3, 8])
+def test_shard_unpack_kernel_matches_reference(cuda, W):
+    from hierarchicalglobalattention_b200.shard import PIECES, ShardedPrefill, ShardLayout
+    lay = ShardLayout(B=2, KVH=3, Dh=128, M=4, rows=128, chunks=2, dtype=torch.bfloat16)
+    recv = torch.randn(W * lay.numel, device=cuda).to(torch.bfloat16)
+    sp = ShardedPrefill(W, 0)
+    nb = PIECES * W
+    for rank_elems, off, rows, row_elems, base in (
+            (lay.sum_numel, 0, lay.chunks, lay.Dh, "sum"), (lay.sum_numel, lay.ck_numel, lay.chunks, lay.M * lay.Dh, "sum"),
+            (lay.kv_numel, 0, lay.rows, lay.Dh, "kv"), (lay.kv_numel, lay.k_numel, lay.rows, lay.Dh, "kv")):
+        src = recv[:W * rank_elems]
+        got = torch.empty(lay.B * lay.KVH * nb * rows * row_elems, device=cuda, dtype=torch.bfloat16)
+        want = torch.empty_like(got)
+        sp._unpack(lay, src, rank_elems, off, rows, row_elems, got)
+        unpack_reference(lay, src, W, rank_elems, off, rows, row_elems, want)
+        assert torch.equal(got, want)
