@@ -21,6 +21,25 @@ using namespace tc;
 
 constexpr int kThreads = 192;
 
+// Phase timestamps for development builds (-DHGA_ROUTE_PROFILE): thread 0 of the first 4096 CTAs
+// records %globaltimer after each block-wide barrier.  Compiled out otherwise.
+#ifdef HGA_ROUTE_PROFILE
+__device__ unsigned long long g_rprof[4096][16];
+#define HGA_RPROF_W(k)                                                                                \
+  do {                                                                                                \
+    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);              \
+    if ((threadIdx.x & 31) == 0 && cta < 4096) g_rprof[cta][k] = global_ns();                         \
+  } while (0)
+#define HGA_RPROF(k)                                                                                  \
+  do {                                                                                                \
+    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);              \
+    if (threadIdx.x == 0 && cta < 4096) g_rprof[cta][k] = global_ns();                                \
+  } while (0)
+#else
+#define HGA_RPROF(k) do { } while (0)
+#define HGA_RPROF_W(k) do { } while (0)
+#endif
+
 struct Args {
   int S, H, KVH, N, Kc, Kg, Kgr, keep_first, keep_last, q_layout;
   int chunk0, nl, sq;  // query chunks [chunk0, chunk0 + nl); q and the lists hold only those
@@ -34,6 +53,23 @@ struct Args {
 
 __device__ __forceinline__ uint32_t ord16(float s) {  // order-preserving key of a bf16 value, 0 reserved
   const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(s));
+  return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
+}
+
+// Round-to-nearest-even of a finite fp32 value to bf16 precision, on its bit pattern (the
+// definition of IEEE rounding at 8 mantissa bits; scores are never NaN).  Integer ops only: the
+// scoring loop runs it twice per score, and conversion instructions were the loop's bottleneck.
+__device__ __forceinline__ uint32_t round_bf16_bits(uint32_t b) {
+  return (b + 0x7fffu + ((b >> 16) & 1u)) & 0xffff0000u;
+}
+// bits of T(T(acc) * scale): the reference's rounding points for a score (bf16 einsum output,
+// then "* scale" evaluated in fp32 and stored in bf16)
+__device__ __forceinline__ uint32_t bf16_score_bits(uint32_t acc_bits, float scale) {
+  return round_bf16_bits(__float_as_uint(__fmul_rn(__uint_as_float(round_bf16_bits(acc_bits)), scale)));
+}
+// ord16 of a value already rounded to bf16 (its high 16 bits)
+__device__ __forceinline__ uint32_t ord16_bits(uint32_t rounded) {
+  const uint32_t b = rounded >> 16;
   return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
 }
 
@@ -111,6 +147,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int row0 = n * C;
   const int nvalid = (a.S - row0) < C ? (a.S - row0) : C;
   const int N = a.N, NP = a.NP;
+  HGA_RPROF(0);
   uint32_t* pooled = reinterpret_cast<uint32_t*>(smem + L::kFixed);      // [2][NP]
   uint32_t* t0c = pooled + 2 * NP;                                        // [2][NP]
   unsigned char* flags = reinterpret_cast<unsigned char*>(t0c + 2 * NP);  // [2][NP]
@@ -168,6 +205,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   fence_before();
   __syncthreads();
+  HGA_RPROF(1);
   fence_after();
   const uint32_t tmem = ms->tmem;
   unsigned char* q_s = smem + L::kQ;
@@ -221,10 +259,12 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int j = 0; j < KL; ++j) lst[j] = 0u;
     const size_t dbg_row = ((hs ? out1 : out0) * C + t) * (size_t)N + pool_lo;
+    if (warp == 2) HGA_RPROF_W(12);
     for (int i = 0; i < ntile; ++i) {
       const int st = i & 1;
       // tcgen05.ld is warp-collective: keep the branch around it warp-uniform
       if (!__all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 15))) break;
+      if (warp == 2 && i == 0) HGA_RPROF_W(13);
       fence_after();
       const uint32_t sa = tmem + lane_addr + st * 128;
       const int cmax = (npool - 128 * i) < 128 ? (npool - 128 * i) : 128;
@@ -232,30 +272,60 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint32_t r[32];
         HGA_LD32(sa + 32 * c4, r);
         tmem_wait_ld();
-        if (rvalid) {
+        // keys of the 32 columns, and the mask of those above the row's current threshold
+        uint32_t mask = 0u;
+        const uint32_t thr = lst[KL - 1];
 #pragma unroll
-          for (int cc = 0; cc < 32; ++cc) {
-            const int c = 32 * c4 + cc;
-            if (c < cmax) {
-              const float sc = bf16_score(r[cc], a.scale);
-              const uint32_t cr = 128 * i + c;
-              if (a.dbg_l1) a.dbg_l1[dbg_row + cr] = sc;
-              uint32_t x = (ord16(sc) << 16) | (0xffffu - cr);
-              if (x > lst[KL - 1]) {
+        for (int cc = 0; cc < 32; ++cc) {
+          const int c = 32 * c4 + cc;
+          uint32_t key = 0u;
+          if (rvalid && c < cmax) {
+            const uint32_t sb = bf16_score_bits(r[cc], a.scale);
+            const uint32_t cr = 128 * i + c;
+            if (a.dbg_l1) a.dbg_l1[dbg_row + cr] = __uint_as_float(sb);
+            key = (ord16_bits(sb) << 16) | (0xffffu - cr);
+          }
+          r[cc] = key;
+          mask |= (key > thr ? 1u : 0u) << cc;
+        }
+        // insert the candidates lane by lane: the warp loops as often as its busiest lane needs,
+        // not once per column that any lane needs
+        const int rounds = __reduce_max_sync(0xffffffffu, __popc(mask));
+        for (int it = 0; it < rounds; ++it) {
+          uint32_t x = 0u;
+          if (mask) {
+            const int c0 = __ffs(mask) - 1;
+            mask &= mask - 1u;
+            // r[c0] by a 5-level select tree on the bits of c0 (depth 5, not a 32-long chain)
+            uint32_t v16[16], v8[8], v4[4], v2[2];
 #pragma unroll
-                for (int j = 0; j < KL; ++j) {
-                  const uint32_t hi = max(lst[j], x);
-                  x = min(lst[j], x);
-                  lst[j] = hi;
-                }
-              }
+            for (int k = 0; k < 16; ++k) v16[k] = (c0 & 1) ? r[2 * k + 1] : r[2 * k];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v8[k] = (c0 & 2) ? v16[2 * k + 1] : v16[2 * k];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v4[k] = (c0 & 4) ? v8[2 * k + 1] : v8[2 * k];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) v2[k] = (c0 & 8) ? v4[2 * k + 1] : v4[2 * k];
+            x = (c0 & 16) ? v2[1] : v2[0];
+          }
+          if (x > lst[KL - 1]) {
+            // every slot of the descending list is computed from the old list at once (keys
+            // are unique), so the update has no serial dependence chain
+            uint32_t nl[KL];
+#pragma unroll
+            for (int j = 0; j < KL; ++j) {
+              const uint32_t prev_j = j == 0 ? 0xffffffffu : lst[j - 1];
+              nl[j] = lst[j] > x ? lst[j] : (prev_j > x ? x : prev_j);
             }
+#pragma unroll
+            for (int j = 0; j < KL; ++j) lst[j] = nl[j];
           }
         }
       }
       fence_before();
       mbar_arrive(s_free + st);
     }
+    if (warp == 2) HGA_RPROF_W(14);
     // requests = top k1 of the union of the four lists (4-way merge) -> pooled max score and
     // first requesting row per chunk
     const int k1 = a.Kc < npool ? a.Kc : npool;
@@ -271,6 +341,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
   __syncthreads();
+  HGA_RPROF(2);
 
   // ================================ chunk choice (one warp per head) ==========================
   if (warp == 2 || warp == 3) {
@@ -279,7 +350,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     unsigned char* fl = flags + hs * NP;
     for (int c = lane; c < npool; c += 32) keys[c] = keys[c] ? ((keys[c] << 16) | (0xffffu - c)) : 0u;
     __syncwarp();
+    if (hs == 0) HGA_RPROF_W(8);
     warp_select_u32(keys, npool, a.Kc, fl);
+    if (hs == 0) HGA_RPROF_W(9);
     const int prev = n - 1;
     const bool prev_in = n > 0 && prev >= pool_lo && prev < l_lo;
     if (prev_in) {
@@ -303,6 +376,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (lane == 0) t0c[hs * NP + pr] = 0;
       __syncwarp();
     }
+    if (hs == 0) HGA_RPROF_W(10);
     int k = 0;
     const size_t o = (hs ? out1 : out0) * a.Kc;
     for (int base = 0; base < npool; base += 32) {
@@ -320,8 +394,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       k += __popc(bal);
     }
     if (lane == 0) ms->ksel[hs] = k;
+    if (hs == 0) HGA_RPROF_W(11);
   }
   __syncthreads();
+  HGA_RPROF(3);
   const bool do_l2 = a.Kg > 0 && a.Kgr > 0 && !ms->abort;
 
   // ================================ level 2 ===================================================
@@ -342,6 +418,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     fence_before();
     __syncthreads();
+    HGA_RPROF(4);
     fence_after();
     if (warp == 1 && lane == 0) {
       const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((256u >> 3) << 17) | ((128u >> 4) << 24);
@@ -376,9 +453,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint32_t key = 0u;
         if (rvalid && j < th) {
           if (t >= ms->selt0[hs][j >> 2]) {
-            const float s = bf16_score(r[j], a.scale);
-            key = ord16(s);
-            if (a.dbg_l2) a.dbg_l2[dbg_row + j] = s;
+            const uint32_t sb = bf16_score_bits(r[j], a.scale);
+            key = ord16_bits(sb);
+            if (a.dbg_l2) a.dbg_l2[dbg_row + j] = __uint_as_float(sb);
           } else if (a.dbg_l2) {
             a.dbg_l2[dbg_row + j] = kNeg;
           }
@@ -422,6 +499,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
     __syncthreads();
+    HGA_RPROF(5);
     if (warp == 2 || warp == 3) {
       const int hs = warp - 2;
       const int th = 4 * ms->ksel[hs];
@@ -455,6 +533,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   fence_before();
   __syncthreads();
+  HGA_RPROF(6);
   if (warp == 1) {
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
@@ -523,5 +602,11 @@ cudaError_t launch_route_tc(const hga_params& p, int64_t S, const QRange& qr, co
 }
 
 HGA_DEFINE_ERROR_READER(route_tc_error_status)
+
+#ifdef HGA_ROUTE_PROFILE
+extern "C" int hga_route_profile_read(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, rtc::g_rprof, sizeof(rtc::g_rprof)) == cudaSuccess ? 0 : -1;
+}
+#endif
 
 }  // namespace hga
