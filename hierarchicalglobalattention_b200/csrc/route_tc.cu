@@ -113,11 +113,11 @@ __device__ void warp_select_u32(const uint32_t* keys, int n, int k, unsigned cha
     const int mmax = (n + 31) / 32;
     for (int bit = 31; bit >= 0; --bit) {
       const uint32_t cand = T | (1u << bit);
-      int cnt = 0;
+      int c4[4] = {0, 0, 0, 0};  // four partial counts: short dependence chains
 #pragma unroll
       for (int m = 0; m < 64; ++m)
-        if (m < mmax) cnt += kr[m] >= cand;
-      cnt = __reduce_add_sync(0xffffffffu, cnt);
+        if (m < mmax) c4[m & 3] += kr[m] >= cand;
+      const int cnt = __reduce_add_sync(0xffffffffu, c4[0] + c4[1] + c4[2] + c4[3]);
       if (cnt >= k) T = cand;
     }
   } else {
@@ -404,16 +404,34 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (do_l2) {
     // gather the chosen chunks' group summaries: head hs -> rows [hs*128, hs*128 + 4*ksel)
     const __nv_bfloat16* gk = a.group_k + ((size_t)b * a.KVH + kvh) * a.sum_cap * M * 128;
-    for (int pc = tid; pc < 256 * 16; pc += kThreads) {
-      const int rrow = pc >> 4, c16 = pc & 15;
-      const int hs = rrow >> 7, j = rrow & 127;
-      uint4 val = make_uint4(0, 0, 0, 0);
-      if (j < 4 * ms->ksel[hs]) {
-        const int chunk = ms->sel[hs][j >> 2];
-        val = *reinterpret_cast<const uint4*>(gk + ((size_t)chunk * M + (j & 3)) * 128 + c16 * 8);
+    // every thread issues its 16-byte loads in two batches before storing, so the gather costs
+    // two memory round trips instead of one per piece
+    constexpr int kPieces = 256 * 16, kBatch = (kPieces / kThreads + 2) / 2;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint4 vals[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const int pc = tid + (half * kBatch + k) * kThreads;
+        vals[k] = make_uint4(0, 0, 0, 0);
+        if (pc < kPieces) {
+          const int rrow = pc >> 4, c16 = pc & 15;
+          const int hs = rrow >> 7, j = rrow & 127;
+          if (j < 4 * ms->ksel[hs]) {
+            const int chunk = ms->sel[hs][j >> 2];
+            vals[k] = __ldg(reinterpret_cast<const uint4*>(gk + ((size_t)chunk * M + (j & 3)) * 128 + c16 * 8));
+          }
+        }
       }
-      const int kb = c16 >> 3, cc = c16 & 7;
-      *reinterpret_cast<uint4*>(tile_s + kb * 32768 + rrow * 128 + ((cc ^ (rrow & 7)) << 4)) = val;
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const int pc = tid + (half * kBatch + k) * kThreads;
+        if (pc < kPieces) {
+          const int rrow = pc >> 4, c16 = pc & 15;
+          const int kb = c16 >> 3, cc = c16 & 7;
+          *reinterpret_cast<uint4*>(tile_s + kb * 32768 + rrow * 128 + ((cc ^ (rrow & 7)) << 4)) = vals[k];
+        }
+      }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     fence_before();
@@ -472,10 +490,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (active && !all) {
         for (int bit = 15; bit >= 0; --bit) {
           const uint32_t cand = T | (1u << bit);
-          int cnt = 0;
+          int c4[4] = {0, 0, 0, 0};  // four partial counts: short dependence chains
 #pragma unroll
-          for (int j = 0; j < KT; ++j) cnt += r[j] >= cand;
-          if (cnt >= a.Kgr) T = cand;
+          for (int j = 0; j < KT; ++j) c4[j & 3] += r[j] >= cand;
+          if (c4[0] + c4[1] + c4[2] + c4[3] >= a.Kgr) T = cand;
         }
         int gt = 0;
 #pragma unroll
