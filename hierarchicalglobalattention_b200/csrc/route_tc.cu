@@ -19,7 +19,6 @@ namespace rtc {
 
 using namespace tc;
 
-constexpr int kThreads = 192;
 
 // Phase timestamps for development builds (-DHGA_ROUTE_PROFILE): thread 0 of the first 4096 CTAs
 // records %globaltimer after each block-wide barrier.  Compiled out otherwise.
@@ -133,8 +132,67 @@ __device__ void warp_select_u32(const uint32_t* keys, int n, int k, unsigned cha
   __syncwarp();
 }
 
+// Threads per CTA: TMA warp, MMA warp, then the row warps.  With KL = 16 two row warps share each
+// TMEM lane quarter (each scores half of every 128-chunk tile; the lists merge at the end), which
+// doubles the row warps per SM of the latency-bound scoring loop; KL = 32 lists leave room for one.
+// ---- sorting networks on register arrays (descending; fully unrolled, no serial chains) -----
+__device__ __forceinline__ void cas_desc(uint32_t& a, uint32_t& b) {
+  const uint32_t hi = max(a, b), lo = min(a, b);
+  a = hi;
+  b = lo;
+}
+// bitonic sort of v[0..N) into descending order (N a power of two)
+template <int N>
+__device__ __forceinline__ void sort_desc(uint32_t* v) {
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1)
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1)
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          if ((i & size) == 0) cas_desc(v[i], v[j]);
+          else cas_desc(v[j], v[i]);
+        }
+      }
+}
+// a bitonic v[0..N) into descending order
+template <int N>
+__device__ __forceinline__ void clean_desc(uint32_t* v) {
+#pragma unroll
+  for (int stride = N >> 1; stride > 0; stride >>= 1)
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const int j = i ^ stride;
+      if (j > i) cas_desc(v[i], v[j]);
+    }
+}
+// lst (descending, KL) := the KL largest of lst and the 32 keys in b (b is clobbered)
 template <int KL>
-__global__ void __launch_bounds__(kThreads, 2)
+__device__ __forceinline__ void merge_batch(uint32_t* lst, uint32_t* b) {
+  if constexpr (KL == 16) {
+    sort_desc<16>(b);
+    sort_desc<16>(b + 16);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) b[i] = max(b[i], b[31 - i]);  // top 16 of the batch, bitonic
+    clean_desc<16>(b);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) lst[i] = max(lst[i], b[15 - i]);
+    clean_desc<16>(lst);
+  } else {
+    sort_desc<32>(b);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) lst[i] = max(lst[i], b[31 - i]);
+    clean_desc<32>(lst);
+  }
+}
+
+template <int KL>
+__host__ __device__ constexpr int threads_for() { return KL <= 16 ? 320 : 192; }
+
+template <int KL>
+__global__ void __launch_bounds__(threads_for<KL>(), 2)
     route_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ck, const Args a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -144,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int kvh = h0 / (a.H / a.KVH);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int C = 64, M = 4;
+  constexpr int NT = threads_for<KL>(), kRowWarps = NT / 32 - 2, kHalves = kRowWarps / 4;
   const int row0 = n * C;
   const int nvalid = (a.S - row0) < C ? (a.S - row0) : C;
   const int N = a.N, NP = a.NP;
@@ -165,12 +224,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int pool_lo = f_hi, npool = l_lo > f_hi ? l_lo - f_hi : 0;
   const size_t out0 = (((size_t)b * a.H + h0) * a.nl + ln);
   const size_t out1 = out0 + a.nl;  // head h0+1
-  for (int i = tid; i < 2 * a.Kc; i += kThreads) {
+  for (int i = tid; i < 2 * a.Kc; i += NT) {
     const size_t o = (i < a.Kc ? out0 : out1) * a.Kc + (i % a.Kc);
     a.sel_chunk[o] = -1;
     a.sel_t0[o] = -1;
   }
-  for (int i = tid; i < 2 * a.Kg; i += kThreads) {
+  for (int i = tid; i < 2 * a.Kg; i += NT) {
     const size_t o = (i < a.Kg ? out0 : out1) * a.Kg + (i % a.Kg);
     a.open_gid[o] = -1;
     a.open_t0[o] = -1;
@@ -184,17 +243,17 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(ck_full + i, 1);
       mbar_init(ck_empty + i, 1);
       mbar_init(s_full + i, 1);
-      mbar_init(s_free + i, 128);
+      mbar_init(s_free + i, 32 * kRowWarps);
     }
     mbar_init(s2_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     ms->abort = 0;
   }
-  for (int i = tid; i < 2 * npool; i += kThreads) {
+  for (int i = tid; i < 2 * npool; i += NT) {
     pooled[(i / npool) * NP + i % npool] = 0u;
     t0c[(i / npool) * NP + i % npool] = 0xffffffffu;
   }
-  for (int i = tid; i < 2 * 128; i += kThreads) {
+  for (int i = tid; i < 2 * 128; i += NT) {
     ms->gpool[i / 128][i % 128] = 0u;
     ms->gt0[i / 128][i % 128] = 0xffffffffu;
   }
@@ -251,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else {
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;  // which share of every tile's columns this warp scores
     const int row = quarter * 32 + lane;
     const int hs = row >> 6, t = row & 63;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
@@ -259,16 +319,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int j = 0; j < KL; ++j) lst[j] = 0u;
     const size_t dbg_row = ((hs ? out1 : out0) * C + t) * (size_t)N + pool_lo;
-    if (warp == 2) HGA_RPROF_W(12);
     for (int i = 0; i < ntile; ++i) {
       const int st = i & 1;
       // tcgen05.ld is warp-collective: keep the branch around it warp-uniform
       if (!__all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 15))) break;
-      if (warp == 2 && i == 0) HGA_RPROF_W(13);
+      if (warp == 2 && i < 4) HGA_RPROF_W(12 + i);
       fence_after();
       const uint32_t sa = tmem + lane_addr + st * 128;
       const int cmax = (npool - 128 * i) < 128 ? (npool - 128 * i) : 128;
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c4 = half * (4 / kHalves); c4 < (half + 1) * (4 / kHalves); ++c4) {
         uint32_t r[32];
         HGA_LD32(sa + 32 * c4, r);
         tmem_wait_ld();
@@ -288,29 +347,41 @@ __global__ void __launch_bounds__(kThreads, 2)
           r[cc] = key;
           mask |= (key > thr ? 1u : 0u) << cc;
         }
-        // insert the candidates lane by lane: the warp loops as often as its busiest lane needs,
-        // not once per column that any lane needs
+        // the batch's keys join the row's list through sorting networks (no per-key insertion);
+        // skipped when no row of the warp has a key above its current threshold
+        if (__any_sync(0xffffffffu, mask != 0u)) merge_batch<KL>(lst, r);
+      }
+      fence_before();
+      mbar_arrive(s_free + st);
+      if (warp == 2 && i < 3) HGA_RPROF_W(8 + i);
+    }
+    if (kHalves == 2) {
+      // the second half's lists join the first half's (staged in the consumed tile stages)
+      uint32_t* mbuf = reinterpret_cast<uint32_t*>(tile_s);
+      if (half == 1) {
+#pragma unroll
+        for (int j = 0; j < KL; ++j) mbuf[j * 128 + row] = lst[j];
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * kRowWarps) : "memory");
+      if (half == 0) {
+        uint32_t mask = 0u;
+        const uint32_t thr = lst[KL - 1];
+        uint32_t other[KL];
+#pragma unroll
+        for (int j = 0; j < KL; ++j) {
+          other[j] = mbuf[j * 128 + row];
+          mask |= (other[j] > thr ? 1u : 0u) << j;
+        }
         const int rounds = __reduce_max_sync(0xffffffffu, __popc(mask));
         for (int it = 0; it < rounds; ++it) {
           uint32_t x = 0u;
           if (mask) {
             const int c0 = __ffs(mask) - 1;
             mask &= mask - 1u;
-            // r[c0] by a 5-level select tree on the bits of c0 (depth 5, not a 32-long chain)
-            uint32_t v16[16], v8[8], v4[4], v2[2];
 #pragma unroll
-            for (int k = 0; k < 16; ++k) v16[k] = (c0 & 1) ? r[2 * k + 1] : r[2 * k];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) v8[k] = (c0 & 2) ? v16[2 * k + 1] : v16[2 * k];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) v4[k] = (c0 & 4) ? v8[2 * k + 1] : v8[2 * k];
-#pragma unroll
-            for (int k = 0; k < 2; ++k) v2[k] = (c0 & 8) ? v4[2 * k + 1] : v4[2 * k];
-            x = (c0 & 16) ? v2[1] : v2[0];
+            for (int j = 0; j < KL; ++j) x = j == c0 ? other[j] : x;
           }
           if (x > lst[KL - 1]) {
-            // every slot of the descending list is computed from the old list at once (keys
-            // are unique), so the update has no serial dependence chain
             uint32_t nl[KL];
 #pragma unroll
             for (int j = 0; j < KL; ++j) {
@@ -322,14 +393,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
       }
-      fence_before();
-      mbar_arrive(s_free + st);
     }
-    if (warp == 2) HGA_RPROF_W(14);
-    // requests = top k1 of the union of the four lists (4-way merge) -> pooled max score and
-    // first requesting row per chunk
+    // requests = top k1 of the row's list -> pooled max score and first requesting row per chunk
     const int k1 = a.Kc < npool ? a.Kc : npool;
-    if (rvalid) {
+    if (rvalid && half == 0) {
 #pragma unroll
       for (int j = 0; j < KL; ++j) {
         if (j < k1 && lst[j] != 0u) {
@@ -406,13 +473,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     const __nv_bfloat16* gk = a.group_k + ((size_t)b * a.KVH + kvh) * a.sum_cap * M * 128;
     // every thread issues its 16-byte loads in two batches before storing, so the gather costs
     // two memory round trips instead of one per piece
-    constexpr int kPieces = 256 * 16, kBatch = (kPieces / kThreads + 2) / 2;
+    constexpr int kPieces = 256 * 16, kBatch = (kPieces / NT + 2) / 2;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       uint4 vals[kBatch];
 #pragma unroll
       for (int k = 0; k < kBatch; ++k) {
-        const int pc = tid + (half * kBatch + k) * kThreads;
+        const int pc = tid + (half * kBatch + k) * NT;
         vals[k] = make_uint4(0, 0, 0, 0);
         if (pc < kPieces) {
           const int rrow = pc >> 4, c16 = pc & 15;
@@ -425,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
 #pragma unroll
       for (int k = 0; k < kBatch; ++k) {
-        const int pc = tid + (half * kBatch + k) * kThreads;
+        const int pc = tid + (half * kBatch + k) * NT;
         if (pc < kPieces) {
           const int rrow = pc >> 4, c16 = pc & 15;
           const int kb = c16 >> 3, cc = c16 & 7;
@@ -447,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                  idesc, (kb | kk) != 0);
       mma_commit(s2_full);
     }
-    if (warp >= 2) {
+    if (warp >= 2 && warp < 6) {
       const int quarter = warp & 3;
       const int row = quarter * 32 + lane;
       const int hs = row >> 6, t = row & 63;
@@ -610,11 +677,11 @@ cudaError_t launch_route_tc(const hga_params& p, int64_t S, const QRange& qr, co
   if (Kc <= 16) {
     e = cudaFuncSetAttribute(rtc::route_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    rtc::route_tc_kernel<16><<<grid, rtc::kThreads, smem, st>>>(mq, mck, a);
+    rtc::route_tc_kernel<16><<<grid, rtc::threads_for<16>(), smem, st>>>(mq, mck, a);
   } else {
     e = cudaFuncSetAttribute(rtc::route_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    rtc::route_tc_kernel<32><<<grid, rtc::kThreads, smem, st>>>(mq, mck, a);
+    rtc::route_tc_kernel<32><<<grid, rtc::threads_for<32>(), smem, st>>>(mq, mck, a);
   }
   return cudaGetLastError();
 }
