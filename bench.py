@@ -404,6 +404,54 @@ def decode_bench(device, steps: int = 64, warmup: int = 8):
     return res
 
 
+def decode_mixed_bench(device, layers: int = 2, batch: int = 8, steps: int = 32, warmup: int = 4):
+    """configs[4] on one GPU (its per-GPU share, scaled): `batch` sequences whose lengths are drawn
+    uniformly from {8192, 8256, ..., 131072}, cold K/V in pinned host memory, configs[0] routing,
+    `layers` attention layers per step through ChunkRouter.decode_step (per-sequence positions).
+    The 8-GPU config runs 8 such shares with no collective."""
+    from hierarchicalglobalattention_b200 import ChunkPlacementPolicy, ChunkRouter, RouterConfig
+    from hierarchicalglobalattention_b200.store_ram import RamKVCacheStore
+    H, KVH, Dh, C = 32, 4, 128, 64
+    dt = torch.bfloat16
+    g = torch.Generator(device="cpu").manual_seed(4)
+    lens = [int(x) * 64 for x in torch.randint(8192 // 64, 131072 // 64 + 1, (batch,), generator=g)]
+    cfg = RouterConfig(nhead=H, kv_heads=KVH, head_dim=Dh, chunk_size=C, group_size=16, topk_chunks=16,
+                       topk_groups=64, theta=1e6)
+    pol = ChunkPlacementPolicy(keep_first=2, keep_last=8, first_token_level=True)
+    store = RamKVCacheStore(compute_device=device, policy=pol, kv_heads=KVH, head_dim=Dh, chunk_size=C,
+                            groups_per_chunk=4, batch_size=batch, dtype=dt,
+                            initial_capacity=(max(lens) + (steps + warmup + 2) * 1) // C + 2)
+    router = ChunkRouter(cfg, store)
+    gd = torch.Generator(device=device).manual_seed(5)
+    Smax = max(lens)
+    for layer in range(layers):
+        k = torch.randn(batch, KVH, Smax, Dh, device=device, dtype=dt, generator=gd)
+        router.seed_mixed(layer, k, k, k, lens)
+        del k
+    torch.cuda.synchronize()
+    n = warmup + steps
+    qs = torch.randn(n, batch, H, 1, Dh, device=device, dtype=dt, generator=gd)
+    ks = torch.randn(n, batch, KVH, 1, Dh, device=device, dtype=dt, generator=gd)
+    pos = list(lens)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(n):
+        if i == warmup:
+            torch.cuda.synchronize()
+            e0.record()
+        seq = torch.tensor(pos, dtype=torch.int32, device=device)
+        for layer in range(layers):
+            rk = router.decode_step(layer, qs[i], ks[i], ks[i], ks[i], seq, pos)
+            rk.attend(qs[i])
+        pos = [p_ + 1 for p_ in pos]
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"workload": f"configs[4] per-GPU share: {batch} sequences, lengths {min(lens)}-{max(lens)} "
+                        f"(uniform in 8192..131072 step 64), {layers} layers, cold K/V in pinned host memory",
+            "us_per_layer_step": ms * 1e3 / layers, "tokens_per_s": batch / (ms / 1e3), "layers": layers,
+            "batch": batch}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -504,6 +552,10 @@ def main():
                               "tier": "ram (cold K/V in pinned host memory)", **d}
         except Exception as e:
             line["decode"] = {"error": str(e)[:300]}
+        try:
+            line["decode_mixed"] = decode_mixed_bench(device)
+        except Exception as e:
+            line["decode_mixed"] = {"error": str(e)[:300]}
     print(json.dumps(line))
     if world > 1:
         torch.distributed.destroy_process_group()

@@ -353,7 +353,6 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
       }
       fence_before();
       mbar_arrive(s_free + st);
-      if (warp == 2 && i < 3) HGA_RPROF_W(8 + i);
     }
     if (kHalves == 2) {
       // the second half's lists join the first half's (staged in the consumed tile stages)

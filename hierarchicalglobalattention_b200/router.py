@@ -202,6 +202,33 @@ class ChunkRouter:
         hp = self.cfg.hga_params(self.store.policy, B, k_rope.dtype)
         self._seed_store(layer, hp, k_rope, k_raw, v, k_rope.shape[2])
 
+    def seed_mixed(self, layer: int, k_rope: torch.Tensor, k_raw: torch.Tensor, v: torch.Tensor,
+                   seq_lens) -> None:
+        """``seed`` for a batch whose sequences have different lengths (``seq_lens``, host ints):
+        row b of k_* / v [B,KVH,Smax,Dh] holds its context in [0, seq_lens[b]).  Decode then
+        continues through ``decode_step`` at per-sequence positions (no reference counterpart:
+        the reference's batches share one position)."""
+        import copy
+        cfg, store = self.cfg, self.store
+        C = cfg.chunk_size
+        B = k_rope.shape[0]
+        hp1 = copy.copy(cfg.hga_params(store.policy, B, k_rope.dtype))
+        hp1.batch = 1
+        nmax = max(seq_lens) // C
+        st = store.ensure_capacity(layer, max(nmax, 1), max(seq_lens) + C)
+        store.write_tokens(layer, 0, k_rope, v)
+        for b, S in enumerate(seq_lens):
+            n = S // C
+            if n:
+                cos32, sin32 = self._rotary(k_raw.device, S)
+                ops.summaries(hp1, k_raw[b:b + 1], k_rope[b:b + 1], v[b:b + 1], cos32, sin32, seq_len=n * C,
+                              out=(st.chunk_k[b:b + 1], st.group_k[b:b + 1], st.group_v[b:b + 1]), out_chunk0=0)
+            rem = S - n * C
+            if rem:
+                store.active_raw(layer)[b, :, :rem].copy_(k_raw[b, :, n * C:S])
+            store.after_seed(layer, S, row=b)
+        store.mark_closed(layer, min(seq_lens) // C)
+
     def _seed_store(self, layer, hp, k_rope, k_raw, v, S):
         """Store seed of a fresh prefill (chunk_router.py:553-599): summaries of the closed chunks with
         fixed anchors and fp32 rotary rows, token rows, and the partial active chunk."""

@@ -159,8 +159,9 @@ class VramKVCacheStore(KVCacheStore):
     def on_chunk_closed(self, layer: int, n: int, row: Optional[int] = None) -> None:
         """Hook after chunk n closed (the RAM tier moves it into its window slots)."""
 
-    def after_seed(self, layer: int, seq_len: int) -> None:
-        """Hook after a prefill seeded tokens [0, seq_len) (the RAM tier fills its hot slots)."""
+    def after_seed(self, layer: int, seq_len: int, row: Optional[int] = None) -> None:
+        """Hook after a prefill seeded tokens [0, seq_len) of every batch row, or of ``row`` (the
+        RAM tier fills its hot slots)."""
 
     def adopt_tokens(self, layer: int, token_k: torch.Tensor, token_v: torch.Tensor) -> None:
         """Take ownership of freshly written [B,KVH,cap,Dh] token buffers (zero-copy prefill seed)."""

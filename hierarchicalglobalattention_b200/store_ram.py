@@ -80,9 +80,14 @@ class RamKVCacheStore(VramKVCacheStore):
         st.token_k[:, :, row0:row0 + L].copy_(token_k)
         st.token_v[:, :, row0:row0 + L].copy_(token_v)
 
-    def _to_slot(self, layer: int, c: int, src_k: torch.Tensor, src_v: torch.Tensor, row: Optional[int]) -> None:
+    def _to_slot(self, layer: int, c: int, src_k: torch.Tensor, src_v: torch.Tensor, row: Optional[int],
+                 dst_row: Optional[int] = None) -> None:
+        """Copy chunk c's rows (batch row ``row`` of src, all rows if None) into its window slots
+        (batch row ``dst_row``, default the same as ``row``)."""
         st = self.layer_buffers(layer)
+        dst_row = row if dst_row is None else dst_row
         bs = slice(None) if row is None else slice(row, row + 1)
+        bd = slice(None) if dst_row is None else slice(dst_row, dst_row + 1)
         dsts = []
         if c < self.kf:
             dsts.append(c)
@@ -90,30 +95,32 @@ class RamKVCacheStore(VramKVCacheStore):
             dsts.append(self.kf + c % self.kl)
         for slot in dsts:
             sl = slice(slot * self.C, (slot + 1) * self.C)
-            st.hot_k[bs, :, sl].copy_(src_k[bs], non_blocking=True)
-            st.hot_v[bs, :, sl].copy_(src_v[bs], non_blocking=True)
+            st.hot_k[bd, :, sl].copy_(src_k[bs], non_blocking=True)
+            st.hot_v[bd, :, sl].copy_(src_v[bs], non_blocking=True)
 
     def on_chunk_closed(self, layer: int, n: int, row: Optional[int] = None) -> None:
         """The closed active chunk enters the keep_last ring (and the keep_first window)."""
         k_act, v_act = self.active_rows(layer, n)
         self._to_slot(layer, n, k_act.clone(), v_act.clone(), row)
 
-    def after_seed(self, layer: int, seq_len: int) -> None:
-        """Fill the window / active slots after a prefill wrote the record (ram_kv_cache_store.py:511-526)."""
+    def after_seed(self, layer: int, seq_len: int, row: Optional[int] = None) -> None:
+        """Fill the window / active slots after a prefill wrote the record (ram_kv_cache_store.py:511-526),
+        for every batch row or only ``row``."""
         st = self.layer_buffers(layer)
         C = self.C
         n = seq_len // C
         f_lo, f_hi = self.policy.hot_first_range(n)
         l_lo, l_hi = self.policy.hot_last_range(n)
+        bs = slice(None) if row is None else slice(row, row + 1)
         for c in sorted(set(range(f_lo, f_hi)) | set(range(l_lo, l_hi))):
             sl = slice(c * C, (c + 1) * C)
-            self._to_slot(layer, c, st.token_k[:, :, sl].to(self.compute_device),
-                          st.token_v[:, :, sl].to(self.compute_device), None)
+            self._to_slot(layer, c, st.token_k[bs, :, sl].to(self.compute_device),
+                          st.token_v[bs, :, sl].to(self.compute_device), None if row is None else 0, row)
         rem = seq_len - n * C
         if rem:
             k_act, v_act = self.active_rows(layer, n)
-            k_act[:, :, :rem].copy_(st.token_k[:, :, n * C:seq_len])
-            v_act[:, :, :rem].copy_(st.token_v[:, :, n * C:seq_len])
+            k_act[bs, :, :rem].copy_(st.token_k[bs, :, n * C:seq_len])
+            v_act[bs, :, :rem].copy_(st.token_v[bs, :, n * C:seq_len])
 
     def hot_tokens(self, layer, lo, hi):
         st = self.layer_buffers(layer)

@@ -203,7 +203,9 @@ def test_mixed_length_decode_step_equals_per_sequence_runs(cuda, tier):
     # the batched run: prefill each sequence's prefix through its own batch row
     router = _router(p, B, c["dtype"], dev, tier)
     pre = {k: t for k, t in zip(("q", "k_rope", "k_raw", "v"), (q, kr, kraw, v))}
-    _seed_mixed(router, pre, starts, c)
+    Smax = max(starts)
+    router.seed_mixed(0, *(pre[k][None, :, :Smax].expand(B, -1, -1, -1).contiguous() for k in ("k_rope", "k_raw", "v")),
+                      starts)
     seq_host = list(starts)
     outs = []
     for _ in range(steps):
@@ -219,34 +221,6 @@ def test_mixed_length_decode_step_equals_per_sequence_runs(cuda, tier):
     out = torch.cat(outs, dim=2)
     for b in range(B):
         assert torch.equal(out[b], singles[b]), f"sequence {b} differs from its B=1 run"
-
-
-def _seed_mixed(router, pre, starts, c):
-    """Seed batch row b of the router's store with the prefix [0, starts[b]) by running B=1 prefills
-    into a scratch router and copying the per-row state (the public API seeds uniform batches)."""
-    p = c["params"]
-    store = router.store
-    C = p.chunk_size
-    nmax = max(starts) // C
-    store.ensure_capacity(0, max(nmax, 1), (nmax + 1) * C)
-    for b, s0 in enumerate(starts):
-        r1 = _router(p, 1, c["dtype"], pre["q"].device, "vram" if store.hot_mode == 0 else "ram")
-        g1 = {k: t[None, :, :s0] for k, t in pre.items()}
-        for rk, lo, hi in r1.route_query_block(0, g1["q"], g1["k_rope"], g1["k_raw"], g1["v"], 0):
-            rk.attend(g1["q"][:, :, lo:hi], use_summaries=False)
-        s1, st = r1.store.layer_buffers(0), store.layer_buffers(0)
-        n = s0 // C
-        st.chunk_k[b, :, :n] = s1.chunk_k[0, :, :n]
-        st.group_k[b, :, :n] = s1.group_k[0, :, :n]
-        st.group_v[b, :, :n] = s1.group_v[0, :, :n]
-        st.token_k[b, :, :s0] = s1.token_k[0, :, :s0]
-        st.token_v[b, :, :s0] = s1.token_v[0, :, :s0]
-        store.active_raw(0)[b] = r1.store.active_raw(0)[0]
-        if store.hot_mode == 1:
-            st.hot_k[b] = s1.hot_k[0]
-            st.hot_v[b] = s1.hot_v[0]
-    st.n_closed = min(s // C for s in starts)
-    torch.cuda.synchronize()
 
 
 @pytest.mark.parametrize("tier", TIERS)
