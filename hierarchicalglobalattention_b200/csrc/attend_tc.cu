@@ -314,18 +314,17 @@ __global__ void __launch_bounds__(kThreads, 2)
         cnt[u] = rvalid ? c : 0;
       }
       tmem_wait_ld();
-      float mx = -INFINITY;
+      // row max over the visible keys: four independent partial maxima (short dependence chains)
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int u = 0; u < kUnitsPerTile; ++u) {
-        if (cnt[u] == 16) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) mx = fmaxf(mx, __uint_as_float(r[u * 16 + j]));
-        } else if (cnt[u] > 0) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (j < cnt[u]) mx = fmaxf(mx, __uint_as_float(r[u * 16 + j]));
+        for (int j = 0; j < 16; ++j) {
+          const float x = j < cnt[u] ? __uint_as_float(r[u * 16 + j]) : -INFINITY;
+          mx4[j & 3] = fmaxf(mx4[j & 3], x);
         }
       }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       const float m_tile = mx * sl2;
       // lazy rescale: only when the max grows by more than 2^8 (or the first visible keys arrive)
       float alpha = 1.f;
@@ -354,33 +353,23 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tmem_wait_st();
       }
-      float psum = 0.f;
+      float ps4[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums (short dependence chains)
       uint32_t pk[32];
-      const float nm = -m_run;
+      const float nm = m_run == -INFINITY ? 0.f : -m_run;  // no visible key yet: every p is 0
 #pragma unroll
       for (int u = 0; u < kUnitsPerTile; ++u) {
-        if (cnt[u] == 16) {
 #pragma unroll
-          for (int j = 0; j < 16; j += 2) {
-            const float p0 = ex2(fmaf(__uint_as_float(r[u * 16 + j]), sl2, nm));
-            const float p1 = ex2(fmaf(__uint_as_float(r[u * 16 + j + 1]), sl2, nm));
-            psum += p0 + p1;
-            pk[(u * 16 + j) >> 1] = pack_bf16(p0, p1);
-          }
-        } else if (cnt[u] == 0) {
-#pragma unroll
-          for (int j = 0; j < 16; j += 2) pk[(u * 16 + j) >> 1] = 0u;
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; j += 2) {
-            const float p0 = j < cnt[u] ? ex2(fmaf(__uint_as_float(r[u * 16 + j]), sl2, nm)) : 0.f;
-            const float p1 = j + 1 < cnt[u] ? ex2(fmaf(__uint_as_float(r[u * 16 + j + 1]), sl2, nm)) : 0.f;
-            psum += p0 + p1;
-            pk[(u * 16 + j) >> 1] = pack_bf16(p0, p1);
-          }
+        for (int j = 0; j < 16; j += 2) {
+          // invisible keys: exponent of -inf, which ex2 maps to 0
+          const float x0 = j < cnt[u] ? __uint_as_float(r[u * 16 + j]) : -INFINITY;
+          const float x1 = j + 1 < cnt[u] ? __uint_as_float(r[u * 16 + j + 1]) : -INFINITY;
+          const float p0 = ex2(fmaf(x0, sl2, nm));
+          const float p1 = ex2(fmaf(x1, sl2, nm));
+          ps4[(j >> 1) & 3] += p0 + p1;
+          pk[(u * 16 + j) >> 1] = pack_bf16(p0, p1);
         }
       }
-      l_run += psum;
+      l_run += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
       HGA_ST32(s_addr, pk);
       tmem_wait_st();
       fence_before();
