@@ -89,6 +89,99 @@ __global__ void __launch_bounds__(kProWarps * 32) prologue_kernel(
   }
 }
 
+// Vectorised variant for head_dim = 32 * EPL: lane l holds elements [EPL*l, EPL*l + EPL) of the
+// row (one 8- or 16-byte load), the rotate-half partner lives in lane l ^ (16) and is fetched with a
+// shuffle, so nothing is staged in shared memory and every access is a whole-row line.  Same
+// arithmetic and rounding points as prologue_kernel; the sum of squares is reduced in another order.
+template <int BYTES> struct VecT;
+template <> struct VecT<4> { using type = uint32_t; };
+template <> struct VecT<8> { using type = uint2; };
+template <> struct VecT<16> { using type = uint4; };
+// EPL contiguous elements as one aligned vector access (the row layouts keep it aligned)
+template <typename T, int EPL>
+__device__ __forceinline__ void ld_vec(const T* src, T* v) {
+  using V = typename VecT<sizeof(T) * EPL>::type;
+  const V x = *reinterpret_cast<const V*>(src);
+  memcpy(v, &x, sizeof(V));
+}
+template <typename T, int EPL>
+__device__ __forceinline__ void st_vec(T* dst, const T* v) {
+  using V = typename VecT<sizeof(T) * EPL>::type;
+  V x;
+  memcpy(&x, v, sizeof(V));
+  *reinterpret_cast<V*>(dst) = x;
+}
+
+template <typename T, int EPL>
+__global__ void __launch_bounds__(kProWarps * 32) prologue_vec_kernel(
+    hga_params p, int64_t S, const T* __restrict__ qkv, int64_t row_stride, const T* __restrict__ qw,
+    const T* __restrict__ kw, float eps, int norm_mode, const void* __restrict__ cos_t,
+    const void* __restrict__ sin_t, int rope_mode, int64_t rot_row0, int64_t pos0, T* __restrict__ q_out,
+    T* __restrict__ kraw_out, T* __restrict__ krope_out, T* __restrict__ v_out, int64_t kv_cap, int64_t kv_row0) {
+  constexpr int Dh = 32 * EPL;
+  const int H = p.nhead, KVH = p.kv_heads;
+  const int rows_per_tok = H + 2 * KVH;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * kProWarps + warp;
+  const int64_t total = (int64_t)p.batch * S * rows_per_tok;
+  if (gw >= total) return;
+  const int r = (int)(gw % rows_per_tok);
+  const int64_t bt = gw / rows_per_tok;  // b * S + t
+  const int64_t t = bt % S;
+  const int b = (int)(bt / S);
+  const bool is_q = r < H, is_k = r >= H && r < H + KVH;
+  const int kvh = is_q ? 0 : (is_k ? r - H : r - H - KVH);
+  const int d0 = lane * EPL;
+  T xin[EPL];
+  ld_vec<T, EPL>(qkv + bt * row_stride + (int64_t)r * Dh + d0, xin);
+  if (!is_q && !is_k) {  // v: layout transform only
+    st_vec<T, EPL>(v_out + (((int64_t)b * KVH + kvh) * kv_cap + kv_row0 + t) * Dh + d0, xin);
+    return;
+  }
+  float x[EPL];
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    x[e] = Num<T>::to_f(xin[e]);
+    ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
+  }
+  const T* w = is_q ? qw : kw;
+  if (w) {
+    for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const float mean = __fdiv_rn(ss, (float)Dh);
+    const float rs = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, eps)));
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const float wf = Num<T>::to_f(w[d0 + e]);
+      x[e] = norm_mode == 0 ? Num<T>::round(__fmul_rn(__fmul_rn(wf, x[e]), rs))
+                            : Num<T>::round(__fmul_rn(wf, Num<T>::round(__fmul_rn(x[e], rs))));
+    }
+  }
+  // RoPE: the partner of element d is d +- Dh/2, held by lane ^ 16 at the same position
+  const int64_t rr = (pos0 + t - rot_row0) * Dh + d0;
+  T* dst_rope = is_q ? q_out + (bt * H + r) * Dh + d0
+                     : krope_out + (((int64_t)b * KVH + kvh) * kv_cap + kv_row0 + t) * Dh + d0;
+  T* dst_raw = is_k ? kraw_out + (((int64_t)b * KVH + kvh) * kv_cap + kv_row0 + t) * Dh + d0 : nullptr;
+  T yo[EPL], xo[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
+    const float xp = lane < 16 ? -other : other;
+    float y;
+    if (rope_mode == 0) {
+      const float cs = ((const float*)cos_t)[rr + e], sn = ((const float*)sin_t)[rr + e];
+      y = __fadd_rn(__fmul_rn(x[e], cs), __fmul_rn(xp, sn));
+    } else {
+      const float cs = Num<T>::to_f(((const T*)cos_t)[rr + e]), sn = Num<T>::to_f(((const T*)sin_t)[rr + e]);
+      y = __fadd_rn(Num<T>::round(__fmul_rn(x[e], cs)), Num<T>::round(__fmul_rn(xp, sn)));
+    }
+    yo[e] = Num<T>::from_f(y);
+    xo[e] = Num<T>::from_f(x[e]);
+  }
+  st_vec<T, EPL>(dst_rope, yo);
+  if (dst_raw) st_vec<T, EPL>(dst_raw, xo);
+}
+
 cudaError_t launch_prologue(const hga_params& p, int64_t S, const void* qkv, int64_t row_stride, const void* qw,
                             const void* kw, float eps, int norm_mode, const void* cos, const void* sin,
                             int rope_mode, int64_t rot_row0, int64_t pos0, void* q_out, void* kraw_out,
@@ -96,6 +189,22 @@ cudaError_t launch_prologue(const hga_params& p, int64_t S, const void* qkv, int
   const int64_t rows = (int64_t)p.batch * S * (p.nhead + 2 * p.kv_heads);
   const int64_t blocks = (rows + kProWarps - 1) / kProWarps;
   const size_t smem = (size_t)kProWarps * p.head_dim * sizeof(float);
+#define HGA_PRO_VEC(T, EPL)                                                                                     \
+  prologue_vec_kernel<T, EPL><<<(unsigned)blocks, kProWarps * 32, 0, st>>>(                                    \
+      p, S, (const T*)qkv, row_stride, (const T*)qw, (const T*)kw, eps, norm_mode, cos, sin, rope_mode, rot_row0, \
+      pos0, (T*)q_out, (T*)kraw_out, (T*)krope_out, (T*)v_out, kv_cap, kv_row0);                                \
+  return cudaGetLastError();
+  if (p.head_dim == 128 || p.head_dim == 64) {
+    switch (p.dtype) {
+      case HGA_DTYPE_F32:
+        if (p.head_dim == 128) { HGA_PRO_VEC(float, 4) } else { HGA_PRO_VEC(float, 2) }
+      case HGA_DTYPE_BF16:
+        if (p.head_dim == 128) { HGA_PRO_VEC(__nv_bfloat16, 4) } else { HGA_PRO_VEC(__nv_bfloat16, 2) }
+      case HGA_DTYPE_F16:
+        if (p.head_dim == 128) { HGA_PRO_VEC(__half, 4) } else { HGA_PRO_VEC(__half, 2) }
+    }
+  }
+#undef HGA_PRO_VEC
 #define HGA_PRO(T)                                                                                              \
   prologue_kernel<T><<<(unsigned)blocks, kProWarps * 32, smem, st>>>(                                          \
       p, S, (const T*)qkv, row_stride, (const T*)qw, (const T*)kw, eps, norm_mode, cos, sin, rope_mode, rot_row0, \
