@@ -92,49 +92,6 @@ struct Misc {
   uint32_t gt0[2][128];
 };
 
-// Warp-wide radix select over keys[0..n) (unique 32-bit keys, 0 = absent): flags the k largest.
-// Keys are cached in registers (up to 64 per lane, n <= 2048); larger n streams from smem.
-__device__ void warp_select_u32(const uint32_t* keys, int n, int k, unsigned char* flag) {
-  const int lane = threadIdx.x & 31;
-  int nreal = 0;
-  for (int i = lane; i < n; i += 32) nreal += keys[i] != 0u;
-  for (int o = 16; o; o >>= 1) nreal += __shfl_xor_sync(0xffffffffu, nreal, o);
-  if (nreal <= k) {
-    for (int i = lane; i < n; i += 32) flag[i] = keys[i] != 0u;
-    __syncwarp();
-    return;
-  }
-  uint32_t T = 0;
-  if (n <= 32 * 64) {
-    uint32_t kr[64];
-#pragma unroll
-    for (int m = 0; m < 64; ++m) kr[m] = (lane + 32 * m < n) ? keys[lane + 32 * m] : 0u;
-    const int mmax = (n + 31) / 32;
-    for (int bit = 31; bit >= 0; --bit) {
-      const uint32_t cand = T | (1u << bit);
-      int c4[4] = {0, 0, 0, 0};  // four partial counts: short dependence chains
-#pragma unroll
-      for (int m = 0; m < 64; ++m)
-        if (m < mmax) c4[m & 3] += kr[m] >= cand;
-      const int cnt = __reduce_add_sync(0xffffffffu, c4[0] + c4[1] + c4[2] + c4[3]);
-      if (cnt >= k) T = cand;
-    }
-  } else {
-    for (int bit = 31; bit >= 0; --bit) {
-      const uint32_t cand = T | (1u << bit);
-      int cnt = 0;
-      for (int i = lane; i < n; i += 32) cnt += keys[i] >= cand;
-      cnt = __reduce_add_sync(0xffffffffu, cnt);
-      if (cnt >= k) T = cand;
-    }
-  }
-  for (int i = lane; i < n; i += 32) flag[i] = keys[i] >= T;  // keys are unique: exactly k
-  __syncwarp();
-}
-
-// Threads per CTA: TMA warp, MMA warp, then the row warps.  With KL = 16 two row warps share each
-// TMEM lane quarter (each scores half of every 128-chunk tile; the lists merge at the end), which
-// doubles the row warps per SM of the latency-bound scoring loop; KL = 32 lists leave room for one.
 // ---- sorting networks on register arrays (descending; fully unrolled, no serial chains) -----
 __device__ __forceinline__ void cas_desc(uint32_t& a, uint32_t& b) {
   const uint32_t hi = max(a, b), lo = min(a, b);
@@ -188,6 +145,78 @@ __device__ __forceinline__ void merge_batch(uint32_t* lst, uint32_t* b) {
   }
 }
 
+// Warp-wide top-k for n <= 512 unique 32-bit keys: every lane sorts its 16 keys (a sorting network),
+// then k rounds of one warp max-reduction pop the largest remaining key from its owner lane.  Flags
+// the k largest and returns the smallest flagged key (0 if fewer than k keys are non-zero: then
+// every non-zero key is flagged).
+__device__ uint32_t warp_topk_small(const uint32_t* keys, int n, int k, unsigned char* flag) {
+  const int lane = threadIdx.x & 31;
+  uint32_t v[16];
+#pragma unroll
+  for (int m = 0; m < 16; ++m) v[m] = (lane + 32 * m < n) ? keys[lane + 32 * m] : 0u;
+  sort_desc<16>(v);
+  for (int i = lane; i < n; i += 32) flag[i] = 0;
+  __syncwarp();
+  uint32_t last = 0u;
+  for (int it = 0; it < k; ++it) {
+    const uint32_t best = __reduce_max_sync(0xffffffffu, v[0]);
+    if (best == 0u) break;
+    last = best;
+    if (v[0] == best) {  // the owner pops its head (keys are unique: exactly one lane)
+#pragma unroll
+      for (int m = 0; m < 15; ++m) v[m] = v[m + 1];
+      v[15] = 0u;
+    }
+  }
+  __syncwarp();
+  for (int i = lane; i < n; i += 32) flag[i] = keys[i] != 0u && keys[i] >= last;
+  __syncwarp();
+  return last;
+}
+
+// Warp-wide radix select over keys[0..n) (unique 32-bit keys, 0 = absent): flags the k largest.
+// Keys are cached in registers (up to 64 per lane, n <= 2048); larger n streams from smem.
+__device__ void warp_select_u32(const uint32_t* keys, int n, int k, unsigned char* flag) {
+  const int lane = threadIdx.x & 31;
+  int nreal = 0;
+  for (int i = lane; i < n; i += 32) nreal += keys[i] != 0u;
+  for (int o = 16; o; o >>= 1) nreal += __shfl_xor_sync(0xffffffffu, nreal, o);
+  if (nreal <= k) {
+    for (int i = lane; i < n; i += 32) flag[i] = keys[i] != 0u;
+    __syncwarp();
+    return;
+  }
+  uint32_t T = 0;
+  if (n <= 32 * 64) {
+    uint32_t kr[64];
+#pragma unroll
+    for (int m = 0; m < 64; ++m) kr[m] = (lane + 32 * m < n) ? keys[lane + 32 * m] : 0u;
+    const int mmax = (n + 31) / 32;
+    for (int bit = 31; bit >= 0; --bit) {
+      const uint32_t cand = T | (1u << bit);
+      int c4[4] = {0, 0, 0, 0};  // four partial counts: short dependence chains
+#pragma unroll
+      for (int m = 0; m < 64; ++m)
+        if (m < mmax) c4[m & 3] += kr[m] >= cand;
+      const int cnt = __reduce_add_sync(0xffffffffu, c4[0] + c4[1] + c4[2] + c4[3]);
+      if (cnt >= k) T = cand;
+    }
+  } else {
+    for (int bit = 31; bit >= 0; --bit) {
+      const uint32_t cand = T | (1u << bit);
+      int cnt = 0;
+      for (int i = lane; i < n; i += 32) cnt += keys[i] >= cand;
+      cnt = __reduce_add_sync(0xffffffffu, cnt);
+      if (cnt >= k) T = cand;
+    }
+  }
+  for (int i = lane; i < n; i += 32) flag[i] = keys[i] >= T;  // keys are unique: exactly k
+  __syncwarp();
+}
+
+// Threads per CTA: TMA warp, MMA warp, then the row warps.  With KL = 16 two row warps share each
+// TMEM lane quarter (each scores half of every 128-chunk tile; the lists merge at the end), which
+// doubles the row warps per SM of the latency-bound scoring loop; KL = 32 lists leave room for one.
 template <int KL>
 __host__ __device__ constexpr int threads_for() { return KL <= 16 ? 320 : 192; }
 
@@ -417,7 +446,8 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
     for (int c = lane; c < npool; c += 32) keys[c] = keys[c] ? ((keys[c] << 16) | (0xffffu - c)) : 0u;
     __syncwarp();
     if (hs == 0) HGA_RPROF_W(8);
-    warp_select_u32(keys, npool, a.Kc, fl);
+    if (npool <= 512) warp_topk_small(keys, npool, a.Kc, fl);
+    else warp_select_u32(keys, npool, a.Kc, fl);
     if (hs == 0) HGA_RPROF_W(9);
     const int prev = n - 1;
     const bool prev_in = n > 0 && prev >= pool_lo && prev < l_lo;
