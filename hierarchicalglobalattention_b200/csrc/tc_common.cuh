@@ -43,6 +43,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+#ifndef HGA_TRY_WAIT_NS
+#define HGA_TRY_WAIT_NS 20000  // suspend at most ~20 us per attempt
+#endif
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -50,7 +53,7 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(20000)  // suspend at most ~20 us per attempt
+      : "r"(smem_u32(bar)), "r"(parity), "r"(HGA_TRY_WAIT_NS)
       : "memory");
   return ok != 0;
 }
