@@ -77,6 +77,6 @@ def test_gather_and_unpack_two_gloo_ranks():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    out = mp.Manager().dict()
+    out = mp.get_context("spawn").Manager().dict()
     mp.spawn(_worker, args=(2, port, out), nprocs=2, join=True)
     assert out[0] and out[1]
