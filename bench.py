@@ -5,7 +5,8 @@ python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--s
 One step = one forward of ``HierarchicalGlobalAttentionRouted`` (fused QKV GEMM, q/k RMSNorm +
 RoPE prologue, summary builder, two-level router, working-set attention, o_proj) over one
 synthetic batch (seeded N(0,1) hidden states, N(0,0.02) weights).
-Prints ONE JSON line (rank 0).  See DESIGN.md for the metric definitions.
+Prints ONE JSON line (rank 0): the prefill line, plus `decode` and `decode_mixed`
+(one GPU's share of configs[4]) measurements at N=1.
 """
 from __future__ import annotations
 

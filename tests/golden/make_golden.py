@@ -222,9 +222,12 @@ def run_qwen_case(ref, case):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("HGA_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("HGA_REFERENCE_ROOT"),
+                    help="checkout of the reference repository (or set HGA_REFERENCE_ROOT)")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("--ref (or HGA_REFERENCE_ROOT) must point at the reference checkout")
     ref = _import_reference(args.ref)
     torch.set_num_threads(os.cpu_count() or 1)
     for case in cases.CASES:
