@@ -100,3 +100,59 @@ def test_qwen_patch_host_side():
     assert sum(p.numel() for p in model.parameters()) == n_params                 # no new parameters
     assert restore_original_attention(model) == 2
     assert isinstance(model.model.layers[0].self_attn, Attn)
+
+
+def _p(**kw):
+    from hierarchicalglobalattention_b200 import _lib
+    base = dict(batch=1, nhead=4, kv_heads=2, head_dim=16, chunk_size=8, group_size=4, topk_chunks=2,
+                topk_groups=4, keep_first=1, keep_last=1, theta=1e4, dtype=torch.float32)
+    base.update(kw)
+    return _lib.make_params(**base)
+
+
+def test_range_decode_and_unpack_entry_points_validate_before_any_launch():
+    """Bad ranges, impl choices, positions lists and unpack layouts are rejected with a message
+    naming the problem; none of these calls reaches the device."""
+    from hierarchicalglobalattention_b200 import _lib
+    h = _lib.lib()
+    p = _p()
+    P = ctypes.byref(p)
+    one = ctypes.c_void_p(16)  # any non-NULL pointer: validation fails before it is used
+    # query-chunk range outside the sequence / empty
+    rc = h.hga_route_prefill_range(P, 40, 3, 9, one, 0, one, one, 8, one, one, one, one, None, None, 0, None)
+    assert rc == -1 and b"range" in h.hga_last_error()
+    rc = h.hga_attend_prefill_range(P, 40, 2, 2, one, 0, one, one, 64, one, one, one, 1, 0, None)
+    assert rc == -1 and b"range" in h.hga_last_error()
+    # unknown kernel choice
+    rc = h.hga_route_decode_impl(P, 1, one, one, one, one, 8, 4, one, one, one, one, 7, None)
+    assert rc == -1 and b"impl" in h.hga_last_error()
+    rc = h.hga_attend_decode_impl(P, 1, one, one, one, one, 64, 0, one, one, 64, one, one, 4, one, 9, None)
+    assert rc == -1 and b"impl" in h.hga_last_error()
+    # a fast kernel asked for where it does not apply (fp32, head_dim 16)
+    rc = h.hga_attend_decode_impl(P, 1, one, one, one, one, 64, 0, one, one, 64, one, one, 4, one, 2, None)
+    assert rc == -2 and b"fast kernel" in h.hga_last_error()
+    # decode block longer than a chunk, unknown hot_mode
+    rc = h.hga_append_tokens(P, 9, one, one, one, None, one, one, 64, 0, None, None, 0, None, None)
+    assert rc == -1 and b"chunk_size" in h.hga_last_error()
+    rc = h.hga_append_tokens(P, 1, one, one, one, None, one, one, 64, 3, None, None, 0, None, None)
+    assert rc == -1 and b"hot_mode" in h.hga_last_error()
+    # unpack: misaligned row size, out-of-range destination block
+    tab = (ctypes.c_int32 * 4)(0, 3, 1, 2)
+    rc = h.hga_shard_unpack(one, 64, 0, 2, 2, ctypes.cast(tab, ctypes.c_void_p), 1, 4, 24, one, None)
+    assert rc == -1 and b"aligned" in h.hga_last_error()
+    bad = (ctypes.c_int32 * 4)(0, 3, 1, 7)
+    rc = h.hga_shard_unpack(one, 64, 0, 2, 2, ctypes.cast(bad, ctypes.c_void_p), 1, 4, 32, one, None)
+    assert rc == -1 and b"block" in h.hga_last_error()
+
+
+def test_host_size_rules_match_the_reference():
+    """(N, Kc, Kg, Kg_request) of a prefill and (Kc, Kg) of a decode block: vectorized.py:304,
+    365-366 and chunk_router.py:226, 256."""
+    from hierarchicalglobalattention_b200 import ops
+    p = _p(chunk_size=64, group_size=16, topk_chunks=16, topk_groups=64)
+    assert ops.route_sizes(p, 32768) == (512, 16, 64, 32)
+    assert ops.route_sizes(p, 100) == (2, 2, 8, 8)
+    assert ops.route_sizes(_p(chunk_size=64, group_size=16, topk_chunks=16, topk_groups=1), 4096)[2] == 0
+    assert ops.decode_sizes(p, 502) == (16, 64)
+    assert ops.decode_sizes(p, 3) == (3, 12)
+    assert ops.decode_sizes(_p(topk_chunks=0), 10) == (0, 0)
