@@ -105,7 +105,8 @@ __global__ void __launch_bounds__(256) route_decode1_kernel(
   __syncthreads();
   // selection runs in warp 0 alone (shuffle reductions, no block barriers)
   if (warp == 0) {
-    warp_select(keys, n_mid, Kc, flag);
+    if (n_mid <= 512) warp_topk_small(keys, n_mid, Kc, flag);
+    else warp_select(keys, n_mid, Kc, flag);
     // the previous chunk replaces the lowest chosen one (ties: the highest index) when in the pool
     const int prev = n_closed - 1;
     if (prev >= f_hi && prev < l_lo && !flag[prev - f_hi]) {
@@ -144,7 +145,8 @@ __global__ void __launch_bounds__(256) route_decode1_kernel(
     keys[j] = ord_f32(ref_score<T>(dot_row<T, DH>(qs, gkb + ((size_t)idx[j / M] * M + (j % M)) * DH), p.scale));
   __syncthreads();
   if (warp == 0) {
-    warp_select(keys, Gs, Kgr < Gs ? Kgr : Gs, flag);
+    if (Gs <= 512) warp_topk_small(keys, Gs, Kgr < Gs ? Kgr : Gs, flag);
+    else warp_select(keys, Gs, Kgr < Gs ? Kgr : Gs, flag);
     int k = 0;
     for (int base = 0; base < Gs; base += 32) {
       const int j = base + lane;

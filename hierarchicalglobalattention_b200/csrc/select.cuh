@@ -100,6 +100,55 @@ __device__ __forceinline__ void warp_select(const uint32_t* keys, int n, int k, 
   __syncwarp();
 }
 
+// Warp-wide top-k of keys[0..n), n <= 512 (ordered-float keys, 0 = absent), ties resolved by lower
+// index — the same selection as warp_select.  Each lane sorts its 16 (key, index) pairs with a
+// bitonic network, then k rounds of warp max-reductions pop the largest remaining pair from its
+// owner lane: O(k) reductions instead of 32 radix passes over the keys.
+__device__ __forceinline__ void cas_desc64(unsigned long long& a, unsigned long long& b) {
+  const unsigned long long hi = a > b ? a : b, lo = a > b ? b : a;
+  a = hi;
+  b = lo;
+}
+__device__ __forceinline__ void warp_topk_small(const uint32_t* keys, int n, int k, unsigned char* flag) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long v[16];
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    const int i = lane + 32 * m;
+    const uint32_t key = i < n ? keys[i] : 0u;
+    v[m] = key ? ((unsigned long long)key << 32) | (0xffffffffu - (uint32_t)i) : 0ull;
+  }
+#pragma unroll
+  for (int size = 2; size <= 16; size <<= 1)
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          if ((i & size) == 0) cas_desc64(v[i], v[j]);
+          else cas_desc64(v[j], v[i]);
+        }
+      }
+  unsigned long long last = 0ull;
+  for (int it = 0; it < k; ++it) {
+    const uint32_t hi = __reduce_max_sync(0xffffffffu, (uint32_t)(v[0] >> 32));
+    if (hi == 0u) break;
+    const uint32_t lo = __reduce_max_sync(0xffffffffu, (uint32_t)(v[0] >> 32) == hi ? (uint32_t)v[0] : 0u);
+    last = ((unsigned long long)hi << 32) | lo;
+    if (v[0] == last) {  // the owner pops its head (pairs are unique)
+#pragma unroll
+      for (int m = 0; m < 15; ++m) v[m] = v[m + 1];
+      v[15] = 0ull;
+    }
+  }
+  for (int i = lane; i < n; i += 32) {
+    const unsigned long long c = keys[i] ? ((unsigned long long)keys[i] << 32) | (0xffffffffu - (uint32_t)i) : 0ull;
+    flag[i] = c != 0ull && c >= last;
+  }
+  __syncwarp();
+}
+
 // Insert key into a descending list of length k (list[k-1] is the current threshold).
 __device__ __forceinline__ void list_insert(unsigned long long* list, int k, unsigned long long key) {
   if (key <= list[k - 1]) return;
