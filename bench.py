@@ -424,6 +424,24 @@ def decode_bench(device, steps: int = 64, warmup: int = 8):
         summ = B * KVH * (S // C) * Dh * 2 + B * H * c["topk_chunks"] * (C // gs) * Dh * 2
         res[tier] = {"us_per_layer_step": us, "wall_us_per_step": wall_us, "cold_bytes_per_step": cold,
                      "hbm_bytes_per_step": hot + summ + (0 if tier == "ram" else cold)}
+        # the same steps replayed from a CUDA graph (DecodeStepGraph), continuing the sequences
+        from hierarchicalglobalattention_b200.decode_graph import DecodeStepGraph
+        graph = DecodeStepGraph(router, [0], [pos] * B, capacity_tokens=pos + n + 1, dtype=dt)
+        for i in range(n):
+            if i == warmup:
+                torch.cuda.synchronize()
+                t_wall = time.perf_counter()
+                e0.record()
+            graph.q[0].copy_(qs[i])
+            graph.k_rope[0].copy_(ks[i])
+            graph.k_raw[0].copy_(ks[i])
+            graph.v[0].copy_(ks[i])
+            graph.step()
+        e1.record()
+        torch.cuda.synchronize()
+        res[tier]["graph_us_per_layer_step"] = e0.elapsed_time(e1) * 1e3 / steps
+        res[tier]["graph_wall_us_per_step"] = (time.perf_counter() - t_wall) * 1e6 / steps
+        del graph
         if tier == "ram":
             res[tier]["host_link_GBps"] = cold / (us / 1e6) / 1e9
         del router, store

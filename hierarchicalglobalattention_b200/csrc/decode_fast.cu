@@ -6,7 +6,9 @@
 //  * routing, L = 1: with one row the pooled score of a chunk IS the row's score, so the block's
 //    top-Kc and the row's requests are the same set (every chosen chunk is visible from row 0),
 //    and the visible groups are the row's top-Kg_request among the chosen chunks' groups (a
-//    subset of the pooled top-Kg).  One thread scores one summary row with 16-byte loads.
+//    subset of the pooled top-Kg).  One CTA serves the query heads of one KV head that share
+//    it (up to 8): one thread scores one summary row for all of them with 16-byte loads, and the
+//    heads' selections run in separate warps.
 //  * attention: one warp streams one 16-token unit at a time (a window group, an opened group or
 //    a group of the active chunk).  The unit's K rows are read as whole lines (consecutive lanes,
 //    consecutive 16-byte pieces) and staged in shared memory, a lane pair then scores one key
@@ -32,23 +34,6 @@ __device__ __forceinline__ void unpack16(const uint4& u, float* f) {
   }
 }
 
-// q . row over DH elements, fp32 FMAs in column order (q in shared memory as fp32).
-template <typename T, int DH>
-__device__ __forceinline__ float dot_row(const float* qs, const T* row) {
-  constexpr int PER = 16 / (int)sizeof(T);
-  const uint4* r = reinterpret_cast<const uint4*>(row);
-  float acc = 0.f;
-#pragma unroll 4
-  for (int v = 0; v < DH / PER; ++v) {
-    const uint4 u = __ldg(r + v);
-    float f[PER];
-    unpack16<T>(u, f);
-#pragma unroll
-    for (int e = 0; e < PER; ++e) acc = fmaf(qs[v * PER + e], f[e], acc);
-  }
-  return acc;
-}
-
 // Ascending compaction of flag[0..n) by warp 0: writes idx[k] = i of the k-th set flag, returns k.
 __device__ __forceinline__ int warp_compact(const unsigned char* flag, int n, int* idx) {
   const int lane = threadIdx.x & 31;
@@ -63,23 +48,47 @@ __device__ __forceinline__ int warp_compact(const unsigned char* flag, int n, in
   return k;
 }
 
-template <typename T, int DH>
-__global__ void __launch_bounds__(256) route_decode1_kernel(
+// q_h . row for HB query heads at once (the row is read once, its 16-byte pieces all in flight);
+// every head's sum runs in column order with fp32 FMAs, like dot_row.
+template <typename T, int DH, int HB>
+__device__ __forceinline__ void dot_rows(const float* qs, const T* row, float* acc) {
+  constexpr int PER = 16 / (int)sizeof(T);
+  constexpr int NV = DH / PER;
+  const uint4* r = reinterpret_cast<const uint4*>(row);
+#pragma unroll
+  for (int j = 0; j < HB; ++j) acc[j] = 0.f;
+#pragma unroll 16
+  for (int v = 0; v < NV; ++v) {
+    const uint4 u = __ldg(r + v);
+    float f[PER];
+    unpack16<T>(u, f);
+#pragma unroll
+    for (int e = 0; e < PER; ++e)
+#pragma unroll
+      for (int j = 0; j < HB; ++j) acc[j] = fmaf(qs[j * DH + v * PER + e], f[e], acc[j]);
+  }
+}
+
+// One CTA routes HB query heads that share one KV head (h0 .. h0+HB-1 of batch row b): thread i
+// scores pool chunk i (and later candidate group i) for all HB heads from one read of the summary
+// row, then warp j selects head j's chunks and groups, the HB selections running side by side.
+template <typename T, int DH, int HB>
+__global__ void __launch_bounds__(256, 2) route_decode1_kernel(
     hga_params p, const T* __restrict__ q, const int32_t* __restrict__ seq_pos, const T* __restrict__ chunk_k,
     const T* __restrict__ group_k, int64_t sum_cap, int Kcmax, int Kgmax, int32_t* __restrict__ mid_chunk,
     int32_t* __restrict__ mid_t0, int32_t* __restrict__ open_gid, int32_t* __restrict__ open_t0, int nkey_max) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int h = blockIdx.x, b = blockIdx.y;
+  const int h0 = blockIdx.x * HB, b = blockIdx.y;
   const int H = p.nhead, KVH = p.kv_heads, C = p.chunk_size, M = C / p.group_size;
-  const int kvh = h / (H / KVH);
+  const int kvh = h0 / (H / KVH);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_closed = seq_pos[b] / C;
   int f_hi, l_lo;
   windows(n_closed, p.keep_first, p.keep_last, f_hi, l_lo);
   const int n_mid = l_lo > f_hi ? l_lo - f_hi : 0;
-  const size_t bh = (size_t)b * H + h;
-  for (int i = tid; i < Kcmax; i += blockDim.x) { mid_chunk[bh * Kcmax + i] = -1; mid_t0[bh * Kcmax + i] = -1; }
-  for (int i = tid; i < Kgmax; i += blockDim.x) { open_gid[bh * Kgmax + i] = -1; open_t0[bh * Kgmax + i] = -1; }
+  const size_t bh0 = (size_t)b * H + h0;
+  for (int i = tid; i < HB * Kcmax; i += blockDim.x) { mid_chunk[bh0 * Kcmax + i] = -1; mid_t0[bh0 * Kcmax + i] = -1; }
+  for (int i = tid; i < HB * Kgmax; i += blockDim.x) { open_gid[bh0 * Kgmax + i] = -1; open_t0[bh0 * Kgmax + i] = -1; }
   if (n_mid == 0 || p.topk_chunks <= 0) return;
   if ((int64_t)l_lo > sum_cap || n_mid > nkey_max) {
     if (tid == 0) atomicCAS(&g_decode_fast_error, 0, kErrBoundsRouteDecode);
@@ -90,30 +99,38 @@ __global__ void __launch_bounds__(256) route_decode1_kernel(
   const int Kg = p.topk_groups > 0 ? (p.topk_groups < G ? p.topk_groups : G) : 0;
   const int Kgr = p.topk_groups > 0 ? ((p.topk_groups / 2) < G ? p.topk_groups / 2 : G) : 0;
 
-  float* qs = (float*)smem;                                   // [DH]
-  uint32_t* keys = (uint32_t*)(qs + DH);                      // [nkey_max]
-  int* sred = (int*)(keys + nkey_max);                        // [16]
-  int* idx = sred + 16;                                       // [nkey_max]
-  unsigned char* flag = (unsigned char*)(idx + nkey_max);     // [nkey_max]
+  float* qs = (float*)smem;                                   // [HB][DH]
+  uint32_t* keys = (uint32_t*)(qs + HB * DH);                 // [HB][nkey_max]
+  int* sred = (int*)(keys + (size_t)HB * nkey_max);           // [16]
+  int* idx = sred + 16;                                       // [HB][nkey_max]
+  unsigned char* flag = (unsigned char*)(idx + (size_t)HB * nkey_max);   // [HB][nkey_max]
 
-  for (int i = tid; i < DH; i += blockDim.x) qs[i] = Num<T>::to_f(q[bh * DH + i]);
+  for (int i = tid; i < HB * DH; i += blockDim.x) qs[i] = Num<T>::to_f(q[bh0 * DH + i]);
   __syncthreads();
-  // ---- level 1: one thread per pool chunk ------------------------------------------------------
+  // ---- level 1: one thread per pool chunk, all HB heads ------------------------------------------
   const T* ckb = chunk_k + ((size_t)b * KVH + kvh) * sum_cap * DH;
-  for (int i = tid; i < n_mid; i += blockDim.x)
-    keys[i] = ord_f32(ref_score<T>(dot_row<T, DH>(qs, ckb + (size_t)(f_hi + i) * DH), p.scale));
+  for (int i = tid; i < n_mid; i += blockDim.x) {
+    float acc[HB];
+    dot_rows<T, DH, HB>(qs, ckb + (size_t)(f_hi + i) * DH, acc);
+#pragma unroll
+    for (int j = 0; j < HB; ++j) keys[(size_t)j * nkey_max + i] = ord_f32(ref_score<T>(acc[j], p.scale));
+  }
   __syncthreads();
-  // selection runs in warp 0 alone (shuffle reductions, no block barriers)
-  if (warp == 0) {
-    if (n_mid <= 512) warp_topk_small(keys, n_mid, Kc, flag);
-    else warp_select(keys, n_mid, Kc, flag);
+  // selection: warp j owns head j (shuffle reductions, no block barriers)
+  if (warp < HB) {
+    const size_t bh = bh0 + warp;
+    uint32_t* kw = keys + (size_t)warp * nkey_max;
+    unsigned char* fw = flag + (size_t)warp * nkey_max;
+    int* iw = idx + (size_t)warp * nkey_max;
+    if (n_mid <= 512) warp_topk_small(kw, n_mid, Kc, fw);
+    else warp_select(kw, n_mid, Kc, fw);
     // the previous chunk replaces the lowest chosen one (ties: the highest index) when in the pool
     const int prev = n_closed - 1;
-    if (prev >= f_hi && prev < l_lo && !flag[prev - f_hi]) {
+    if (prev >= f_hi && prev < l_lo && !fw[prev - f_hi]) {
       unsigned long long worst = ~0ull;
       for (int i = lane; i < n_mid; i += 32)
-        if (flag[i]) {
-          const unsigned long long c = ((unsigned long long)keys[i] << 32) | (0xffffffffu - (uint32_t)i);
+        if (fw[i]) {
+          const unsigned long long c = ((unsigned long long)kw[i] << 32) | (0xffffffffu - (uint32_t)i);
           worst = c < worst ? c : worst;
         }
       for (int o = 16; o; o >>= 1) {
@@ -121,40 +138,49 @@ __global__ void __launch_bounds__(256) route_decode1_kernel(
         worst = other < worst ? other : worst;
       }
       if (lane == 0) {
-        flag[0xffffffffu - (uint32_t)(worst & 0xffffffffull)] = 0;
-        flag[prev - f_hi] = 1;
+        fw[0xffffffffu - (uint32_t)(worst & 0xffffffffull)] = 0;
+        fw[prev - f_hi] = 1;
       }
       __syncwarp();
     }
-    const int k = warp_compact(flag, n_mid, idx);
+    const int k = warp_compact(fw, n_mid, iw);
     __syncwarp();
     for (int i = lane; i < k; i += 32) {
-      idx[i] += f_hi;
-      mid_chunk[bh * Kcmax + i] = idx[i];
+      iw[i] += f_hi;
+      mid_chunk[bh * Kcmax + i] = iw[i];
       mid_t0[bh * Kcmax + i] = 0;
     }
-    if (lane == 0) sred[8] = k;
+    if (lane == 0) sred[warp] = k;
   }
   __syncthreads();
-  const int ksel = sred[8];
   if (Kg <= 0 || Kgr <= 0) return;
-  // ---- level 2: one thread per candidate group of the chosen chunks ----------------------------
-  const int Gs = ksel * M;
+  // ---- level 2: one thread per (head, candidate group of its chosen chunks) ---------------------
   const T* gkb = group_k + ((size_t)b * KVH + kvh) * sum_cap * M * DH;
-  for (int j = tid; j < Gs; j += blockDim.x)
-    keys[j] = ord_f32(ref_score<T>(dot_row<T, DH>(qs, gkb + ((size_t)idx[j / M] * M + (j % M)) * DH), p.scale));
+  for (int t = tid; t < HB * G; t += blockDim.x) {
+    const int j = t / G, g = t - j * G;
+    if (g < sred[j] * M) {
+      float acc[1];
+      dot_rows<T, DH, 1>(qs + j * DH, gkb + ((size_t)idx[(size_t)j * nkey_max + g / M] * M + (g % M)) * DH, acc);
+      keys[(size_t)j * nkey_max + g] = ord_f32(ref_score<T>(acc[0], p.scale));
+    }
+  }
   __syncthreads();
-  if (warp == 0) {
-    if (Gs <= 512) warp_topk_small(keys, Gs, Kgr < Gs ? Kgr : Gs, flag);
-    else warp_select(keys, Gs, Kgr < Gs ? Kgr : Gs, flag);
+  if (warp < HB) {
+    const size_t bh = bh0 + warp;
+    uint32_t* kw = keys + (size_t)warp * nkey_max;
+    unsigned char* fw = flag + (size_t)warp * nkey_max;
+    const int* iw = idx + (size_t)warp * nkey_max;
+    const int Gs = sred[warp] * M;
+    if (Gs <= 512) warp_topk_small(kw, Gs, Kgr < Gs ? Kgr : Gs, fw);
+    else warp_select(kw, Gs, Kgr < Gs ? Kgr : Gs, fw);
     int k = 0;
     for (int base = 0; base < Gs; base += 32) {
       const int j = base + lane;
-      const bool f = j < Gs && flag[j];
+      const bool f = j < Gs && fw[j];
       const unsigned bal = __ballot_sync(0xffffffffu, f);
       if (f) {
         const int at = k + __popc(bal & ((1u << lane) - 1u));
-        open_gid[bh * Kgmax + at] = idx[j / M] * M + (j % M);
+        open_gid[bh * Kgmax + at] = iw[j / M] * M + (j % M);
         open_t0[bh * Kgmax + at] = 0;
       }
       k += __popc(bal);
@@ -162,8 +188,35 @@ __global__ void __launch_bounds__(256) route_decode1_kernel(
   }
 }
 
-size_t route_decode1_smem(int Dh, int nkey_max) {
-  return (size_t)Dh * 4 + (size_t)nkey_max * 4 + 64 + (size_t)nkey_max * 4 + (size_t)nkey_max + 16;
+size_t route_decode1_smem(int Dh, int nkey_max, int hb) {
+  return (size_t)hb * Dh * 4 + (size_t)hb * nkey_max * 4 + 64 + (size_t)hb * nkey_max * 4 + (size_t)hb * nkey_max +
+         16;
+}
+
+// Heads per CTA: the largest of 8, 4, 2 that divides the query heads of one KV head and still
+// leaves at least one CTA per SM (148 SMs), else 1 (small batches route with the most CTAs).
+static int route_decode1_heads(const hga_params& p) {
+  const int rep = p.nhead / p.kv_heads;
+  for (int hb = 8; hb > 1; hb >>= 1)
+    if (rep % hb == 0 && (int64_t)p.batch * (p.nhead / hb) >= 148) return hb;
+  return 1;
+}
+
+template <typename T, int DH, int HB>
+static cudaError_t launch_route_decode1_h(const hga_params& p, const void* q, const int32_t* seq_pos, const void* ck,
+                                          const void* gk, int64_t sum_cap, int nkey, int Kcmax, int Kgmax,
+                                          int32_t* mc, int32_t* mt, int32_t* og, int32_t* ot, cudaStream_t st) {
+  const size_t smem = route_decode1_smem(DH, nkey, HB);
+  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
+  auto kern = route_decode1_kernel<T, DH, HB>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid(p.nhead / HB, p.batch);
+  kern<<<grid, 256, smem, st>>>(p, (const T*)q, seq_pos, (const T*)ck, (const T*)gk, sum_cap, Kcmax, Kgmax, mc, mt,
+                                og, ot, nkey);
+  return cudaGetLastError();
 }
 
 template <typename T, int DH>
@@ -172,17 +225,12 @@ static cudaError_t launch_route_decode1_t(const hga_params& p, const void* q, co
                                           int32_t* mc, int32_t* mt, int32_t* og, int32_t* ot, cudaStream_t st) {
   const int M = p.chunk_size / p.group_size;
   const int nkey = nmid_max > Kcmax * M ? nmid_max : Kcmax * M;
-  const size_t smem = route_decode1_smem(DH, nkey);
-  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
-  auto kern = route_decode1_kernel<T, DH>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+  switch (route_decode1_heads(p)) {
+    case 8: return launch_route_decode1_h<T, DH, 8>(p, q, seq_pos, ck, gk, sum_cap, nkey, Kcmax, Kgmax, mc, mt, og, ot, st);
+    case 4: return launch_route_decode1_h<T, DH, 4>(p, q, seq_pos, ck, gk, sum_cap, nkey, Kcmax, Kgmax, mc, mt, og, ot, st);
+    case 2: return launch_route_decode1_h<T, DH, 2>(p, q, seq_pos, ck, gk, sum_cap, nkey, Kcmax, Kgmax, mc, mt, og, ot, st);
+    default: return launch_route_decode1_h<T, DH, 1>(p, q, seq_pos, ck, gk, sum_cap, nkey, Kcmax, Kgmax, mc, mt, og, ot, st);
   }
-  dim3 grid(p.nhead, p.batch);
-  kern<<<grid, 256, smem, st>>>(p, (const T*)q, seq_pos, (const T*)ck, (const T*)gk, sum_cap, Kcmax, Kgmax, mc, mt,
-                                og, ot, nkey);
-  return cudaGetLastError();
 }
 
 bool route_decode1_supported(const hga_params& p, int L) {

@@ -59,6 +59,8 @@ def close_chunk(router, layer: int, hp, n, rows=None) -> None:
     C = router.cfg.chunk_size
     st = store.layer_buffers(layer)
     act = store.active_raw(layer)
+    if rows is not None and len(rows) == act.shape[0] and len(set(n)) == 1 and list(rows) == list(range(len(rows))):
+        rows, n = None, n[0]          # every row closes the same chunk: one batched launch
     if rows is None:
         k_act, v_act = store.active_rows(layer, n)
         cos, sin = router.chunk_rotary(n, act.device)
