@@ -360,8 +360,9 @@ CFG2 = dict(batch=16, ctx=32768, nhead=32, kv_heads=4, head_dim=128, chunk_size=
 
 def decode_bench(device, steps: int = 64, warmup: int = 8):
     """batched decode step (B=16 sequences, 32768 cached tokens each, one new token per
-    sequence), one layer, through ChunkRouter.decode_block + RoutedKV.attend.  Timed per tier:
-    RAM (cold record in pinned host memory, windows in HBM; the config's tier) and VRAM."""
+    sequence), one layer, through ChunkRouter.decode_block + RoutedKV.attend and replayed from a
+    CUDA graph (DecodeStepGraph).  Timed per tier: RAM (cold record in pinned host memory, windows
+    in HBM; the config's tier) and VRAM, then VRAM with one sequence (a launch-bound step)."""
     from hierarchicalglobalattention_b200 import ChunkPlacementPolicy, ChunkRouter, RouterConfig, VramKVCacheStore
     from hierarchicalglobalattention_b200.store_ram import RamKVCacheStore
     c = CFG2
@@ -382,7 +383,9 @@ def decode_bench(device, steps: int = 64, warmup: int = 8):
     torch.cuda.synchronize()
     res["h2d_copy_GBps"] = 4 * hbuf.numel() / (e0.elapsed_time(e1) / 1e3) / 1e9
     del hbuf, dbuf
-    for tier in ("ram", "vram"):
+    B16 = B
+    # the config's batch in both tiers, then one sequence (VRAM tier), where a step is launch-bound
+    for tier, B in (("ram", B16), ("vram", B16), ("vram_b1", 1)):
         cfg = RouterConfig(nhead=H, kv_heads=KVH, head_dim=Dh, chunk_size=C, group_size=gs,
                            topk_chunks=c["topk_chunks"], topk_groups=c["topk_groups"], theta=c["theta"])
         pol = ChunkPlacementPolicy(keep_first=c["keep_first"], keep_last=c["keep_last"], first_token_level=True)
@@ -427,15 +430,13 @@ def decode_bench(device, steps: int = 64, warmup: int = 8):
         # the same steps replayed from a CUDA graph (DecodeStepGraph), continuing the sequences
         from hierarchicalglobalattention_b200.decode_graph import DecodeStepGraph
         graph = DecodeStepGraph(router, [0], [pos] * B, capacity_tokens=pos + n + 1, dtype=dt)
+        packed = torch.cat([t.reshape(n, -1) for t in (qs, ks, ks, ks)], dim=1)   # graph.inputs' layout
         for i in range(n):
             if i == warmup:
                 torch.cuda.synchronize()
                 t_wall = time.perf_counter()
                 e0.record()
-            graph.q[0].copy_(qs[i])
-            graph.k_rope[0].copy_(ks[i])
-            graph.k_raw[0].copy_(ks[i])
-            graph.v[0].copy_(ks[i])
+            graph.inputs[0].copy_(packed[i])
             graph.step()
         e1.record()
         torch.cuda.synchronize()

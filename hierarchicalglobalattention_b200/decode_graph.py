@@ -46,10 +46,15 @@ class DecodeStepGraph:
             raise ValueError("seq_pos beyond capacity_tokens")
         self.seq_pos = torch.tensor(seq_pos_host, dtype=torch.int32, device=dev)
         n = len(self.layers)
-        self.q = torch.zeros(n, B, H, 1, Dh, device=dev, dtype=dtype)
-        self.k_rope = torch.zeros(n, B, KVH, 1, Dh, device=dev, dtype=dtype)
-        self.k_raw = torch.zeros_like(self.k_rope)
-        self.v = torch.zeros_like(self.k_rope)
+        # one flat input vector per layer holding q [B,H,1,Dh] | k_rope | k_raw | v [B,KVH,1,Dh],
+        # each segment contiguous: a caller fills a step with one copy per layer, and the kernels
+        # read the segments in place
+        nq, nk = B * H * Dh, B * KVH * Dh
+        self.inputs = torch.zeros(n, nq + 3 * nk, device=dev, dtype=dtype)
+        self.q = self.inputs[:, :nq].view(n, B, H, 1, Dh)
+        self.k_rope = self.inputs[:, nq:nq + nk].view(n, B, KVH, 1, Dh)
+        self.k_raw = self.inputs[:, nq + nk:nq + 2 * nk].view(n, B, KVH, 1, Dh)
+        self.v = self.inputs[:, nq + 2 * nk:].view(n, B, KVH, 1, Dh)
         self.out = torch.zeros(n, B, H, 1, Dh, device=dev, dtype=dtype)
         self.graph = torch.cuda.CUDAGraph()
         self._capture()
@@ -84,9 +89,10 @@ class DecodeStepGraph:
             self._launch_all()
 
     def step(self) -> torch.Tensor:
-        """Replay one step on the inputs already written into ``q`` / ``k_rope`` / ``k_raw`` / ``v``
-        ([layers, B, heads, 1, Dh]); returns ``out`` [layers, B, H, 1, Dh] (overwritten by the next
-        step).  Chunks completed by this step are closed afterwards, on the host's schedule."""
+        """Replay one step on the inputs already written into ``inputs`` [layers, flat] (or
+        through its views ``q`` / ``k_rope`` / ``k_raw`` / ``v``, [layers, B, heads, 1, Dh]); returns ``out``
+        [layers, B, H, 1, Dh] (overwritten by the next step).  Chunks completed by this step are
+        closed afterwards, on the host's schedule."""
         C = self.C
         if max(self.pos_host) >= self.capacity:
             raise RuntimeError("DecodeStepGraph: a sequence reached capacity_tokens; build a larger graph")

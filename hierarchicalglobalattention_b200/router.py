@@ -118,23 +118,31 @@ class ChunkRouter:
             self._rot_cache[key] = cached
         return cached
 
+    _ROT_BLOCK = 64   # chunks per cached close table
+
     def chunk_rotary(self, n: int, device) -> Tuple[torch.Tensor, torch.Tensor]:
         """fp32 cos/sin ``[C, Dh]`` for the positions of chunk n (rows [n*C, n*C + C)), as the
         chunk-close summaries read them (their anchors, chunk_router.py:702-709).  Built on the host
-        for a few KB per chunk and kept for the layers that close the same chunk."""
-        key = (str(device), n)
+        (the same elementwise arange * inv_freq and cos/sin as a per-chunk table) for a block of
+        64 chunks at a time and kept on the device, so the pinned staging copy - whose allocation
+        can wait for the device - happens once per 64 closed chunks, not at every close."""
+        blk = n // self._ROT_BLOCK
+        key = (str(device), blk)
         t = self._close_rot.get(key)
         if t is None:
-            if len(self._close_rot) > 256:
+            if len(self._close_rot) > 8:
                 self._close_rot.clear()
             C, half = self.cfg.chunk_size, self.cfg.head_dim // 2
             inv = 1.0 / (self.cfg.theta ** (torch.arange(half, dtype=torch.float32) / half))
-            f = torch.arange(n * C, n * C + C, dtype=torch.float32).unsqueeze(-1) * inv
+            r0 = blk * self._ROT_BLOCK * C
+            f = torch.arange(r0, r0 + self._ROT_BLOCK * C, dtype=torch.float32).unsqueeze(-1) * inv
             emb = torch.cat((f, f), dim=-1)
             t = (emb.cos().pin_memory().to(device, non_blocking=True),
                  emb.sin().pin_memory().to(device, non_blocking=True))
             self._close_rot[key] = t
-        return t
+        C = self.cfg.chunk_size
+        lo = (n - blk * self._ROT_BLOCK) * C
+        return t[0][lo:lo + C], t[1][lo:lo + C]
 
     # ---------------------------------------------------------------------------------------
     def route_query_block(self, layer: int, q: torch.Tensor, k_rope: torch.Tensor, k_raw: torch.Tensor,
