@@ -118,31 +118,49 @@ class ChunkRouter:
             self._rot_cache[key] = cached
         return cached
 
-    _ROT_BLOCK = 64   # chunks per cached close table
+    _ROT_RING = 16    # pinned staging slots for close tables
+
+    def _rot_stage_ready(self) -> None:
+        """Allocate the pinned staging ring of the close tables (1 MB at C=64, Dh=128) once, when a
+        context is loaded for decode, rather than at the first chunk close of a decode loop."""
+        if getattr(self, "_rot_stage", None) is None:
+            C, Dh = self.cfg.chunk_size, self.cfg.head_dim
+            self._rot_stage = torch.empty(self._ROT_RING, 2, C, Dh, dtype=torch.float32).pin_memory()
+            self._rot_events = [None] * self._ROT_RING
+            self._rot_slot = 0
 
     def chunk_rotary(self, n: int, device) -> Tuple[torch.Tensor, torch.Tensor]:
         """fp32 cos/sin ``[C, Dh]`` for the positions of chunk n (rows [n*C, n*C + C)), as the
         chunk-close summaries read them (their anchors, chunk_router.py:702-709).  Built on the host
-        (the same elementwise arange * inv_freq and cos/sin as a per-chunk table) for a block of
-        64 chunks at a time and kept on the device, so the pinned staging copy - whose allocation
-        can wait for the device - happens once per 64 closed chunks, not at every close."""
-        blk = n // self._ROT_BLOCK
-        key = (str(device), blk)
+        for a few KB per chunk and kept for the layers that close the same chunk.  The host table
+        goes through a ring of pinned staging slots allocated once: a fresh pinned allocation
+        per close could wait for the whole queued decode work, and a slot is reused only after
+        the copy issued from it 16 closes earlier has completed."""
+        key = (str(device), n)
         t = self._close_rot.get(key)
         if t is None:
-            if len(self._close_rot) > 8:
+            if len(self._close_rot) > 256:
                 self._close_rot.clear()
-            C, half = self.cfg.chunk_size, self.cfg.head_dim // 2
+            C, Dh = self.cfg.chunk_size, self.cfg.head_dim
+            half = Dh // 2
             inv = 1.0 / (self.cfg.theta ** (torch.arange(half, dtype=torch.float32) / half))
-            r0 = blk * self._ROT_BLOCK * C
-            f = torch.arange(r0, r0 + self._ROT_BLOCK * C, dtype=torch.float32).unsqueeze(-1) * inv
+            f = torch.arange(n * C, n * C + C, dtype=torch.float32).unsqueeze(-1) * inv
             emb = torch.cat((f, f), dim=-1)
-            t = (emb.cos().pin_memory().to(device, non_blocking=True),
-                 emb.sin().pin_memory().to(device, non_blocking=True))
+            self._rot_stage_ready()
+            slot = self._rot_slot
+            self._rot_slot = (slot + 1) % self._ROT_RING
+            if self._rot_events[slot] is not None:
+                self._rot_events[slot].synchronize()
+            stage = self._rot_stage[slot]
+            torch.cos(emb, out=stage[0])
+            torch.sin(emb, out=stage[1])
+            dev_t = stage.to(device, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(device))
+            self._rot_events[slot] = ev
+            t = (dev_t[0], dev_t[1])
             self._close_rot[key] = t
-        C = self.cfg.chunk_size
-        lo = (n - blk * self._ROT_BLOCK) * C
-        return t[0][lo:lo + C], t[1][lo:lo + C]
+        return t
 
     # ---------------------------------------------------------------------------------------
     def route_query_block(self, layer: int, q: torch.Tensor, k_rope: torch.Tensor, k_raw: torch.Tensor,
@@ -222,6 +240,7 @@ class ChunkRouter:
         B = k_rope.shape[0]
         hp1 = copy.copy(cfg.hga_params(store.policy, B, k_rope.dtype))
         hp1.batch = 1
+        self._rot_stage_ready()
         nmax = max(seq_lens) // C
         st = store.ensure_capacity(layer, max(nmax, 1), max(seq_lens) + C)
         store.write_tokens(layer, 0, k_rope, v)
@@ -240,6 +259,7 @@ class ChunkRouter:
     def _seed_store(self, layer, hp, k_rope, k_raw, v, S):
         """Store seed of a fresh prefill (chunk_router.py:553-599): summaries of the closed chunks with
         fixed anchors and fp32 rotary rows, token rows, and the partial active chunk."""
+        self._rot_stage_ready()
         cfg, store = self.cfg, self.store
         C = cfg.chunk_size
         n_closed = S // C
