@@ -540,12 +540,17 @@ def attend_decode(p: OracleParams, q, keys, vals, key_first_row):
     return torch.einsum("bhlr,bhrd->bhld", torch.softmax(s, -1), vals.float()).to(vals.dtype)
 
 
-def decode_sequence(p: OracleParams, q, k_rope, k_raw, v, block: int, start_pos: int = 0):
+def decode_sequence(p: OracleParams, q, k_rope, k_raw, v, block: int, start_pos: int = 0, calls=None,
+                    attend=None):
     """The reference's incremental path over a whole sequence: ``ChunkRouter.decode_block`` fed
     block by block and chunk-aligned (chunk_router.py:279-442), token-only attention.
 
     q ``[B,H,S,Dh]``, k_* / v ``[B,KVH,S,Dh]`` cover positions [0, S); rows before ``start_pos``
     are the already-closed prefix (its chunks are summarised exactly like closed decode chunks).
+    ``calls`` (default ``[(start_pos, S)]``) are the caller's forward calls: each is fed in pieces
+    of at most ``block`` tokens that never cross a chunk boundary (route_query_block,
+    chunk_router.py:500-516).  ``attend(pos, L, rows, first)`` replaces the flat token attention
+    (rows ``[B,H,R]`` absolute key positions, first ``[B,H,R]`` the first query row seeing each).
     Returns (out ``[B,H,S-start_pos,Dh]``, list of per-block dicts with ``pos``, ``L``, the
     routing result and its tie flag).
     """
@@ -555,34 +560,100 @@ def decode_sequence(p: OracleParams, q, k_rope, k_raw, v, block: int, start_pos:
     kv_of_h = torch.arange(H) // rep
     bi = torch.arange(B).view(B, 1, 1)
     hi_ = kv_of_h.view(1, H, 1)
+    if attend is None:
+        def attend(pos, L, rows_t, first_t):
+            return attend_decode(p, q[:, :, pos:pos + L], k_rope[bi, hi_, rows_t], v[bi, hi_, rows_t], first_t)
     outs, blocks = [], []
-    pos = start_pos
-    while pos < S:
-        L = min(block, C - pos % C, S - pos)
-        n, c0 = pos // C, pos % C
-        f_hi, l_lo = _windows(p, n)
-        qb = q[:, :, pos:pos + L]
-        r = route_decode(p, qb, ck_all[:, :, f_hi:max(l_lo, f_hi)],
-                         lambda mid: gk_all[bi, hi_, mid], f_hi, n)
-        rows, first = [], []
-        win = list(range(0, f_hi * C)) + list(range(l_lo * C, n * C))
-        if win:
-            rows.append(torch.tensor(win).view(1, 1, -1).expand(B, H, -1))
-            first.append(torch.zeros(B, H, len(win), dtype=torch.long))
-        if r["open_chunk"].shape[-1]:
-            base = (r["open_chunk"] * C + r["open_grp"] * gs).unsqueeze(-1) + torch.arange(gs)
-            rows.append(base.reshape(B, H, -1))
-            first.append(r["open_t0"].unsqueeze(-1).expand(*r["open_t0"].shape, gs).reshape(B, H, -1))
-        act = torch.arange(n * C, n * C + c0 + L)
-        rows.append(act.view(1, 1, -1).expand(B, H, -1))
-        first.append((torch.arange(c0 + L) - c0).view(1, 1, -1).expand(B, H, -1))
-        rows_t, first_t = torch.cat(rows, -1), torch.cat(first, -1)
-        keys = k_rope[bi, hi_, rows_t]
-        vals = v[bi, hi_, rows_t]
-        outs.append(attend_decode(p, qb, keys, vals, first_t))
-        blocks.append({"pos": pos, "L": L, "route": r})
-        pos += L
+    for lo, hi in (calls if calls is not None else [(start_pos, S)]):
+        pos = lo
+        while pos < hi:
+            L = min(block, C - pos % C, hi - pos)
+            n, c0 = pos // C, pos % C
+            f_hi, l_lo = _windows(p, n)
+            qb = q[:, :, pos:pos + L]
+            r = route_decode(p, qb, ck_all[:, :, f_hi:max(l_lo, f_hi)],
+                             lambda mid: gk_all[bi, hi_, mid], f_hi, n)
+            rows, first = [], []
+            win = list(range(0, f_hi * C)) + list(range(l_lo * C, n * C))
+            if win:
+                rows.append(torch.tensor(win).view(1, 1, -1).expand(B, H, -1))
+                first.append(torch.zeros(B, H, len(win), dtype=torch.long))
+            if r["open_chunk"].shape[-1]:
+                base = (r["open_chunk"] * C + r["open_grp"] * gs).unsqueeze(-1) + torch.arange(gs)
+                rows.append(base.reshape(B, H, -1))
+                first.append(r["open_t0"].unsqueeze(-1).expand(*r["open_t0"].shape, gs).reshape(B, H, -1))
+            act = torch.arange(n * C, n * C + c0 + L)
+            rows.append(act.view(1, 1, -1).expand(B, H, -1))
+            first.append((torch.arange(c0 + L) - c0).view(1, 1, -1).expand(B, H, -1))
+            outs.append(attend(pos, L, torch.cat(rows, -1), torch.cat(first, -1)))
+            blocks.append({"pos": pos, "L": L, "route": r})
+            pos += L
     return torch.cat(outs, dim=2), blocks
+
+
+# ---------------------------------------------------------------------------------------------
+# Dual Chunk Attention (the Qwen3 wrapper's dca_chunk > 0 path)
+# ---------------------------------------------------------------------------------------------
+DCA_NEG = -1.0e4  # finite mask fill of the DCA attention (qwen_routed_attention.py:63)
+
+
+def dca_rope_table(positions: torch.Tensor, head_dim: int, theta: float, dtype: torch.dtype):
+    """Default-RoPE cos/sin ``[*positions.shape, Dh]`` at (remapped) positions, cast to ``dtype``
+    (qwen_routed_attention.py:66-81)."""
+    half = head_dim // 2
+    inv = 1.0 / (theta ** (torch.arange(half, dtype=torch.float32) / half))
+    f = positions.to(torch.float32).unsqueeze(-1) * inv
+    emb = torch.cat((f, f), dim=-1)
+    return emb.cos().to(dtype), emb.sin().to(dtype)
+
+
+def dca_apply(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """rotate-half RoPE evaluated in x's dtype, each operation rounded like the reference's
+    (qwen_routed_attention.py:84-88)."""
+    half = x.shape[-1] // 2
+    return x * cos + torch.cat((-x[..., half:], x[..., :half]), dim=-1) * sin
+
+
+def dca_sequence(p: OracleParams, q_raw, k_raw, v, dca_chunk: int, dca_local: int, calls):
+    """The wrapper's Dual Chunk Attention over a sequence fed as forward ``calls`` [(lo, hi)]
+    (qwen_routed_attention.py:210-283).
+
+    Keys are roped at their intra-chunk position ``pos % dca_chunk`` and routed with intra-roped
+    queries through the incremental path (route_query_block with return_positions); each query
+    then scores a key with one of three ropings of itself, chosen by the two DCA-chunk indices:
+    intra (same chunk, position pos % L_c), successor (the chunk just before, min(pos % L_c + L_c,
+    ceil)) or inter (any earlier chunk, ceil), ceil = dca_chunk + dca_local.  q_raw ``[B,H,S,Dh]``
+    and k_raw / v ``[B,KVH,S,Dh]`` are pre-RoPE.  Returns (out ``[B,H,S,Dh]``, routing blocks).
+    """
+    B, H, S, Dh = q_raw.shape
+    L_c, ceil = dca_chunk, dca_chunk + dca_local
+    pos = torch.arange(S)
+    c_, s_ = dca_rope_table(pos % L_c, Dh, p.theta, k_raw.dtype)
+    k_dca = dca_apply(k_raw, c_, s_)
+    q_sel = dca_apply(q_raw, c_, s_)
+    bi = torch.arange(B).view(B, 1, 1)
+    hi_ = (torch.arange(H) // p.rep).view(1, H, 1)
+
+    def attend(pos0, L, rows_t, first_t):
+        qf = q_raw[:, :, pos0:pos0 + L].float()
+        qpos = torch.arange(pos0, pos0 + L)
+        qp = qpos % L_c
+        q_i = dca_apply(qf, *dca_rope_table(qp, Dh, p.theta, torch.float32))
+        q_s = dca_apply(qf, *dca_rope_table((qp + L_c).clamp(max=ceil), Dh, p.theta, torch.float32))
+        q_t = dca_apply(qf, *dca_rope_table(torch.full_like(qpos, ceil), Dh, p.theta, torch.float32))
+        kf = k_dca[bi, hi_, rows_t].float()
+        vals = v[bi, hi_, rows_t]
+        s_i = torch.einsum("bhld,bhrd->bhlr", q_i, kf) * p.scale
+        s_s = torch.einsum("bhld,bhrd->bhlr", q_s, kf) * p.scale
+        s_t = torch.einsum("bhld,bhrd->bhlr", q_t, kf) * p.scale
+        cq = (qpos // L_c).view(1, 1, L, 1)
+        ck = (rows_t // L_c).unsqueeze(2)
+        sc = torch.where(ck == cq, s_i, torch.where(ck == cq - 1, s_s, s_t))
+        seen = torch.arange(L).view(1, 1, L, 1) >= first_t.unsqueeze(2)
+        sc = sc.masked_fill(~seen, DCA_NEG)
+        return torch.einsum("bhlr,bhrd->bhld", torch.softmax(sc, -1), vals.float()).to(vals.dtype)
+
+    return decode_sequence(p, q_sel, k_dca, k_raw, v, p.chunk_size, calls=calls, attend=attend)
 
 
 # ---------------------------------------------------------------------------------------------

@@ -59,6 +59,14 @@ CASES = [
     dict(name="qwen_wrap_fp32", kind="qwen", dtype=F32, seed=21, B=1, S=1100, prefix=1024, block=19, row_step=3,
          d_model=512, params=_p(nhead=8, kv_heads=2, head_dim=64, chunk_size=64, group_size=16, topk_chunks=4,
                                 topk_groups=8, keep_first=1, keep_last=2, theta=1e6)),
+    # Dual Chunk Attention of the Qwen3 wrapper (dca_chunk > 0): pre-RoPE q / k and v fed as a
+    # `prefix` call and then `block`-token calls (qwen_routed_attention.py:210-283).
+    dict(name="dca_fp32", kind="dca", dtype=F32, seed=22, B=1, S=300, prefix=100, block=7, dca_chunk=32,
+         dca_local=8, params=_p(nhead=4, kv_heads=2, head_dim=32, chunk_size=16, group_size=4, topk_chunks=3,
+                                topk_groups=6, keep_first=1, keep_last=2, theta=1e4)),
+    dict(name="dca_bf16", kind="dca", dtype=BF16, seed=23, B=2, S=400, prefix=130, block=5, dca_chunk=64, row_step=4,
+         dca_local=12, params=_p(nhead=8, kv_heads=2, head_dim=64, chunk_size=16, group_size=4, topk_chunks=3,
+                                 topk_groups=6, keep_first=1, keep_last=2, theta=1e4)),
 ]
 
 
@@ -86,6 +94,16 @@ def make_inputs(c):
     cos, sin = module_rotary(p.theta, Dh, S)
     return {"q": rope_apply(q_raw, cos, sin), "k_rope": rope_apply(k_raw, cos, sin), "k_raw": k_raw,
             "v": v, "cos": cos.to(dtype), "sin": sin.to(dtype)}
+
+
+def make_dca_inputs(c):
+    """Pre-RoPE q [B,H,S,Dh], k_raw and v [B,KVH,S,Dh], N(0, 1) in the case dtype."""
+    p, B, S, dtype = c["params"], c["B"], c["S"], c["dtype"]
+    g = torch.Generator().manual_seed(c["seed"])
+    H, KVH, Dh = p.nhead, p.kv_heads, p.head_dim
+    return {"q": torch.randn(B, H, S, Dh, generator=g).to(dtype),
+            "k_raw": torch.randn(B, KVH, S, Dh, generator=g).to(dtype),
+            "v": torch.randn(B, KVH, S, Dh, generator=g).to(dtype)}
 
 
 def make_module_inputs(c):
@@ -175,6 +193,6 @@ def load(name):
     return torch.load(fixture_path(name), weights_only=False)
 
 
-__all__ = ["CASES", "case", "make_inputs", "make_module_inputs", "make_qwen_inputs", "qwen_config",
+__all__ = ["CASES", "case", "make_inputs", "make_dca_inputs", "make_module_inputs", "make_qwen_inputs", "qwen_config",
            "load_qwen_weights", "qwen_schedule", "output_rows", "checksum", "load",
            "rope_apply", "math"]

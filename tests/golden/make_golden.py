@@ -7,7 +7,7 @@ Run here (where the reference checkout is readable):
 Each case draws seeded inputs (``cases.make_inputs``), runs the reference's own code path
 (``assemble_routed_kv`` + ``RoutedKV.attend`` for prefill, ``ChunkRouter.decode_block`` +
 ``attend`` for the incremental path, the ``HierarchicalGlobalAttentionRouted`` module for the
-module case) and stores the outputs and routing decisions as ``tests/golden/<case>.pt``.
+module case, the Qwen3 wrapper's Dual Chunk Attention methods for the DCA cases) and stores the outputs and routing decisions as ``tests/golden/<case>.pt``.
 Routing decisions are captured by wrapping the reference's own gather helpers, which receive
 the selected chunk / group indices (vectorized.py:339, 388) — the reference is not modified.
 Large tensors (inputs) are NOT stored; they are regenerated from the seed and checked with a
@@ -220,6 +220,41 @@ def run_qwen_case(ref, case):
             "out": out[:, rows].clone()}
 
 
+def run_dca_case(ref, case):
+    """The reference wrapper's Dual Chunk Attention (QwenRoutedAttention._dca_forward and
+    _dca_attend, qwen_routed_attention.py:210-283) over the case's call schedule.  The two methods
+    read only the attributes set below, so they run on a plain namespace carrying them, with an
+    identity o_proj (the output is then the concatenated heads)."""
+    import types
+    _, ChunkRouter, RouterConfig, VramKVCacheStore, _, Policy, hgar = ref
+    qra = hgar.__qwen__
+    p = case["params"]
+    inp = cases.make_dca_inputs(case)
+    q, k_raw, v = inp["q"], inp["k_raw"], inp["v"]
+    B, H, S, Dh = q.shape
+    C, gs = p.chunk_size, p.group_size
+    cfg = RouterConfig(nhead=p.nhead, kv_heads=p.kv_heads, head_dim=Dh, chunk_size=C, group_size=gs,
+                       topk_chunks=p.topk_chunks, topk_groups=p.topk_groups, theta=p.theta)
+    policy = Policy(keep_first=p.keep_first, keep_last=p.keep_last, first_token_level=True)
+    store = VramKVCacheStore(compute_device=torch.device("cpu"), policy=policy, kv_heads=p.kv_heads,
+                             head_dim=Dh, chunk_size=C, groups_per_chunk=C // gs, batch_size=B, dtype=q.dtype)
+    router = ChunkRouter(cfg, store)
+    w = types.SimpleNamespace(num_heads=H, num_kv_heads=p.kv_heads, head_dim=Dh, layer_idx=0, _cfg=cfg,
+                              dca_chunk=case["dca_chunk"], dca_ceil=case["dca_chunk"] + case["dca_local"])
+    w._dca_attend = lambda qb, routed, qpos: qra.QwenRoutedAttention._dca_attend(w, qb, routed, qpos)
+    o = types.SimpleNamespace(o_proj=lambda x: x)
+    outs = []
+    with torch.no_grad():
+        for lo, hi in cases.qwen_schedule(case):
+            y, _ = qra.QwenRoutedAttention._dca_forward(w, o, q[:, :, lo:hi], k_raw[:, :, lo:hi],
+                                                        v[:, :, lo:hi], lo, router, B, hi - lo)
+            outs.append(y.view(B, hi - lo, H, Dh).transpose(1, 2))
+    out = torch.cat(outs, dim=2)
+    rows = cases.output_rows(case, S)
+    return {"name": case["name"], "input_checksum": cases.checksum(inp), "out_rows": rows,
+            "out": out[:, :, rows].clone()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("HGA_REFERENCE_ROOT"),
@@ -235,7 +270,8 @@ def main():
             continue
         kind = case["kind"]
         fn = {"prefill": run_prefill_case, "summary": run_summary_case,
-              "incremental": run_incremental_case, "module": run_module_case, "qwen": run_qwen_case}[kind]
+              "incremental": run_incremental_case, "module": run_module_case, "qwen": run_qwen_case,
+              "dca": run_dca_case}[kind]
         gold = fn(ref, case)
         path = os.path.join(HERE, f"{case['name']}.pt")
         torch.save(gold, path)

@@ -79,3 +79,16 @@ def test_incremental_decode_matches_reference(name):
     assert torch.equal(ck[:, :, :n], g["store_chunk_k"])
     tol = 1e-5 if c["dtype"] == torch.float32 else 2e-2
     torch.testing.assert_close(out[:, :, g["out_rows"]].float(), g["out"].float(), atol=tol, rtol=tol)
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in cases.CASES if c["kind"] == "dca"])
+def test_dca_matches_reference(name):
+    """Dual Chunk Attention of the Qwen3 wrapper (qwen_routed_attention.py:210-283): intra-chunk
+    keys routed through the incremental path, three query ropings chosen per key."""
+    c, g = cases.case(name), cases.load(name)
+    inp = cases.make_dca_inputs(c)
+    assert cases.checksum(inp) == pytest.approx(g["input_checksum"], rel=1e-6)
+    out, _ = O.dca_sequence(c["params"], inp["q"], inp["k_raw"], inp["v"], c["dca_chunk"], c["dca_local"],
+                            cases.qwen_schedule(c))
+    tol = 1e-5 if c["dtype"] == torch.float32 else 2e-2
+    torch.testing.assert_close(out[:, :, g["out_rows"]].float(), g["out"].float(), atol=tol, rtol=tol)
