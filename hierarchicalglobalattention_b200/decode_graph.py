@@ -31,7 +31,6 @@ class DecodeStepGraph:
         self.C = cfg.chunk_size
         self.capacity = int(capacity_tokens)
         B = len(seq_pos_host)
-        self.B = B
         dev = store.compute_device
         H, KVH, Dh = cfg.nhead, cfg.kv_heads, cfg.head_dim
         self.hp = cfg.hga_params(store.policy, B, dtype)
