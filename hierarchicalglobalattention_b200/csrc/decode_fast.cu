@@ -90,11 +90,12 @@ __global__ void __launch_bounds__(256, 2) route_decode1_kernel(
   for (int i = tid; i < HB * Kcmax; i += blockDim.x) { mid_chunk[bh0 * Kcmax + i] = -1; mid_t0[bh0 * Kcmax + i] = -1; }
   for (int i = tid; i < HB * Kgmax; i += blockDim.x) { open_gid[bh0 * Kgmax + i] = -1; open_t0[bh0 * Kgmax + i] = -1; }
   if (n_mid == 0 || p.topk_chunks <= 0) return;
-  if ((int64_t)l_lo > sum_cap || n_mid > nkey_max) {
+  const int Kc = p.topk_chunks < n_mid ? p.topk_chunks : n_mid;
+  // a pool larger than the caller's nmid_max can ask for more chunks than the output rows hold
+  if ((int64_t)l_lo > sum_cap || n_mid > nkey_max || Kc > Kcmax) {
     if (tid == 0) atomicCAS(&g_decode_fast_error, 0, kErrBoundsRouteDecode);
     return;
   }
-  const int Kc = p.topk_chunks < n_mid ? p.topk_chunks : n_mid;
   const int G = Kc * M;
   const int Kg = p.topk_groups > 0 ? (p.topk_groups < G ? p.topk_groups : G) : 0;
   const int Kgr = p.topk_groups > 0 ? ((p.topk_groups / 2) < G ? p.topk_groups / 2 : G) : 0;

@@ -201,7 +201,8 @@ int hga_shard_unpack(const void* recv, int64_t rank_stride, int64_t part_offset,
  * bounded mbarrier wait that timed out (the CTA then released its TMEM and returned without
  * output); the decode kernels record 0x101 / 0x102 / 0x103 (routing / attention / append) when a
  * sequence position or a list entry addresses rows past a buffer's capacity (those rows are
- * skipped; a (b, h) whose position is past the capacity gets a zero output).
+ * skipped; a (b, h) whose position is past the capacity gets a zero output), and 0x101 also when
+ * a sequence's routed pool exceeds the nmid_max given to hga_route_decode (its lists stay -1).
  * Synchronous (reads device memory); clear != 0 resets the words. */
 int hga_device_status(int32_t* code, int32_t clear);
 
