@@ -76,7 +76,8 @@ template <typename T, int DH, int HB>
 __global__ void __launch_bounds__(256, 2) route_decode1_kernel(
     hga_params p, const T* __restrict__ q, const int32_t* __restrict__ seq_pos, const T* __restrict__ chunk_k,
     const T* __restrict__ group_k, int64_t sum_cap, int Kcmax, int Kgmax, int32_t* __restrict__ mid_chunk,
-    int32_t* __restrict__ mid_t0, int32_t* __restrict__ open_gid, int32_t* __restrict__ open_t0, int nkey_max) {
+    int32_t* __restrict__ mid_t0, int32_t* __restrict__ open_gid, int32_t* __restrict__ open_t0, int nkey_max,
+    int nmid_max) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int h0 = blockIdx.x * HB, b = blockIdx.y;
   const int H = p.nhead, KVH = p.kv_heads, C = p.chunk_size, M = C / p.group_size;
@@ -91,8 +92,9 @@ __global__ void __launch_bounds__(256, 2) route_decode1_kernel(
   for (int i = tid; i < HB * Kgmax; i += blockDim.x) { open_gid[bh0 * Kgmax + i] = -1; open_t0[bh0 * Kgmax + i] = -1; }
   if (n_mid == 0 || p.topk_chunks <= 0) return;
   const int Kc = p.topk_chunks < n_mid ? p.topk_chunks : n_mid;
-  // a pool larger than the caller's nmid_max can ask for more chunks than the output rows hold
-  if ((int64_t)l_lo > sum_cap || n_mid > nkey_max || Kc > Kcmax) {
+  // a pool larger than the caller's nmid_max is reported and left unrouted, as by the portable
+  // kernel (the smem key arrays may be larger than nmid_max: they also hold Kcmax * M groups)
+  if ((int64_t)l_lo > sum_cap || n_mid > nmid_max || n_mid > nkey_max || Kc > Kcmax) {
     if (tid == 0) atomicCAS(&g_decode_fast_error, 0, kErrBoundsRouteDecode);
     return;
   }
@@ -205,8 +207,8 @@ static int route_decode1_heads(const hga_params& p) {
 
 template <typename T, int DH, int HB>
 static cudaError_t launch_route_decode1_h(const hga_params& p, const void* q, const int32_t* seq_pos, const void* ck,
-                                          const void* gk, int64_t sum_cap, int nkey, int Kcmax, int Kgmax,
-                                          int32_t* mc, int32_t* mt, int32_t* og, int32_t* ot, cudaStream_t st) {
+                                          const void* gk, int64_t sum_cap, int nkey, int nmid_max, int Kcmax,
+                                          int Kgmax, int32_t* mc, int32_t* mt, int32_t* og, int32_t* ot, cudaStream_t st) {
   const size_t smem = route_decode1_smem(DH, nkey, HB);
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
   auto kern = route_decode1_kernel<T, DH, HB>;
@@ -216,7 +218,7 @@ static cudaError_t launch_route_decode1_h(const hga_params& p, const void* q, co
   }
   dim3 grid(p.nhead / HB, p.batch);
   kern<<<grid, 256, smem, st>>>(p, (const T*)q, seq_pos, (const T*)ck, (const T*)gk, sum_cap, Kcmax, Kgmax, mc, mt,
-                                og, ot, nkey);
+                                og, ot, nkey, nmid_max);
   return cudaGetLastError();
 }
 
@@ -227,10 +229,10 @@ static cudaError_t launch_route_decode1_t(const hga_params& p, const void* q, co
   const int M = p.chunk_size / p.group_size;
   const int nkey = nmid_max > Kcmax * M ? nmid_max : Kcmax * M;
   switch (route_decode1_heads(p)) {
-    case 8: return launch_route_decode1_h<T, DH, 8>(p, q, seq_pos, ck, gk, sum_cap, nkey, Kcmax, Kgmax, mc, mt, og, ot, st);
-    case 4: return launch_route_decode1_h<T, DH, 4>(p, q, seq_pos, ck, gk, sum_cap, nkey, Kcmax, Kgmax, mc, mt, og, ot, st);
-    case 2: return launch_route_decode1_h<T, DH, 2>(p, q, seq_pos, ck, gk, sum_cap, nkey, Kcmax, Kgmax, mc, mt, og, ot, st);
-    default: return launch_route_decode1_h<T, DH, 1>(p, q, seq_pos, ck, gk, sum_cap, nkey, Kcmax, Kgmax, mc, mt, og, ot, st);
+    case 8: return launch_route_decode1_h<T, DH, 8>(p, q, seq_pos, ck, gk, sum_cap, nkey, nmid_max, Kcmax, Kgmax, mc, mt, og, ot, st);
+    case 4: return launch_route_decode1_h<T, DH, 4>(p, q, seq_pos, ck, gk, sum_cap, nkey, nmid_max, Kcmax, Kgmax, mc, mt, og, ot, st);
+    case 2: return launch_route_decode1_h<T, DH, 2>(p, q, seq_pos, ck, gk, sum_cap, nkey, nmid_max, Kcmax, Kgmax, mc, mt, og, ot, st);
+    default: return launch_route_decode1_h<T, DH, 1>(p, q, seq_pos, ck, gk, sum_cap, nkey, nmid_max, Kcmax, Kgmax, mc, mt, og, ot, st);
   }
 }
 

@@ -288,3 +288,30 @@ def test_positions_past_capacity_are_reported_not_read(cuda):
     ops.attend_decode(hp, q, ok, st.token_k, st.token_v, 0, st.token_k, st.token_v, r["open_gid"], r["open_t0"])
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
+
+
+def test_pool_above_nmid_max_is_reported_by_both_routers(cuda):
+    """A routed pool larger than the caller's nmid_max (but small enough for the fast router's
+    scratch, which also holds Kc*M group keys) is reported with 0x101 and left unrouted by both
+    decode routers alike."""
+    from hierarchicalglobalattention_b200 import _lib, ops
+    c, inp = _synthetic(DECODE_SHAPES[0], seed=6)
+    p = c["params"]
+    g = {k: t.to(cuda) for k, t in inp.items() if k not in ("cos", "sin")}
+    router = _router(p, 1, c["dtype"], cuda, "vram")
+    S0 = 640                                     # 10 closed chunks: pool [keep_first, n - keep_last) = 7
+    router.seed(0, g["k_rope"][:, :, :S0], g["k_raw"][:, :, :S0], g["v"][:, :, :S0])
+    hp = router.cfg.hga_params(router.store.policy, 1, c["dtype"])
+    st = router.store.layer_buffers(0)
+    q = g["q"][:, :, :1].contiguous()
+    pos = torch.tensor([S0], dtype=torch.int32, device=cuda)
+    nmid_max = 6                                 # < 7 <= max(nmid_max, Kc * M) = 16
+    _lib.device_status(clear=True)
+    outs = []
+    for impl in (1, 2):
+        outs.append(ops.route_decode(hp, q, pos, st.chunk_k, st.group_k, nmid_max, impl=impl))
+        torch.cuda.synchronize()
+        assert _lib.device_status(clear=True) == 0x101, impl
+    for k in outs[0]:
+        assert torch.equal(outs[0][k], outs[1][k]), k
+        assert bool((outs[0][k] == -1).all()), k
