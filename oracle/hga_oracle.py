@@ -189,11 +189,15 @@ def summaries_store(p: OracleParams, k_raw, k_rope, v, first_chunk: int = 0):
 _ACC_BOUND = 2.0 ** -22
 
 
-def score_bounds(q: torch.Tensor, k: torch.Tensor, scale: float, dtype: torch.dtype, eq: str):
-    """Possible-score interval (lo, hi) as fp64 for ``einsum(eq, q, k) * scale`` in ``dtype``."""
+def score_bounds(q: torch.Tensor, k: torch.Tensor, scale: float, dtype: torch.dtype, eq: str,
+                 acc: float = _ACC_BOUND):
+    """Possible-score interval (lo, hi) as fp64 for ``einsum(eq, q, k) * scale`` in ``dtype``.
+
+    ``acc`` is the relative accumulation bound (times sqrt(Dh) * sum|q_i k_i|); ``acc=0`` gives the
+    exactly rounded score."""
     qd, kd = q.double(), k.double()
     d = torch.einsum(eq, qd, kd)
-    e = torch.einsum(eq, qd.abs(), kd.abs()) * (_ACC_BOUND * math.sqrt(q.shape[-1]))
+    e = torch.einsum(eq, qd.abs(), kd.abs()) * (acc * math.sqrt(q.shape[-1]))
     if dtype in (torch.bfloat16, torch.float16):
         lo = ((d - e).to(dtype).float() * scale).to(dtype).double()
         hi = ((d + e).to(dtype).float() * scale).to(dtype).double()
@@ -202,12 +206,31 @@ def score_bounds(q: torch.Tensor, k: torch.Tensor, scale: float, dtype: torch.dt
     return lo, hi
 
 
-def _set_tie(lo, hi, selected, real):
-    """True where a selected real candidate could score <= an unselected real one."""
+def _set_tie(lo, hi, selected, real, resolved: bool = False):
+    """True where a selected real candidate could score <= an unselected real one.
+
+    ``resolved``: equal scores are ordered by a fixed rule shared by both implementations (the
+    ``"index"`` tie rule), so a selected and an unselected candidate whose intervals are the SAME
+    single point are not ambiguous; only intervals that span a rounding boundary are."""
     big = torch.finfo(torch.float64).max
-    sel_lo = torch.where(selected & real, lo, torch.full_like(lo, big)).min(dim=-1).values
-    rest_hi = torch.where(~selected & real, hi, torch.full_like(hi, -big)).max(dim=-1).values
-    return sel_lo <= rest_hi
+    s_m, u_m = selected & real, ~selected & real
+    sel_lo = torch.where(s_m, lo, torch.full_like(lo, big)).min(dim=-1).values
+    rest_hi = torch.where(u_m, hi, torch.full_like(hi, -big)).max(dim=-1).values
+    if not resolved:
+        return sel_lo <= rest_hi
+    wide = hi != lo
+    s_wide = (s_m & (lo == sel_lo.unsqueeze(-1)) & wide).any(-1)
+    u_wide = (u_m & (hi == rest_hi.unsqueeze(-1)) & wide).any(-1)
+    return (sel_lo < rest_hi) | ((sel_lo == rest_hi) & (s_wide | u_wide))
+
+
+def _pair_ambiguous(lo_a, hi_a, lo_b, hi_b, resolved: bool):
+    """Elementwise: could a score in [lo_a, hi_a] rank at or below one in [lo_b, hi_b]?"""
+    amb = lo_a <= hi_b
+    if resolved:
+        same_point = (lo_a == hi_a) & (lo_b == hi_b) & (lo_a == lo_b)
+        amb &= ~same_point
+    return amb
 
 
 def _onehot(idx: torch.Tensor, R: int) -> torch.Tensor:
@@ -235,25 +258,44 @@ def _windows(p: OracleParams, n: int):
     return f_hi, l_lo
 
 
-def _rank_topk(scores: torch.Tensor, k: int, sorted_: bool):
+def _rank_topk(scores: torch.Tensor, k: int, sorted_: bool, rule: str = "torch"):
+    """Top-k along the last axis.  ``rule="torch"``: ``torch.topk`` (the reference's call; its
+    order among EQUAL scores is implementation-defined).  ``rule="index"``: the CUDA kernels' rule,
+    higher score first and, among equal scores, the lower index; the result is then sorted by it."""
     R = scores.shape[-1]
     if k >= R:
         idx = torch.arange(R).expand(*scores.shape[:-1], R)
         return scores, idx, True
+    if rule == "index":
+        s, i = torch.sort(scores, dim=-1, descending=True, stable=True)
+        return s[..., :k], i[..., :k], False
     s, i = torch.topk(scores, k, dim=-1, sorted=sorted_)
     return s, i, False
 
 
+def _lowest_last(top_s: torch.Tensor, top_i: torch.Tensor) -> torch.Tensor:
+    """Position in a top list of its lowest score, among equal lowest scores the highest index
+    (the entry the kernels drop for the previous chunk); [..., 1]."""
+    low = top_s == top_s.min(dim=-1, keepdim=True).values
+    return torch.where(low, top_i, torch.full_like(top_i, -1)).argmax(dim=-1, keepdim=True)
+
+
 def route_prefill(p: OracleParams, q: torch.Tensor, chunk_k: torch.Tensor, group_k: torch.Tensor,
-                  S: int, chunks=None, ties: bool = True) -> Dict[str, torch.Tensor]:
+                  S: int, chunks=None, ties: bool = True, acc_bound: float = _ACC_BOUND,
+                  tie_rule: str = "torch") -> Dict[str, torch.Tensor]:
     """Two-level routing of the chunk-parallel prefill path, per query chunk.
 
     q ``[B,H,S,Dh]`` (RoPE applied); chunk_k ``[B,KVH,N,Dh]``; group_k ``[B,KVH,N,M,Dh]``.
     Returns per (b, h, n): ``chunk_idx``/``chunk_t0`` [.., Kc] and ``group_chunk``/
     ``group_idx``/``group_t0`` [.., Kg] in the reference's slot order, plus ``tie`` [B,H,N]
     flagging tiles whose selection depends on a near tie (see ``score_bounds``).  ``chunks``
-    restricts the query chunks computed (others stay "never visible").
+    restricts the query chunks computed (others stay "never visible").  ``acc_bound`` is passed to
+    ``score_bounds``.  ``tie_rule`` picks the order among equal scores (``_rank_topk``): ``"torch"``
+    is the reference's, ``"index"`` the CUDA kernels'; under ``"index"`` the previous chunk
+    replaces the lowest chosen chunk with the highest index, level-2 candidates are numbered in
+    ascending chunk order, and the tie flags ignore equal scores (both sides order them alike).
     """
+    rz = tie_rule == "index"
     B, H, _, Dh = q.shape
     C, M = p.chunk_size, p.M
     N = (S + C - 1) // C
@@ -289,7 +331,7 @@ def route_prefill(p: OracleParams, q: torch.Tensor, chunk_k: torch.Tensor, group
         sc = torch.einsum("bhcd,bhmd->bhcm", qn, ck) * p.scale           # [B,H,C,N]
         rmask = pool.view(1, 1, 1, N) & qvalid.view(1, 1, C, 1)
         sc = sc.masked_fill(~rmask, NEG)
-        req_s, req_i, all_req = _rank_topk(sc, Kc, sorted_=True)
+        req_s, req_i, all_req = _rank_topk(sc, Kc, sorted_=True, rule=tie_rule)
         if all_req:
             pooled = req_s.max(dim=-2).values                           # [B,H,N]
         else:
@@ -297,31 +339,33 @@ def route_prefill(p: OracleParams, q: torch.Tensor, chunk_k: torch.Tensor, group
             pooled.scatter_reduce_(1, req_i.reshape(B * H, -1), req_s.reshape(B * H, -1),
                                    reduce="amax", include_self=True)
             pooled = pooled.view(B, H, N)
-        top_s, top_i, _ = _rank_topk(pooled, Kc, sorted_=False)
+        top_s, top_i, _ = _rank_topk(pooled, Kc, sorted_=False, rule=tie_rule)
         tie = torch.zeros(B, H, dtype=torch.bool)
         if ties:
-            lo, hi = score_bounds(qn, ck, p.scale, dtype, "bhcd,bhmd->bhcm")
+            lo, hi = score_bounds(qn, ck, p.scale, dtype, "bhcd,bhmd->bhcm", acc_bound)
             real = rmask.expand(B, H, C, N)
             req_m = _onehot(req_i, N) & real
             if not all_req:
-                tie |= (_set_tie(lo, hi, req_m, real) & qvalid.view(1, 1, C)).any(-1)
+                tie |= (_set_tie(lo, hi, req_m, real, rz) & qvalid.view(1, 1, C)).any(-1)
             if Kc < N:
                 plo, phi = _pooled_bounds(lo, hi, req_m)
                 preal = req_m.any(dim=2)
-                tie |= _set_tie(plo, phi, _onehot(top_i, N), preal)
+                tie |= _set_tie(plo, phi, _onehot(top_i, N), preal, rz)
         prev = n - 1
         if n > 0 and f_hi <= prev < l_lo:
             missing = ~(top_i == prev).any(dim=-1, keepdim=True)
-            at = top_s.argmin(dim=-1, keepdim=True)
+            at = _lowest_last(top_s, top_i) if rz else top_s.argmin(dim=-1, keepdim=True)
             if ties and Kc < N:
-                rem = torch.zeros(B, H, N, dtype=torch.bool).scatter_(-1, top_i.gather(-1, at), True)
-                others = _onehot(top_i, N) & ~rem & preal
-                big = torch.finfo(torch.float64).max
-                o_lo = torch.where(others, plo, torch.full_like(plo, big)).min(-1).values
-                r_hi = torch.where(rem, phi, torch.full_like(phi, -big)).max(-1).values
-                tie |= missing.squeeze(-1) & (o_lo <= r_hi)
+                rem_i = top_i.gather(-1, at)                                 # [B,H,1]
+                others = _onehot(top_i, N) & preal
+                others.scatter_(-1, rem_i, False)
+                amb = _pair_ambiguous(plo, phi, plo.gather(-1, rem_i), phi.gather(-1, rem_i), rz) & others
+                tie |= missing.squeeze(-1) & amb.any(-1)
             top_i = top_i.scatter(-1, at, torch.where(missing, torch.full_like(at, prev),
                                                        top_i.gather(-1, at)))
+        if rz:
+            # the kernels number the level-2 candidates by ascending chunk id (their tie order)
+            top_i = top_i.sort(dim=-1).values
         valid_prev = pool[top_i]                                         # [B,H,Kc]
         requested = (req_i.unsqueeze(-1) == top_i.view(B, H, 1, 1, Kc)).any(dim=-2)   # [B,H,C,Kc]
         requested &= valid_prev.unsqueeze(2)
@@ -341,7 +385,7 @@ def route_prefill(p: OracleParams, q: torch.Tensor, chunk_k: torch.Tensor, group
             gmask = vis.unsqueeze(-1).expand(B, H, C, Kc, M).reshape(B, H, C, Tgrp)
             gmask = gmask & gvalid.unsqueeze(2) & qvalid.view(1, 1, C, 1)
             gsc = gsc.masked_fill(~gmask, NEG)
-            greq_s, greq_i, gall = _rank_topk(gsc, Kgr, sorted_=True)
+            greq_s, greq_i, gall = _rank_topk(gsc, Kgr, sorted_=True, rule=tie_rule)
             if gall:
                 gpooled = greq_s.max(dim=-2).values
             else:
@@ -349,15 +393,15 @@ def route_prefill(p: OracleParams, q: torch.Tensor, chunk_k: torch.Tensor, group
                 gpooled.scatter_reduce_(1, greq_i.reshape(B * H, -1), greq_s.reshape(B * H, -1),
                                         reduce="amax", include_self=True)
                 gpooled = gpooled.view(B, H, Tgrp)
-            _, top_g, _ = _rank_topk(gpooled, Kg, sorted_=False)
+            _, top_g, _ = _rank_topk(gpooled, Kg, sorted_=False, rule=tie_rule)
             if ties:
-                glo, ghi = score_bounds(qn, cand_k, p.scale, dtype, "bhcd,bhrd->bhcr")
+                glo, ghi = score_bounds(qn, cand_k, p.scale, dtype, "bhcd,bhrd->bhcr", acc_bound)
                 greq_m = _onehot(greq_i, Tgrp) & gmask
                 if not gall:
-                    tie |= (_set_tie(glo, ghi, greq_m, gmask) & qvalid.view(1, 1, C)).any(-1)
+                    tie |= (_set_tie(glo, ghi, greq_m, gmask, rz) & qvalid.view(1, 1, C)).any(-1)
                 if Kg < Tgrp:
                     gplo, gphi = _pooled_bounds(glo, ghi, greq_m)
-                    tie |= _set_tie(gplo, gphi, _onehot(top_g, Tgrp), greq_m.any(dim=2))
+                    tie |= _set_tie(gplo, gphi, _onehot(top_g, Tgrp), greq_m.any(dim=2), rz)
             top_gvalid = gvalid.gather(-1, top_g)
             parent = top_g // M
             parent_vis = vis.gather(-1, parent.unsqueeze(2).expand(B, H, C, Kg))
@@ -448,17 +492,19 @@ def attend_prefill(p: OracleParams, q, k_rope, v, route, S: int, chunks=None) ->
 # ---------------------------------------------------------------------------------------------
 # decode (single active chunk, incremental path)
 # ---------------------------------------------------------------------------------------------
-def route_decode(p: OracleParams, q, chunk_k_mid, group_k_of, mid_lo: int, n_closed: int):
+def route_decode(p: OracleParams, q, chunk_k_mid, group_k_of, mid_lo: int, n_closed: int,
+                 acc_bound: float = _ACC_BOUND, tie_rule: str = "torch"):
     """Routing of one decode block (chunk_router.py:188-277).
 
     q ``[B,H,L,Dh]``; chunk_k_mid ``[B,KVH,n_mid,Dh]`` = store chunk summaries of the routed
     pool; ``group_k_of(mid_idx[B,H,Kc]) -> [B,H,Kc,M,Dh]``.  Returns absolute chunk ids and
     group picks with their per-row first-visible index (L = never), plus a near-tie flag [B,H]
     (a selection that an accumulation-order difference of one rounding could flip; see
-    ``score_bounds``).
+    ``score_bounds``).  ``acc_bound`` / ``tie_rule`` as in ``route_prefill``.
     """
     B, H, L, Dh = q.shape
     M = p.M
+    rz = tie_rule == "index"
     dtype = q.dtype
     n_mid = chunk_k_mid.shape[2]
     ck = chunk_k_mid.repeat_interleave(p.rep, dim=1)
@@ -469,15 +515,15 @@ def route_decode(p: OracleParams, q, chunk_k_mid, group_k_of, mid_lo: int, n_clo
         return res
     # chunk_router.py:222-232: scores in the model dtype, pooled by max over the block's rows
     sc = torch.einsum("bhld,bhnd->bhln", q, ck) * p.scale
-    lo, hi = score_bounds(q, ck, p.scale, dtype, "bhld,bhnd->bhln")
+    lo, hi = score_bounds(q, ck, p.scale, dtype, "bhld,bhnd->bhln", acc_bound)
     Kc = min(p.topk_chunks, n_mid)
     pooled = sc.max(dim=2).values
-    top_s, mid_rel = torch.topk(pooled, Kc, dim=-1, sorted=False)
-    _, req_rel = torch.topk(sc, Kc, dim=-1, sorted=False)
+    top_s, mid_rel, _ = _rank_topk(pooled, Kc, False, tie_rule)
+    _, req_rel, _ = _rank_topk(sc, Kc, False, tie_rule)
     plo, phi = lo.max(dim=2).values, hi.max(dim=2).values
     every = torch.ones_like(pooled, dtype=torch.bool)
-    tie = _set_tie(plo, phi, _onehot(mid_rel, n_mid), every)
-    tie |= _set_tie(lo, hi, _onehot(req_rel, n_mid), torch.ones_like(sc, dtype=torch.bool)).any(-1)
+    tie = _set_tie(plo, phi, _onehot(mid_rel, n_mid), every, rz)
+    tie |= _set_tie(lo, hi, _onehot(req_rel, n_mid), torch.ones_like(sc, dtype=torch.bool), rz).any(-1)
     # chunk_router.py:234-246: the previous chunk replaces the lowest pooled pick
     prev = n_closed - 1
     mid_hi = mid_lo + n_mid
@@ -485,13 +531,15 @@ def route_decode(p: OracleParams, q, chunk_k_mid, group_k_of, mid_lo: int, n_clo
     if prev_in:
         prev_rel = prev - mid_lo
         missing = ~(mid_rel == prev_rel).any(dim=-1, keepdim=True)
-        at = top_s.argmin(dim=-1, keepdim=True)
+        at = _lowest_last(top_s, mid_rel) if rz else top_s.argmin(dim=-1, keepdim=True)
         sel_lo, sel_hi = plo.gather(-1, mid_rel), phi.gather(-1, mid_rel)
-        min_hi = sel_hi.gather(-1, at)
         others = torch.ones_like(sel_lo, dtype=torch.bool).scatter(-1, at, False)
-        amb = ((sel_lo <= min_hi) & others).any(-1, keepdim=True)
+        amb = (_pair_ambiguous(sel_lo, sel_hi, sel_lo.gather(-1, at), sel_hi.gather(-1, at), rz)
+               & others).any(-1, keepdim=True)
         tie |= (missing & amb).squeeze(-1)
         mid_rel = mid_rel.scatter(-1, at, torch.where(missing, torch.full_like(at, prev_rel), mid_rel.gather(-1, at)))
+    if rz:
+        mid_rel = mid_rel.sort(dim=-1).values    # level-2 candidates in ascending chunk order
     mid_idx = mid_rel + mid_lo
     mreq = (req_rel.unsqueeze(-2) == mid_rel.unsqueeze(2).unsqueeze(-1)).any(dim=-1)
     mvis = torch.cumsum(mreq.int(), dim=2) > 0
@@ -506,14 +554,14 @@ def route_decode(p: OracleParams, q, chunk_k_mid, group_k_of, mid_lo: int, n_clo
     # chunk_router.py:248-277: group candidates of the chosen chunks (not masked), pooled over rows
     gk = group_k_of(mid_idx).reshape(B, H, Kc * M, Dh)
     sg = torch.einsum("bhld,bhrd->bhlr", q, gk) * p.scale
-    glo, ghi = score_bounds(q, gk, p.scale, dtype, "bhld,bhrd->bhlr")
+    glo, ghi = score_bounds(q, gk, p.scale, dtype, "bhld,bhrd->bhlr", acc_bound)
     pg = sg.max(dim=2).values
-    _, top_g = torch.topk(pg, Kg, dim=-1, sorted=False)
+    _, top_g, _ = _rank_topk(pg, Kg, False, tie_rule)
     tie |= _set_tie(glo.max(dim=2).values, ghi.max(dim=2).values, _onehot(top_g, Kc * M),
-                    torch.ones_like(pg, dtype=torch.bool))
+                    torch.ones_like(pg, dtype=torch.bool), rz)
     if Kgr > 0:
-        _, req_g = torch.topk(sg, Kgr, dim=-1, sorted=False)
-        tie |= _set_tie(glo, ghi, _onehot(req_g, Kc * M), torch.ones_like(sg, dtype=torch.bool)).any(-1)
+        _, req_g, _ = _rank_topk(sg, Kgr, False, tie_rule)
+        tie |= _set_tie(glo, ghi, _onehot(req_g, Kc * M), torch.ones_like(sg, dtype=torch.bool), rz).any(-1)
         greq = (req_g.unsqueeze(-2) == top_g.unsqueeze(2).unsqueeze(-1)).any(dim=-1)
     else:
         greq = torch.zeros(B, H, L, Kg, dtype=torch.bool)
@@ -541,7 +589,7 @@ def attend_decode(p: OracleParams, q, keys, vals, key_first_row):
 
 
 def decode_sequence(p: OracleParams, q, k_rope, k_raw, v, block: int, start_pos: int = 0, calls=None,
-                    attend=None):
+                    attend=None, acc_bound: float = _ACC_BOUND, tie_rule: str = "torch"):
     """The reference's incremental path over a whole sequence: ``ChunkRouter.decode_block`` fed
     block by block and chunk-aligned (chunk_router.py:279-442), token-only attention.
 
@@ -572,7 +620,7 @@ def decode_sequence(p: OracleParams, q, k_rope, k_raw, v, block: int, start_pos:
             f_hi, l_lo = _windows(p, n)
             qb = q[:, :, pos:pos + L]
             r = route_decode(p, qb, ck_all[:, :, f_hi:max(l_lo, f_hi)],
-                             lambda mid: gk_all[bi, hi_, mid], f_hi, n)
+                             lambda mid: gk_all[bi, hi_, mid], f_hi, n, acc_bound, tie_rule)
             rows, first = [], []
             win = list(range(0, f_hi * C)) + list(range(l_lo * C, n * C))
             if win:

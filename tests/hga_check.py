@@ -39,8 +39,10 @@ def _top(vals, idxs, k):
     return [idxs[i] for i in order[:k]]
 
 
-def replay_prefill_selection(p, S, res):
-    """Returns the expected (sel_chunk, sel_t0, open_gid, open_t0) lists per tile from dumped scores."""
+def replay_prefill_selection(p, S, res, chunks=None, offset=0):
+    """Returns the expected (sel_chunk, sel_t0, open_gid, open_t0) lists per tile from dumped scores.
+    ``chunks`` (default all) are absolute query chunks; the dumps hold chunk n at index n - offset
+    (a ``chunk_range`` call)."""
     C, M = p.chunk_size, p.M
     N, Kc, Kg, Kgr, Tg = sizes(p, S)
     l1 = res["dbg_l1"].cpu().numpy()
@@ -49,7 +51,8 @@ def replay_prefill_selection(p, S, res):
     exp = {}
     for b in range(B):
         for h in range(H):
-            for n in range(N):
+            for n in (range(N) if chunks is None else chunks):
+                ln = n - offset
                 sel, open_ = [], []
                 f_hi, l_lo = _windows(p, n)
                 pool = list(range(f_hi, l_lo))
@@ -58,9 +61,9 @@ def replay_prefill_selection(p, S, res):
                     k1 = min(Kc, len(pool))
                     pooled, t0 = {}, {}
                     for t in range(nvalid):
-                        row = [float(l1[b, h, n, t, c]) for c in pool]
+                        row = [float(l1[b, h, ln, t, c]) for c in pool]
                         for c in _top(row, pool, k1):
-                            pooled[c] = max(pooled.get(c, -np.inf), float(l1[b, h, n, t, c]))
+                            pooled[c] = max(pooled.get(c, -np.inf), float(l1[b, h, ln, t, c]))
                             t0.setdefault(c, t)
                     req = sorted(pooled)
                     chosen = req if len(req) <= Kc else _top([pooled[c] for c in req], req, Kc)
@@ -79,10 +82,10 @@ def replay_prefill_selection(p, S, res):
                         gpool, gt0 = {}, {}
                         for t in range(nvalid):
                             real = [j for j in range(tsel) if t >= sel[j // M][1]]
-                            vals = [float(l2[b, h, n, t, j]) for j in real]
+                            vals = [float(l2[b, h, ln, t, j]) for j in real]
                             reqj = real if Kgr >= Tg else _top(vals, real, Kgr)
                             for j in reqj:
-                                gpool[j] = max(gpool.get(j, -np.inf), float(l2[b, h, n, t, j]))
+                                gpool[j] = max(gpool.get(j, -np.inf), float(l2[b, h, ln, t, j]))
                                 gt0.setdefault(j, t)
                         js = sorted(gpool)
                         if Kg < Tg and len(js) > Kg:
@@ -92,28 +95,31 @@ def replay_prefill_selection(p, S, res):
     return exp
 
 
-def gpu_lists(res, key_a, key_b):
+def gpu_lists(res, key_a, key_b, offset=0, chunks=None):
+    """{(b, h, n): [(id, t0), ...]} of a GPU routing result whose index n - offset holds chunk n."""
     a = res[key_a].cpu().numpy()
     bb = res[key_b].cpu().numpy()
     out = {}
     B, H, N = a.shape[:3]
     for b in range(B):
         for h in range(H):
-            for n in range(N):
-                out[(b, h, n)] = [(int(x), int(y)) for x, y in zip(a[b, h, n], bb[b, h, n]) if x >= 0]
+            for n in (range(offset, offset + N) if chunks is None else chunks):
+                ln = n - offset
+                out[(b, h, n)] = [(int(x), int(y)) for x, y in zip(a[b, h, ln], bb[b, h, ln]) if x >= 0]
     return out
 
 
-def check_replay(p, S, res):
-    exp = replay_prefill_selection(p, S, res)
-    sel = gpu_lists(res, "sel_chunk", "sel_t0")
-    opn = gpu_lists(res, "open_gid", "open_t0")
+def check_replay(p, S, res, chunks=None, offset=0):
+    exp = replay_prefill_selection(p, S, res, chunks, offset)
+    sel = gpu_lists(res, "sel_chunk", "sel_t0", offset, chunks)
+    opn = gpu_lists(res, "open_gid", "open_t0", offset, chunks)
     bad = [k for k in exp if exp[k][0] != sel[k] or exp[k][1] != opn[k]]
     return bad, exp
 
 
-def check_scores_in_bounds(p, S, q, chunk_k, group_k, res):
-    """Every dumped (valid, real) score lies in the oracle's possible-score interval."""
+def check_scores_in_bounds(p, S, q, chunk_k, group_k, res, chunks=None, offset=0):
+    """Every dumped (valid, real) score lies in the oracle's possible-score interval.  ``chunks`` /
+    ``offset`` as in ``replay_prefill_selection`` (q always holds the whole sequence)."""
     C, M = p.chunk_size, p.M
     N, Kc, Kg, Kgr, Tg = sizes(p, S)
     dtype = q.dtype
@@ -125,16 +131,17 @@ def check_scores_in_bounds(p, S, q, chunk_k, group_k, res):
     sel = res["sel_chunk"].cpu()
     B, H = qc.shape[:2]
     worst = 0
-    for n in range(N):
+    for n in (range(N) if chunks is None else chunks):
+        ln = n - offset
         f_hi, l_lo = _windows(p, n)
         nvalid = min(C, S - n * C)
         qn = qc[:, :, n * C:n * C + nvalid]
         if l_lo > f_hi and Kc:
             lo, hi = O.score_bounds(qn, ck[:, :, f_hi:l_lo], p.scale, dtype, "bhcd,bhmd->bhcm")
-            got = l1[:, :, n, :nvalid, f_hi:l_lo].double()
+            got = l1[:, :, ln, :nvalid, f_hi:l_lo].double()
             worst = max(worst, int(((got < lo) | (got > hi)).sum()))
         if Kg:
-            s = sel[:, :, n]
+            s = sel[:, :, ln]
             ksel = int((s[0, 0] >= 0).sum()) if s.numel() else 0
             for b in range(B):
                 for h in range(H):
@@ -143,7 +150,7 @@ def check_scores_in_bounds(p, S, q, chunk_k, group_k, res):
                         continue
                     keys = gk[b, h, cs].reshape(len(cs) * M, -1)
                     lo, hi = O.score_bounds(qn[b, h], keys, p.scale, dtype, "cd,rd->cr")
-                    got = l2[b, h, n, :nvalid, :len(cs) * M].double()
+                    got = l2[b, h, ln, :nvalid, :len(cs) * M].double()
                     real = got > O.NEG
                     worst = max(worst, int((((got < lo) | (got > hi)) & real).sum()))
             del ksel
@@ -154,10 +161,42 @@ def oracle_sets(route, C, M):
     return O.visible_sets(route, C, M)
 
 
-def gpu_sets(res, M):
-    sel = gpu_lists(res, "sel_chunk", "sel_t0")
-    opn = gpu_lists(res, "open_gid", "open_t0")
+def gpu_sets(res, M, chunks=None, offset=0):
+    sel = gpu_lists(res, "sel_chunk", "sel_t0", offset, chunks)
+    opn = gpu_lists(res, "open_gid", "open_t0", offset, chunks)
     return {k: (dict(sel[k]), dict(opn[k])) for k in sel}
+
+
+def oracle_sets_for(route, C, M, chunks):
+    """``oracle_sets`` restricted to the query chunks ``chunks`` (long sequences)."""
+    B, H, _ = route["tie"].shape
+    gc, gi, gt = (route[k].numpy() for k in ("group_chunk", "group_idx", "group_t0"))
+    cc, ct = route["chunk_idx"].numpy(), route["chunk_t0"].numpy()
+    out = {}
+    for b in range(B):
+        for h in range(H):
+            for n in chunks:
+                g = {int(x) * M + int(y): int(t) for x, y, t in zip(gc[b, h, n], gi[b, h, n], gt[b, h, n]) if t < C}
+                c = {int(x): int(t) for x, t in zip(cc[b, h, n], ct[b, h, n]) if t < C}
+                out[(b, h, n)] = (c, g)
+    return out
+
+
+def tie_report(osets, gsets, tie):
+    """Compare visible sets tile by tile; ``tie`` [B,H,N] are the oracle's near-tie flags.  Returns
+    the tile count, the mismatching tiles, those NOT flagged, the flagged share and the mean
+    Jaccard similarity of the opened-group sets over the mismatching tiles."""
+    keys = sorted(osets)
+    mism = [k for k in keys if osets[k] != gsets[k]]
+    unexplained = [k for k in mism if not bool(tie[k])]
+    jac = []
+    for k in mism:
+        a, b = set(osets[k][1]), set(gsets[k][1])
+        jac.append(len(a & b) / max(1, len(a | b)))
+    n = max(1, len(keys))
+    return {"tiles": len(keys), "mismatch": len(mism), "unexplained": unexplained,
+            "tie_frac": sum(bool(tie[k]) for k in keys) / n, "mismatch_frac": len(mism) / n,
+            "mismatch_jaccard": (sum(jac) / len(jac)) if jac else 1.0}
 
 
 def route_dict_from_gpu(res, p, S):

@@ -107,11 +107,12 @@ def _synthetic(spec, seed=7):
 
 @pytest.mark.parametrize("spec", DECODE_SHAPES, ids=[s[0] for s in DECODE_SHAPES])
 def test_decode_routing_and_output_vs_oracle(cuda, spec):
-    """Per block: routing sets equal the oracle's wherever the block has no near tie; outputs of
-    tie-free (b, h) within tolerance; the share of heads with a tie stays small."""
+    """Per block: routing sets equal the oracle's (run under the kernels' tie rule: equal scores,
+    lower index first) wherever an accumulation-order difference could not flip the selection;
+    outputs of those (b, h) within tolerance; the share of flagged heads stays small."""
     c, inp = _synthetic(spec)
     p, block = c["params"], spec[4]
-    ref_out, blocks = O.decode_sequence(p, inp["q"], inp["k_rope"], inp["k_raw"], inp["v"], block)
+    ref_out, blocks = O.decode_sequence(p, inp["q"], inp["k_rope"], inp["k_raw"], inp["v"], block, tie_rule="index")
     router = _router(p, c["B"], c["dtype"], cuda, "vram")
     out, routes = _run_blocks(router, {k: t.to(cuda) for k, t in inp.items()}, block)
     out = out.cpu()
@@ -131,8 +132,9 @@ def test_decode_routing_and_output_vs_oracle(cuda, spec):
                 assert gg == og, f"groups differ at pos {pos} b{b} h{h}: {gg} vs {og}"
                 torch.testing.assert_close(out[b, h, pos:pos + L].float(), ref_out[b, h, pos:pos + L].float(),
                                            atol=tol, rtol=tol)
-    # bf16 scores are rounded twice to 8 mantissa bits, so pooled multi-row blocks tie often
-    limit = 0.05 if c["dtype"] == torch.float32 else 0.3
+    # under the kernels' tie rule only accumulation-order ambiguities are excluded
+    print(f"\n[{spec[0]}] decode heads {n_heads}, flagged {n_tie}")
+    limit = 0.05 if c["dtype"] == torch.float32 else 0.1
     assert n_tie <= limit * n_heads, f"{n_tie}/{n_heads} heads flagged as near ties"
 
 

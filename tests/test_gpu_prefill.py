@@ -79,8 +79,11 @@ def test_router_and_output_vs_reference(cuda, name):
     mism = [k for k in osets if osets[k] != gsets[k]]
     unexplained = [k for k in mism if not bool(oroute["tie"][k])]
     assert not unexplained, f"{len(unexplained)} non-tie tiles differ, e.g. {unexplained[:3]}"
-    if c["dtype"] == torch.float32:
-        assert len(mism) <= max(1, len(osets) // 50)
+    print(f"\n[{name}] tiles {len(osets)}, differing (all flagged) {len(mism)}, "
+          f"flagged {int(oroute['tie'].sum())}")
+    # fp32: flagged ties are rare; bf16: the reference's own torch.topk order among equal bf16
+    # scores decides many tiles (implementation-defined; measured 9% differing at pf_qwen_bf16)
+    assert len(mism) <= (max(1, len(osets) // 50) if c["dtype"] == torch.float32 else len(osets) * 0.2)
     # outputs on agreeing tiles vs the reference's golden rows
     rows = gold["out_rows"]
     C = p.chunk_size
@@ -96,6 +99,24 @@ def test_router_and_output_vs_reference(cuda, name):
     d = (o.float() - ref.float()).abs()[keep]
     assert d.max().item() < tol_abs
     assert (d.sum() / ref.float().abs()[keep].sum()).item() < tol_rel
+
+
+@pytest.mark.parametrize("name", PREFILL_CASES)
+def test_router_sets_vs_index_rule_oracle(cuda, name):
+    """Strict set parity: the oracle run under the kernels' tie rule (equal scores: lower index)
+    agrees on every tile except those an accumulation-order difference could flip, and those are
+    capped (fp32 5%, bf16 35%)."""
+    c = cases.case(name)
+    p, S = c["params"], c["S"]
+    inp = cases.make_inputs(c)
+    _, _, _, res, _ = _gpu_pipeline(c, inp, cuda)
+    ck, gk, _ = O.summaries_prefill(p, inp["k_raw"], inp["k_rope"], inp["v"], inp["cos"], inp["sin"])
+    r = O.route_prefill(p, inp["q"], ck, gk, S, tie_rule="index")
+    rep = HC.tie_report(HC.oracle_sets(r, p.chunk_size, p.M), HC.gpu_sets(res, p.M), r["tie"])
+    print(f"\n[{name}] index-rule parity: tiles {rep['tiles']}, differing {rep['mismatch']}, "
+          f"flagged {rep['tie_frac']:.3f}")
+    assert not rep["unexplained"], f"non-tie tiles differ, e.g. {rep['unexplained'][:3]}"
+    assert rep["tie_frac"] <= (0.05 if c["dtype"] == torch.float32 else 0.35)
 
 
 @pytest.mark.parametrize("name", PREFILL_CASES)
