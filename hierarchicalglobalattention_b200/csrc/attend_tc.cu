@@ -10,15 +10,19 @@
 // For every row a unit's visible keys form a prefix (causal: keys j <= t - 16u; otherwise all or
 // none), so masking is one count per (row, unit).
 // Per 64-key tile (4 units):
-//   TMA warp      : 16-row boxes of K and V per unit into a 2-stage SW128 smem ring
+//   TMA warp      : 16-row boxes of K and V per unit into a 2-stage SW128 smem ring; K and V of a
+//                   stage have separate full/empty barriers (K is free once Q.K^T has read it)
 //   MMA warp      : S = Q.K^T  (M128 N64, A/B from smem, D in TMEM, double-buffered)
 //                   O += P.V   (A = P from TMEM, B = V from smem as MN-major, D = O in TMEM)
-//   4 softmax warps: one thread per query row (TMEM lane): online softmax in the exp2 domain with
-//                   lazy rescaling (only when the row max grows by > 2^8), P -> TMEM as bf16.
-//                   TMEM loads/stores are warp-collective, so a rescale is decided per warp.
+//   4 softmax warps: one thread per query row (TMEM lane), exp2 domain.  Tile 0 (the causal
+//                   current chunk) sets the row max; later tiles are exponentiated against it and
+//                   take a max pass (and a lazy O rescale) only when a p could exceed 2^8.  Units
+//                   that no row of a warp sees are neither loaded from TMEM nor exponentiated.
+//                   TMEM loads/stores are warp-collective, so these decisions are per warp.
 // ~105 KB smem and 256 TMEM columns per CTA, so two CTAs share an SM and hide each other's
 // serial phases.  Every mbarrier wait is bounded; on timeout the CTA records an error code
-// (hga_device_status) and leaves after releasing its TMEM.
+// (hga_device_status), lets its copies and MMAs in flight land (bounded), releases its TMEM and
+// leaves.
 #include "tc_common.cuh"
 
 namespace hga {
@@ -45,7 +49,7 @@ struct SmemLayout {
   static constexpr int kUnits = kStage + 2 * kStageBytes;
   static constexpr int kLists = kUnits + kMaxUnits * 16;  // [4][kMaxKg] ints: gid0, t00, gid1, t01
   static constexpr int kBars = kLists + 4 * kMaxKg * 4;
-  static constexpr int kMisc = kBars + 16 * 8;
+  static constexpr int kMisc = kBars + 16 * 8;  // 16 mbarriers
   static constexpr int kTotal = kMisc + 64;
 };
 
@@ -68,6 +72,97 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+// sm_100 paired fp32 arithmetic (one instruction for two lanes of work, same rounding as the
+// scalar forms) and the three-input max
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unf2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Row max of one S tile (r: the row's 64 scores, 4 units of 16) over the keys the row sees.
+// CAUSAL (the current chunk's tile): key j of unit u is visible iff j < cnt[u]; otherwise a unit
+// is seen whole (cnt 16) or not at all (cnt 0).  Dead units (no row of the warp sees them) are
+// skipped.  Three-input max in a tree of depth 3 per unit.
+template <bool CAUSAL>
+__device__ __forceinline__ float tile_max(const uint32_t (&r)[64], const int (&cnt)[kUnitsPerTile], unsigned live) {
+  float mx = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < kUnitsPerTile; ++u) {
+    if (!(live >> u & 1)) continue;
+    float x[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      x[j] = __uint_as_float(r[u * 16 + j]);
+      if constexpr (CAUSAL) x[j] = j < cnt[u] ? x[j] : -INFINITY;
+    }
+    const float a = max3(x[0], x[1], x[2]), b = max3(x[3], x[4], x[5]), c = max3(x[6], x[7], x[8]);
+    const float d = max3(x[9], x[10], x[11]), e = max3(x[12], x[13], x[14]);
+    const float mu = fmaxf(max3(a, b, c), max3(d, e, x[15]));
+    mx = fmaxf(mx, (CAUSAL || cnt[u] > 0) ? mu : -INFINITY);
+  }
+  return mx;
+}
+
+// P = 2^(s * scale_log2 - m) of one S tile as packed bf16 pairs (pk, 32 words = the 64 keys) and
+// its row sum added to ps (two paired fp32 partial sums).  Invisible keys get exactly 0.
+template <bool CAUSAL>
+__device__ __forceinline__ void tile_exp(const uint32_t (&r)[64], const int (&cnt)[kUnitsPerTile], unsigned live,
+                                         uint64_t sl2x2, uint64_t nmx2, uint32_t (&pk)[32], uint64_t& ps) {
+#pragma unroll
+  for (int u = 0; u < kUnitsPerTile; ++u) {
+    if (!(live >> u & 1)) {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) pk[u * 8 + w] = 0u;
+      continue;
+    }
+    uint64_t s2 = f2(0.f, 0.f);
+    uint32_t w8[8];
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      float x0 = __uint_as_float(r[u * 16 + j]), x1 = __uint_as_float(r[u * 16 + j + 1]);
+      if constexpr (CAUSAL) {
+        // prefix-visible keys: an invisible key's exponent is -inf, which ex2 maps to exactly 0
+        x0 = j < cnt[u] ? x0 : -INFINITY;
+        x1 = j + 1 < cnt[u] ? x1 : -INFINITY;
+      }
+      float y0, y1;
+      unf2(fma2(f2(x0, x1), sl2x2, nmx2), y0, y1);
+      const float p0 = ex2(y0), p1 = ex2(y1);
+      s2 = add2(s2, f2(p0, p1));
+      w8[j >> 1] = pack_bf16(p0, p1);
+    }
+    if constexpr (CAUSAL) {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) pk[u * 8 + w] = w8[w];
+      ps = add2(ps, s2);
+    } else {
+      // whole-or-nothing units: every key was computed; rows that see none of them get zeros
+      const bool v = cnt[u] > 0;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) pk[u * 8 + w] = v ? w8[w] : 0u;
+      ps = v ? add2(ps, s2) : ps;
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kThreads, 2)
@@ -93,12 +188,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   int* t0B = lists + 3 * kMaxKg;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::kBars);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* p_full = bars + 7;    // [2]
-  uint64_t* pv_done = bars + 9;   // one completion per P.V (its waits are never more than one phase behind)
-  uint64_t* o_done = bars + 10;   // single completion after the last P.V (the epilogue's wait)
+  uint64_t* k_full = bars + 1;    // [2]  K and V of a stage have their own barriers: a stage's K is
+  uint64_t* k_empty = bars + 3;   // [2]  released when Q.K^T is done, its V only after P.V, so the
+  uint64_t* v_full = bars + 5;    // [2]  next K load overlaps the softmax of the current tile
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* p_full = bars + 11;   // [2]
+  uint64_t* pv_done = bars + 13;  // one completion per P.V (its waits are never more than one phase behind)
+  uint64_t* o_done = bars + 14;   // single completion after the last P.V (the epilogue's wait)
+  uint64_t* drain = bars + 15;    // the MMA issuer's last commit: every MMA it issued has completed
   int* misc = reinterpret_cast<int*>(smem + SmemLayout::kMisc);
   volatile int* abort_flag = misc + 0;
   int* n_units_s = misc + 1;
@@ -113,13 +211,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (tid == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(kv_full + i, 1);
-      mbar_init(kv_empty + i, 1);
+      mbar_init(k_full + i, 1);
+      mbar_init(k_empty + i, 1);
+      mbar_init(v_full + i, 1);
+      mbar_init(v_empty + i, 1);
       mbar_init(s_full + i, 1);
       mbar_init(p_full + i, 128);
     }
     mbar_init(pv_done, 1);
     mbar_init(o_done, 1);
+    mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     *abort_flag = 0;
   }
@@ -162,19 +263,37 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   __syncthreads();
   const int la = *la_s, lb = *lb_s;
-  // opened groups: list A (head 0) in order, then the B-only entries (head 1)
-  for (int i = tid; i < la; i += kThreads) {
-    const int g = gidA[i];
-    int t1 = 1 << 20;
-    int lo = 0, hi = lb - 1;
-    while (lo <= hi) {
-      const int mid = (lo + hi) >> 1;
-      const int x = gidB[mid];
-      if (x == g) { t1 = t0B[mid]; break; }
-      if (x < g) lo = mid + 1; else hi = mid - 1;
+  // opened groups in three runs: both heads (in head 0's order), head 0 only, head 1 only.  A
+  // warp's rows belong to one head, so a run of single-head units leaves the other head's warps
+  // whole tiles with nothing visible, which they skip.
+  if (warp == 2) {
+    int both = 0;
+    for (int pass = 0; pass < 2; ++pass) {
+      int written = 0;
+      for (int base = 0; base < la; base += 32) {
+        const int j = base + lane;
+        int g = 0, t1 = 1 << 20;
+        if (j < la) {
+          g = gidA[j];
+          int lo = 0, hi = lb - 1;
+          while (lo <= hi) {
+            const int mid = (lo + hi) >> 1;
+            const int x = gidB[mid];
+            if (x == g) { t1 = t0B[mid]; break; }
+            if (x < g) lo = mid + 1; else hi = mid - 1;
+          }
+        }
+        const bool take = j < la && ((t1 < (1 << 20)) == (pass == 0));
+        const unsigned bal = __ballot_sync(0xffffffffu, take);
+        if (take) {
+          const int slot = n_shared + (pass ? both : 0) + written + __popc(bal & ((1u << lane) - 1u));
+          Unit e; e.pos = g * gs; e.tmin0 = t0A[j]; e.tmin1 = t1; e.causal = 0;
+          units[slot] = e;
+        }
+        written += __popc(bal);
+      }
+      if (pass == 0) both = written;
     }
-    Unit e; e.pos = g * gs; e.tmin0 = t0A[i]; e.tmin1 = t1; e.causal = 0;
-    units[n_shared + i] = e;
   }
   if (warp == 3) {
     int written = 0;
@@ -228,19 +347,36 @@ __global__ void __launch_bounds__(kThreads, 2)
           else tma_load_2d(dst, &tm_q, kb * 64, (b * a.H + h0 + hh) * a.sq + lrow0, q_full);
         }
       const int64_t kvrow = ((int64_t)b * a.KVH + kvh) * a.kv_cap;
-      for (int i = 0; i < ntiles; ++i) {
+      // K of tile i+1 is issued before V of tile i: Q.K^T(i-1), which frees K's stage, completes
+      // before P.V(i-2), which frees V's
+      int armed_k = 0, armed_v = 0;  // loads issued per kind (their barriers' phases, for the drain)
+      auto load = [&](int i, bool is_v) -> bool {
         const int st = i & 1;
-        if (i >= 2 && !mbar_wait(kv_empty + st, ((i >> 1) - 1) & 1, abort_flag, 1)) break;
-        unsigned char* kdst = smem + SmemLayout::kStage + st * SmemLayout::kStageBytes;
-        unsigned char* vdst = kdst + 16384;
-        mbar_expect_tx(kv_full + st, 32768);
+        uint64_t* empty = is_v ? v_empty : k_empty;
+        uint64_t* full = is_v ? v_full : k_full;
+        if (i >= 2 && !mbar_wait(empty + st, ((i >> 1) - 1) & 1, abort_flag, is_v ? 9 : 1)) return false;
+        unsigned char* dst = smem + SmemLayout::kStage + st * SmemLayout::kStageBytes + (is_v ? 16384 : 0);
+        const CUtensorMap* map = is_v ? &tm_v : &tm_k;
+        mbar_expect_tx(full + st, 16384);
         for (int u = 0; u < kUnitsPerTile; ++u) {
           const int row = (int)(kvrow + units[i * kUnitsPerTile + u].pos);
-          for (int kb = 0; kb < 2; ++kb) {
-            tma_load_2d(kdst + kb * 8192 + u * 2048, &tm_k, kb * 64, row, kv_full + st);
-            tma_load_2d(vdst + kb * 8192 + u * 2048, &tm_v, kb * 64, row, kv_full + st);
-          }
+          tma_load_2d(dst + u * 2048, map, 0, row, full + st);
+          tma_load_2d(dst + 8192 + u * 2048, map, 64, row, full + st);
         }
+        (is_v ? armed_v : armed_k) += 1;
+        return true;
+      };
+      bool go = ntiles > 0 && load(0, false);
+      for (int i = 0; go && i < ntiles; ++i) {
+        if (i + 1 < ntiles) go = load(i + 1, false);
+        if (go) go = load(i, true);
+      }
+      // drain: a CTA that gives up must not release its shared memory under loads still in flight
+      for (int st = 0; st < 2; ++st) {
+        const int nk = armed_k > st ? (armed_k - 1 - st) / 2 + 1 : 0;  // loads armed on stage st
+        const int nv = armed_v > st ? (armed_v - 1 - st) / 2 + 1 : 0;
+        if (nk) mbar_drain(k_full + st, (nk - 1) & 1);
+        if (nv) mbar_drain(v_full + st, (nv - 1) & 1);
       }
     }
   } else if (warp == 1) {
@@ -255,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int i = 0; ok && i <= ntiles; ++i) {
         if (i < ntiles) {
           const int st = i & 1;
-          if (!mbar_wait(kv_full + st, (i >> 1) & 1, abort_flag, 3)) break;
+          if (!mbar_wait(k_full + st, (i >> 1) & 1, abort_flag, 3)) break;
           if (i >= 2 && !mbar_wait(pv_done, (i - 2) & 1, abort_flag, 4)) break;
           fence_after();
           const uint32_t k_addr = smem_u32(smem + SmemLayout::kStage + st * SmemLayout::kStageBytes);
@@ -265,10 +401,12 @@ __global__ void __launch_bounds__(kThreads, 2)
               mma_ss(d, sdesc(q_addr + kb * 16384 + kk * 32, 16, 1024), sdesc(k_addr + kb * 8192 + kk * 32, 16, 1024),
                      id_qk, (kb | kk) != 0);
           mma_commit(s_full + st);
+          mma_commit(k_empty + st);
         }
         if (i >= 1) {
           const int j = i - 1, st = j & 1;
           if (!mbar_wait(p_full + st, (j >> 1) & 1, abort_flag, 5)) break;
+          if (!mbar_wait(v_full + st, (j >> 1) & 1, abort_flag, 10)) break;
           fence_after();
           const uint32_t v_addr = smem_u32(smem + SmemLayout::kStage + st * SmemLayout::kStageBytes + 16384);
           const uint32_t p_col = tmem + (st ? kColS1 : kColS0);
@@ -276,10 +414,14 @@ __global__ void __launch_bounds__(kThreads, 2)
             mma_ts(tmem + kColO, p_col + kk * 8, sdesc(v_addr + kk * 2048, 8192, 1024), id_pv,
                    (j > 0 || kk > 0) ? 1u : 0u);
           mma_commit(pv_done);
-          mma_commit(kv_empty + st);
+          mma_commit(v_empty + st);
           if (j == ntiles - 1) mma_commit(o_done);
         }
       }
+      // drain: wait until every MMA this thread issued has completed (it reads smem and TMEM that
+      // are released below), also when the loop was left on a timeout
+      mma_commit(drain);
+      mbar_drain(drain, 0);
     }
   } else {
     // ------------------------------- softmax / epilogue -------------------------------------
@@ -296,15 +438,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     bool ok = true;
     for (int i = 0; i < ntiles && ok; ++i) {
       const int st = i & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 6));
-      if (!ok) break;
-      fence_after();
-      const uint32_t s_addr = tmem + lane_addr + (st ? kColS1 : kColS0);
-      uint32_t r[64];
-      HGA_LD32(s_addr + 0, (r + 0));
-      HGA_LD32(s_addr + 32, (r + 32));
-      // visible-prefix length of each unit for this row
+      // visibility of the tile's units for this row: a visible prefix of cnt[u] keys (the causal
+      // current-chunk tile, i == 0) or all / none of them; `live` marks the units some row of this
+      // warp sees (the others are neither loaded nor exponentiated)
       int cnt[kUnitsPerTile];
+      unsigned live = 0;
 #pragma unroll
       for (int u = 0; u < kUnitsPerTile; ++u) {
         const Unit e = units[i * kUnitsPerTile + u];
@@ -312,64 +450,69 @@ __global__ void __launch_bounds__(kThreads, 2)
         int c = e.causal ? t - tmin + 1 : (t >= tmin ? 16 : 0);
         c = c < 0 ? 0 : (c > 16 ? 16 : c);
         cnt[u] = rvalid ? c : 0;
+        if (__any_sync(0xffffffffu, cnt[u] > 0)) live |= 1u << u;
       }
-      tmem_wait_ld();
-      // row max over the visible keys: four independent partial maxima (short dependence chains)
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 6));
+      if (!ok) break;
+      fence_after();
+      const uint32_t s_addr = tmem + lane_addr + (st ? kColS1 : kColS0);
+      uint32_t r[64];
 #pragma unroll
-      for (int u = 0; u < kUnitsPerTile; ++u) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float x = j < cnt[u] ? __uint_as_float(r[u * 16 + j]) : -INFINITY;
-          mx4[j & 3] = fmaxf(mx4[j & 3], x);
-        }
-      }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      const float m_tile = mx * sl2;
-      // lazy rescale: only when the max grows by more than 2^8 (or the first visible keys arrive)
-      float alpha = 1.f;
-      bool rescale_o = false;
-      if (m_tile > m_run + 8.f) {
-        if (m_run != -INFINITY) {
-          alpha = ex2(m_run - m_tile);
-          l_run *= alpha;
-          rescale_o = true;
-        }
-        m_run = m_tile;
-      }
-      if (__any_sync(0xffffffffu, rescale_o)) {
-        // O holds the sum over tiles < i: wait for the last P.V, then rescale (alpha = 1 elsewhere)
-        ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (i - 1) & 1, abort_flag, 7));
-        if (!ok) break;
-        fence_after();
-        const uint32_t o_addr = tmem + lane_addr + kColO;
-        for (int c0 = 0; c0 < 128; c0 += 32) {
-          uint32_t o[32];
-          HGA_LD32(o_addr + c0, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          HGA_ST32(o_addr + c0, o);
-        }
-        tmem_wait_st();
-      }
-      float ps4[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums (short dependence chains)
+      for (int u = 0; u < kUnitsPerTile; ++u)
+        if (live >> u & 1) HGA_LD16(s_addr + u * 16, (r + u * 16));
+      if (live) tmem_wait_ld();
+      // Tile 0 (the causal current chunk, where every valid row sees at least its own key) sets
+      // the running max.  Later tiles are exponentiated against the running max directly; only
+      // when a p could exceed 2^8 (the row's tile sum is above 2^8, or not finite) does the warp
+      // take the max pass and, if the max grew by more than 2^8, rescale O (lazy rescaling).
       uint32_t pk[32];
-      const float nm = m_run == -INFINITY ? 0.f : -m_run;  // no visible key yet: every p is 0
-#pragma unroll
-      for (int u = 0; u < kUnitsPerTile; ++u) {
-#pragma unroll
-        for (int j = 0; j < 16; j += 2) {
-          // invisible keys: exponent of -inf, which ex2 maps to 0
-          const float x0 = j < cnt[u] ? __uint_as_float(r[u * 16 + j]) : -INFINITY;
-          const float x1 = j + 1 < cnt[u] ? __uint_as_float(r[u * 16 + j + 1]) : -INFINITY;
-          const float p0 = ex2(fmaf(x0, sl2, nm));
-          const float p1 = ex2(fmaf(x1, sl2, nm));
-          ps4[(j >> 1) & 3] += p0 + p1;
-          pk[(u * 16 + j) >> 1] = pack_bf16(p0, p1);
-        }
+      uint64_t ps = f2(0.f, 0.f);                            // paired partial row sums
+      const uint64_t sl2x2 = f2(sl2, sl2);
+      bool redo = i == 0;
+      if (i > 0) {
+        const float nm = m_run == -INFINITY ? 0.f : -m_run;
+        tile_exp<false>(r, cnt, live, sl2x2, f2(nm, nm), pk, ps);
+        float q0, q1;
+        unf2(ps, q0, q1);
+        redo = __any_sync(0xffffffffu, !(q0 + q1 <= 256.f));
       }
-      l_run += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
+      if (redo) {
+        const float mx = i == 0 ? tile_max<true>(r, cnt, live) : tile_max<false>(r, cnt, live);
+        const float m_tile = mx * sl2;
+        float alpha = 1.f;
+        bool rescale_o = false;
+        if (m_tile > m_run + 8.f) {
+          if (m_run != -INFINITY) {
+            alpha = ex2(m_run - m_tile);
+            l_run *= alpha;
+            rescale_o = true;
+          }
+          m_run = m_tile;
+        }
+        if (__any_sync(0xffffffffu, rescale_o)) {
+          // O holds the sum over tiles < i: wait for the last P.V, then rescale (alpha = 1 elsewhere)
+          ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (i - 1) & 1, abort_flag, 7));
+          if (!ok) break;
+          fence_after();
+          const uint32_t o_addr = tmem + lane_addr + kColO;
+          for (int c0 = 0; c0 < 128; c0 += 32) {
+            uint32_t o[32];
+            HGA_LD32(o_addr + c0, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            HGA_ST32(o_addr + c0, o);
+          }
+          tmem_wait_st();
+        }
+        const float nm = m_run == -INFINITY ? 0.f : -m_run;  // no visible key yet: every p is 0
+        ps = f2(0.f, 0.f);
+        if (i == 0) tile_exp<true>(r, cnt, live, sl2x2, f2(nm, nm), pk, ps);
+        else tile_exp<false>(r, cnt, live, sl2x2, f2(nm, nm), pk, ps);
+      }
+      float ps0, ps1;
+      unf2(ps, ps0, ps1);
+      l_run += ps0 + ps1;
       HGA_ST32(s_addr, pk);
       tmem_wait_st();
       fence_before();

@@ -79,6 +79,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return true;
 }
 
+// Bounded wait that ignores the CTA abort flag: used on the way out, to let copies and MMAs that
+// are still in flight land before the CTA releases its shared memory and TMEM.  Gives up after
+// kDrainLimitNs (recording code 0x7f) so a lost completion cannot hang the CTA.
+constexpr unsigned long long kDrainLimitNs = 500000000ull;
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try(bar, parity)) {
+    if (global_ns() - t0 > kDrainLimitNs) {
+      atomicCAS(&g_tc_error, 0, 0x7f);
+      return;
+    }
+  }
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -140,6 +155,13 @@ __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::aft
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),     \
         "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),    \
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                 \
+      : "r"(taddr))
+
+#define HGA_LD16(taddr, r)                                                                                   \
+  asm volatile(                                                                                              \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];" \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),       \
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])   \
       : "r"(taddr))
 
 #define HGA_ST32(taddr, r)                                                                                         \
