@@ -72,6 +72,21 @@ __device__ __forceinline__ uint32_t ord16_bits(uint32_t rounded) {
   return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
 }
 
+// two fp32 values rounded to bf16 (round-to-nearest-even) in one word: lo in bits 0-15
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// (lo, hi) * scale, one paired fp32 multiply (round-to-nearest, like two scalar multiplies)
+__device__ __forceinline__ void mul2_scale(float lo, float hi, float scale, float& o0, float& o1) {
+  uint64_t x, sc, y;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(lo), "f"(hi));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(sc) : "f"(scale));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(y) : "l"(x), "l"(sc));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(o0), "=f"(o1) : "l"(y));
+}
+
 __device__ __forceinline__ float bf16_score(uint32_t acc_bits, float scale) {
   return Num<__nv_bfloat16>::round(__fmul_rn(Num<__nv_bfloat16>::round(__uint_as_float(acc_bits)), scale));
 }
@@ -360,25 +375,35 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
         uint32_t r[32];
         HGA_LD32(sa + 32 * c4, r);
         tmem_wait_ld();
-        // keys of the 32 columns, and the mask of those above the row's current threshold
-        uint32_t mask = 0u;
+        // keys of the 32 columns, two at a time: both reference roundings (bf16 einsum output, then
+        // "* scale" in fp32 stored as bf16) as paired conversions and a paired multiply, then the
+        // order-preserving 16-bit key of each half (sign set: all bits flipped; else the sign
+        // bit set), then the pool index below it (equal scores: the lower index ranks higher)
         const uint32_t thr = lst[KL - 1];
+        const int nv = rvalid ? min(32, cmax - 32 * c4) : 0;  // valid columns of this batch
+        const uint32_t cbase = 0xffffu - (uint32_t)(128 * i + 32 * c4);
+        bool above = false;
 #pragma unroll
-        for (int cc = 0; cc < 32; ++cc) {
-          const int c = 32 * c4 + cc;
-          uint32_t key = 0u;
-          if (rvalid && c < cmax) {
-            const uint32_t sb = bf16_score_bits(r[cc], a.scale);
-            const uint32_t cr = 128 * i + c;
-            if (a.dbg_l1) a.dbg_l1[dbg_row + cr] = __uint_as_float(sb);
-            key = (ord16_bits(sb) << 16) | (0xffffu - cr);
+        for (int cc = 0; cc < 32; cc += 2) {
+          const uint32_t w = cvt_bf16x2(__uint_as_float(r[cc]), __uint_as_float(r[cc + 1]));
+          float s0, s1;
+          mul2_scale(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u), a.scale, s0, s1);
+          const uint32_t w2 = cvt_bf16x2(s0, s1);
+          const uint32_t o = w2 ^ (((w2 >> 15) & 0x00010001u) * 0x7fffu + 0x80008000u);
+          const uint32_t k0 = cc < nv ? ((o << 16) | (cbase - cc)) : 0u;
+          const uint32_t k1 = cc + 1 < nv ? ((o & 0xffff0000u) | (cbase - cc - 1)) : 0u;
+          if (a.dbg_l1) {
+            const size_t cr = dbg_row + 128 * i + 32 * c4 + cc;
+            if (cc < nv) a.dbg_l1[cr] = __uint_as_float(w2 << 16);
+            if (cc + 1 < nv) a.dbg_l1[cr + 1] = __uint_as_float(w2 & 0xffff0000u);
           }
-          r[cc] = key;
-          mask |= (key > thr ? 1u : 0u) << cc;
+          r[cc] = k0;
+          r[cc + 1] = k1;
+          above |= (k0 > thr) | (k1 > thr);
         }
         // the batch's keys join the row's list through sorting networks (no per-key insertion);
         // skipped when no row of the warp has a key above its current threshold
-        if (__any_sync(0xffffffffu, mask != 0u)) merge_batch<KL>(lst, r);
+        if (__any_sync(0xffffffffu, above)) merge_batch<KL>(lst, r);
       }
       fence_before();
       mbar_arrive(s_free + st);
@@ -574,42 +599,91 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
             a.dbg_l2[dbg_row + j] = kNeg;
           }
         }
-        r[j] = key;
+        r[j] = key ? ((key << 16) | (0xffffu - j)) : 0u;  // unique: equal scores -> lower j first
         nreal += key != 0u;
       }
-      // requests = keys > T plus the lowest-index keys == T (Kgr in total); every lane runs the
-      // warp reductions below, rows without real candidates contribute nothing
+      // Requests = the row's Kgr highest keys, equal scores broken by the lower candidate index
+      // (unique 32-bit keys: score << 16 | 0xffff - j).  With 64 candidates and Kgr <= 32 the
+      // threshold comes from sorting networks (two sorted halves, a max-merge to the top-32 set,
+      // one bitonic clean); otherwise from a radix select on the 16-bit score.
       const bool active = rvalid && nreal > 0;
-      uint32_t T = 0;
-      int need = 1 << 30;
       const bool all = a.Kgr >= a.Kc * M || nreal <= a.Kgr;
-      if (active && !all) {
+      uint16_t* pm = reinterpret_cast<uint16_t*>(q_s);           // [2][64][KT], see below
+      auto put = [&](uint32_t k32) {  // record a requested key in the pooling matrix
+        const int j = 0xffff - (int)(k32 & 0xffffu);
+        pm[(size_t)(hs * 64 + t) * KT + j] = (uint16_t)(k32 >> 16);
+      };
+      const bool sorted_path = KT == 64 && a.Kgr <= 32 && active && !all;
+      uint32_t T = 0u;    // radix path: requested iff score > T, or == T for the first `need` (lowest j)
+      int need = 0;
+      if constexpr (KT == 64) {
+        if (sorted_path) {
+          sort_desc<32>(r);
+          sort_desc<32>(r + 32);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = max(r[i], r[KT - 1 - i]);
+          clean_desc<32>(r);  // r[0..31]: the 32 highest keys, descending
+        }
+      }
+      if (!sorted_path && active && !all) {
         for (int bit = 15; bit >= 0; --bit) {
-          const uint32_t cand = T | (1u << bit);
+          const uint32_t cand = (T | (1u << bit)) << 16;
           int c4[4] = {0, 0, 0, 0};  // four partial counts: short dependence chains
 #pragma unroll
           for (int j = 0; j < KT; ++j) c4[j & 3] += r[j] >= cand;
-          if (c4[0] + c4[1] + c4[2] + c4[3] >= a.Kgr) T = cand;
+          if (c4[0] + c4[1] + c4[2] + c4[3] >= a.Kgr) T |= 1u << bit;
         }
-        int gt = 0;
+        need = a.Kgr;
 #pragma unroll
-        for (int j = 0; j < KT; ++j) gt += r[j] > T;
-        need = a.Kgr - gt;
+        for (int j = 0; j < KT; ++j) need -= (r[j] >> 16) > T;
       }
+      // Pooling (max requesting score and first requesting row per candidate): each row thread
+      // stores its requested scores into a [head][row][candidate] u16 matrix in the freed Q area,
+      // then one thread per (head, candidate) reduces the candidate's column over the 64 rows.
+      // every row thread writes its whole row (zeros where nothing is requested); the matrix
+      // reuses the Q area, which the level-2 MMA (waited for above) no longer reads
+      uint4* prow = reinterpret_cast<uint4*>(pm + (size_t)(hs * 64 + t) * KT);
+      if (sorted_path) {
 #pragma unroll
-      for (int j = 0; j < KT; ++j) {
-        bool req = false;
-        if (active && r[j] != 0u) {
-          if (all || r[j] > T) req = true;
-          else if (r[j] == T && need > 0) { req = true; --need; }
+        for (int c = 0; c < KT / 8; ++c) prow[c] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < a.Kgr && r[i]) put(r[i]);
+      } else {
+        // the row's requested scores (0 elsewhere), packed in pairs, as whole 16-byte pieces
+#pragma unroll
+        for (int c = 0; c < KT / 8; ++c) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            uint32_t sc[2] = {r[8 * c + 2 * e] >> 16, r[8 * c + 2 * e + 1] >> 16};
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              bool req = false;
+              if (active && sc[h2]) {
+                if (all || sc[h2] > T) req = true;
+                else if (sc[h2] == T && need > 0) { req = true; --need; }  // ascending j: lowest index first
+              }
+              sc[h2] = req ? sc[h2] : 0u;
+            }
+            w[e] = sc[0] | (sc[1] << 16);
+          }
+          prow[c] = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        // warp-level min/max first: one smem atomic per group per warp
-        const uint32_t tmin = __reduce_min_sync(0xffffffffu, req ? (uint32_t)t : 0xffffffffu);
-        const uint32_t kmax = __reduce_max_sync(0xffffffffu, req ? r[j] : 0u);
-        if (lane == (j & 31) && kmax != 0u) {
-          atomicMin(&ms->gt0[hs][j], tmin);
-          atomicMax(&ms->gpool[hs][j], kmax);
+      }
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      for (int i = row; i < 2 * KT; i += 128) {
+        const int hh = i / KT, j = i % KT;
+        const uint16_t* src = pm + (size_t)hh * 64 * KT + j;  // column j: consecutive lanes, consecutive j
+        uint32_t mx = 0u, first = 0xffffffffu;
+#pragma unroll 16
+        for (int t2 = 63; t2 >= 0; --t2) {
+          const uint32_t v = src[(size_t)t2 * KT];
+          mx = max(mx, v);
+          first = v ? (uint32_t)t2 : first;
         }
+        ms->gpool[hh][j] = mx;
+        ms->gt0[hh][j] = mx ? first : 0xffffffffu;
       }
     }
     __syncthreads();
