@@ -43,6 +43,9 @@ _SIGNATURES = {
     "hga_last_error": (ctypes.c_char_p, []),
     "hga_summaries": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _I64, _P, _P, _P, _I64, _P, _P, _I32, _I64,
                                      _P, _P, _P, _I64, _I64, _P]),
+    "hga_summaries_dual": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _I64, _P, _P, _P, _I64, _P, _P, _I64,
+                                          _I32, _P, _P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _P, _I64, _I64,
+                                          _P]),
     "hga_route_prefill": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _P, _I32, _P, _P, _I64, _P, _P, _P, _P,
                                          _P, _P, _P]),
     "hga_route_prefill_impl": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _P, _I32, _P, _P, _I64, _P, _P, _P,

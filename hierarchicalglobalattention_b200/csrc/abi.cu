@@ -10,6 +10,13 @@ cudaError_t launch_summaries(const hga_params& p, int64_t S, int64_t pos0, const
                              const void* v, int64_t kv_cap, const void* cos, const void* sin, int rot_dtype,
                              int64_t rot_row0, void* ck, void* gk, void* gv, int64_t sum_cap, int64_t out_chunk0,
                              cudaStream_t st);
+bool summaries_dual_supported(const hga_params& p);
+cudaError_t launch_summaries_dual(const hga_params& p, int64_t S, int64_t pos0, const void* k_raw,
+                                  const void* k_rope, const void* v, int64_t kv_cap, const float* cosA,
+                                  const float* sinA, int64_t rowA0, int roundA, void* ckA, void* gkA,
+                                  int64_t capA, int64_t outA0, const float* cosB, const float* sinB,
+                                  int64_t rowB0, int nB, void* ckB, void* gkB, void* gvB, int64_t capB,
+                                  int64_t outB0, cudaStream_t st);
 cudaError_t launch_route_prefill(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout, const void* ck,
                                  const void* gk, int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0,
                                  int32_t* open_gid, int32_t* open_t0, float* dbg1, float* dbg2, cudaStream_t st,
@@ -138,6 +145,37 @@ int hga_summaries(const hga_params* p, int64_t seq_len, int64_t pos0, const void
   return cuda_status(hga::launch_summaries(*p, seq_len, pos0, k_raw, k_rope, v, kv_cap, cos, sin, rot_mode, rot_row0,
                                            chunk_k, group_k, group_v, sum_cap, out_chunk0, stream),
                      "hga_summaries");
+}
+
+int hga_summaries_dual(const hga_params* p, int64_t seq_len, int64_t pos0, const void* k_raw, const void* k_rope,
+                       const void* v, int64_t kv_cap, const float* cos_a, const float* sin_a, int64_t rot_row0_a,
+                       int32_t round_a, void* chunk_a, void* group_a, int64_t sum_cap_a, int64_t out_a0,
+                       const float* cos_b, const float* sin_b, int64_t rot_row0_b, int64_t n_b, void* chunk_b,
+                       void* group_b, void* group_vb, int64_t sum_cap_b, int64_t out_b0, cudaStream_t stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (seq_len <= 0) return HGA_OK;
+  if (!hga::summaries_dual_supported(*p))
+    return fail(HGA_E_UNSUPPORTED, "hga_summaries_dual: needs bf16/fp16, head_dim 64/128, chunk/group multiples of 16");
+  if (!k_raw || !k_rope || !v || !cos_a || !sin_a || !chunk_a || !group_a)
+    return fail(HGA_E_INVALID, "hga_summaries_dual: NULL tensor");
+  if (kv_cap < seq_len) return fail(HGA_E_INVALID, "hga_summaries_dual: kv_cap < seq_len");
+  if (pos0 % p->chunk_size) return fail(HGA_E_INVALID, "hga_summaries_dual: pos0 must be chunk aligned");
+  const int64_t N = (seq_len + p->chunk_size - 1) / p->chunk_size;
+  if (pos0 < rot_row0_a || out_a0 < 0 || out_a0 + N > sum_cap_a)
+    return fail(HGA_E_INVALID, "hga_summaries_dual: set A table or capacity out of range");
+  if (n_b < 0 || n_b > seq_len / p->chunk_size) return fail(HGA_E_INVALID, "hga_summaries_dual: n_b beyond the closed chunks");
+  if (n_b > 0 && (!cos_b || !sin_b || !chunk_b || !group_b || pos0 < rot_row0_b || out_b0 < 0 || out_b0 + n_b > sum_cap_b))
+    return fail(HGA_E_INVALID, "hga_summaries_dual: set B tensors, table or capacity out of range");
+  if ((((uintptr_t)k_raw | (uintptr_t)k_rope | (uintptr_t)v | (uintptr_t)chunk_a | (uintptr_t)group_a |
+        (uintptr_t)chunk_b | (uintptr_t)group_b | (uintptr_t)group_vb | (uintptr_t)cos_a | (uintptr_t)sin_a |
+        (uintptr_t)cos_b | (uintptr_t)sin_b) & 15))
+    return fail(HGA_E_INVALID, "hga_summaries_dual: pointers must be 16-byte aligned");
+  return cuda_status(hga::launch_summaries_dual(*p, seq_len, pos0, k_raw, k_rope, v, kv_cap, cos_a, sin_a, rot_row0_a,
+                                                round_a, chunk_a, group_a, sum_cap_a, out_a0, cos_b, sin_b,
+                                                rot_row0_b, (int)n_b, chunk_b, group_b, group_vb, sum_cap_b, out_b0,
+                                                stream),
+                     "hga_summaries_dual");
 }
 
 int hga_route_prefill(const hga_params* p, int64_t seq_len, const void* q, int32_t q_layout, const void* chunk_k,

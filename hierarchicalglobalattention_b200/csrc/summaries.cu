@@ -151,3 +151,206 @@ cudaError_t launch_summaries(const hga_params& p, int64_t S, int64_t pos0, const
 }
 
 }  // namespace hga
+
+namespace hga {
+
+// Both summary sets of a fresh prefill from one read of K/V: set A (the chunk-parallel routing
+// summaries of all N chunks, endpoint rotation from table A) and set B (the store seed of the first
+// nB closed chunks, endpoint rotation from table B, group V sums included).  The sums are the same
+// for both sets; only the endpoint rotation (table, rounding of the table entries) and the
+// destination differ.
+//
+// Thread = (chunk, 16-row block, 8 contiguous head-dim columns): it reads each of its 16 token rows
+// as one 16-byte piece per tensor and sums them sequentially in fp32 (the order of torch's CPU
+// reduction, as in summaries_kernel).  The block partials meet in shared memory, where the group
+// and chunk totals are formed by adding the partials in block order, then the summaries are
+// rotated and written (16-byte stores).  bf16 / fp16, head_dim 64 or 128, chunk and group sizes
+// multiples of 16, chunk_size <= 128.
+template <typename T, int DH>
+__global__ void __launch_bounds__(256) summaries_dual_kernel(
+    hga_params p, int64_t S, int64_t pos0, const T* __restrict__ k_raw, const T* __restrict__ k_rope,
+    const T* __restrict__ v, int64_t kv_cap, int N, int cpb,
+    const float* __restrict__ cosA, const float* __restrict__ sinA, int64_t rowA0, int roundA, T* ckA, T* gkA,
+    int64_t capA, int64_t outA0,
+    const float* __restrict__ cosB, const float* __restrict__ sinB, int64_t rowB0, int nB, T* ckB, T* gkB, T* gvB,
+    int64_t capB, int64_t outB0) {
+  constexpr int CG = DH / 8, HALF = DH / 2;
+  extern __shared__ float sm[];
+  const int C = p.chunk_size, gs = p.group_size, M = C / gs, NBLK = C / 16, BPG = gs / 16;
+  // smem: block partials [cpb][NBLK][3][DH] (raw, rope, v), then rotation scratch [cpb][M + 1][DH]
+  float* part = sm;
+  float* rot = sm + (size_t)cpb * NBLK * 3 * DH;
+  const int tid = threadIdx.x;
+  const int cg = tid % CG, blk = (tid / CG) % NBLK, ci = tid / (CG * NBLK);
+  const int bk = blockIdx.y;
+  const int c = blockIdx.x * cpb + ci;
+  const bool mine = ci < cpb;
+  const int64_t row0 = (int64_t)c * C;
+  const int len = (mine && c < N) ? (int)((S - row0) < C ? (S - row0) : C) : 0;
+  const size_t base = (size_t)bk * kv_cap * DH + (size_t)cg * 8;
+
+  // ---- phase 1: the 16-row block partials of this thread's 8 columns -------------------------
+  if (mine) {
+    float sr[8], so[8], sv[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sr[e] = so[e] = sv[e] = 0.f;
+    const int t0 = blk * 16;
+#pragma unroll 4
+    for (int u = 0; u < 16; ++u) {
+      const int t = t0 + u;
+      if (t < len) {
+        const size_t off = base + (size_t)(row0 + t) * DH;
+        const uint4 ur = __ldg(reinterpret_cast<const uint4*>(k_raw + off));
+        const uint4 uo = __ldg(reinterpret_cast<const uint4*>(k_rope + off));
+        const uint4 uv = __ldg(reinterpret_cast<const uint4*>(v + off));
+        const T* hr = reinterpret_cast<const T*>(&ur);
+        const T* ho = reinterpret_cast<const T*>(&uo);
+        const T* hv = reinterpret_cast<const T*>(&uv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          sr[e] = __fadd_rn(sr[e], Num<T>::to_f(hr[e]));
+          so[e] = __fadd_rn(so[e], Num<T>::to_f(ho[e]));
+          sv[e] = __fadd_rn(sv[e], Num<T>::to_f(hv[e]));
+        }
+      }
+    }
+    float* pp = part + ((size_t)(ci * NBLK + blk) * 3) * DH + cg * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) { pp[e] = sr[e]; pp[DH + e] = so[e]; pp[2 * DH + e] = sv[e]; }
+  }
+  __syncthreads();
+
+  // ---- phase 2: group and chunk sums (block partials added in order), rounded raw sums -------
+  // slot j < M: group j (thread blk == j, when j < NBLK); slot M: the chunk (thread blk == M % NBLK
+  // for the raw chunk sum, computed by the thread of block 0 when M == NBLK)
+  const int slot = blk < M ? blk : -1;
+  const int cslot = (M < NBLK) ? M : 0;  // which block thread also owns the chunk sums
+  float g_rs[8], g_tw[8], g_vs[8], c_rs[8], c_tw[8];
+  if (mine) {
+    if (slot >= 0) {
+      float gr[8], go[8], gv[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) gr[e] = go[e] = gv[e] = 0.f;
+      for (int q = 0; q < BPG; ++q) {
+        const float* pp = part + ((size_t)(ci * NBLK + slot * BPG + q) * 3) * DH + cg * 8;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          gr[e] = __fadd_rn(gr[e], pp[e]);
+          go[e] = __fadd_rn(go[e], pp[DH + e]);
+          gv[e] = __fadd_rn(gv[e], pp[2 * DH + e]);
+        }
+      }
+      const float sc = p.group_kv_scale;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        g_rs[e] = Num<T>::round(__fmul_rn(Num<T>::round(gr[e]), sc));
+        g_tw[e] = Num<T>::round(__fmul_rn(Num<T>::round(go[e]), sc));
+        g_vs[e] = Num<T>::round(__fmul_rn(Num<T>::round(gv[e]), sc));
+        rot[((size_t)ci * (M + 1) + slot) * DH + cg * 8 + e] = g_rs[e];
+      }
+    }
+    if (blk == cslot) {
+      float cr[8], co[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) cr[e] = co[e] = 0.f;
+      for (int q = 0; q < NBLK; ++q) {
+        const float* pp = part + ((size_t)(ci * NBLK + q) * 3) * DH + cg * 8;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { cr[e] = __fadd_rn(cr[e], pp[e]); co[e] = __fadd_rn(co[e], pp[DH + e]); }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        c_rs[e] = Num<T>::round(cr[e]);
+        c_tw[e] = Num<T>::round(co[e]);
+        rot[((size_t)ci * (M + 1) + M) * DH + cg * 8 + e] = c_rs[e];
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- phase 3: endpoint rotations and stores -----------------------------------------------
+  auto emit = [&](int sl, const float* rs, const float* tw, const float* cs_t, const float* sn_t, int64_t trow,
+                  int rnd, T* dst) {
+    const int d0 = cg * 8;
+    const float4* cp = reinterpret_cast<const float4*>(cs_t + trow * DH + d0);
+    const float4* sp = reinterpret_cast<const float4*>(sn_t + trow * DH + d0);
+    const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+    float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const float* partner = rot + ((size_t)ci * (M + 1) + sl) * DH;
+    uint4 u;
+    T* h = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (rnd) { cs[e] = Num<T>::round(cs[e]); sn[e] = Num<T>::round(sn[e]); }
+      const int d = d0 + e;
+      const float ep = d < HALF ? __fsub_rn(__fmul_rn(rs[e], cs[e]), __fmul_rn(partner[d + HALF], sn[e]))
+                                : __fadd_rn(__fmul_rn(rs[e], cs[e]), __fmul_rn(partner[d - HALF], sn[e]));
+      h[e] = Num<T>::from_f((d % HALF) < p.cutoff_pair ? tw[e] : Num<T>::round(ep));
+    }
+    *reinterpret_cast<uint4*>(dst + d0) = u;
+  };
+  if (len > 0) {
+    if (slot >= 0) {
+      const int m = slot;
+      int glen = len - m * gs;
+      glen = glen < 0 ? 0 : (glen > gs ? gs : glen);
+      int64_t anchor = row0 + m * gs + ((glen < 1 ? 1 : glen) - 1) / 2;
+      if (anchor > S - 1) anchor = S - 1;
+      emit(m, g_rs, g_tw, cosA, sinA, pos0 + anchor - rowA0, roundA,
+           gkA + (((size_t)bk * capA + outA0 + c) * M + m) * DH);
+      if (c < nB) {
+        const size_t o = (((size_t)bk * capB + outB0 + c) * M + m) * DH;
+        emit(m, g_rs, g_tw, cosB, sinB, pos0 + row0 + m * gs + (gs - 1) / 2 - rowB0, 0, gkB + o);
+        if (gvB) {
+          uint4 u;
+          T* h = reinterpret_cast<T*>(&u);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) h[e] = Num<T>::from_f(g_vs[e]);
+          *reinterpret_cast<uint4*>(gvB + o + cg * 8) = u;
+        }
+      }
+    }
+    if (blk == cslot) {
+      int64_t anchor = row0 + ((len < 1 ? 1 : len) - 1) / 2;
+      if (anchor > S - 1) anchor = S - 1;
+      emit(M, c_rs, c_tw, cosA, sinA, pos0 + anchor - rowA0, roundA, ckA + ((size_t)bk * capA + outA0 + c) * DH);
+      if (c < nB)
+        emit(M, c_rs, c_tw, cosB, sinB, pos0 + row0 + (C - 1) / 2 - rowB0, 0,
+             ckB + ((size_t)bk * capB + outB0 + c) * DH);
+    }
+  }
+}
+
+bool summaries_dual_supported(const hga_params& p) {
+  return (p.dtype == HGA_DTYPE_BF16 || p.dtype == HGA_DTYPE_F16) && (p.head_dim == 64 || p.head_dim == 128) &&
+         p.chunk_size % 16 == 0 && p.group_size % 16 == 0 && p.chunk_size <= 128;
+}
+
+cudaError_t launch_summaries_dual(const hga_params& p, int64_t S, int64_t pos0, const void* k_raw,
+                                  const void* k_rope, const void* v, int64_t kv_cap, const float* cosA,
+                                  const float* sinA, int64_t rowA0, int roundA, void* ckA, void* gkA,
+                                  int64_t capA, int64_t outA0, const float* cosB, const float* sinB,
+                                  int64_t rowB0, int nB, void* ckB, void* gkB, void* gvB, int64_t capB,
+                                  int64_t outB0, cudaStream_t st) {
+  const int N = (int)((S + p.chunk_size - 1) / p.chunk_size);
+  const int per_chunk = (p.head_dim / 8) * (p.chunk_size / 16);  // threads per chunk
+  const int cpb = 256 / per_chunk;                                 // chunks per CTA
+  const int M = p.chunk_size / p.group_size;
+  const size_t smem = ((size_t)cpb * (p.chunk_size / 16) * 3 + (size_t)cpb * (M + 1)) * p.head_dim * sizeof(float);
+  const dim3 grid((unsigned)((N + cpb - 1) / cpb), (unsigned)(p.batch * p.kv_heads));
+#define HGA_SD(TT, DHV)                                                                                      \
+  summaries_dual_kernel<TT, DHV><<<grid, 256, smem, st>>>(p, S, pos0, (const TT*)k_raw, (const TT*)k_rope,   \
+                                                          (const TT*)v, kv_cap, N, cpb, cosA, sinA, rowA0,   \
+                                                          roundA, (TT*)ckA, (TT*)gkA, capA, outA0, cosB, sinB, \
+                                                          rowB0, nB, (TT*)ckB, (TT*)gkB, (TT*)gvB, capB, outB0)
+  if (p.dtype == HGA_DTYPE_BF16) {
+    if (p.head_dim == 128) HGA_SD(__nv_bfloat16, 128); else HGA_SD(__nv_bfloat16, 64);
+  } else {
+    if (p.head_dim == 128) HGA_SD(__half, 128); else HGA_SD(__half, 64);
+  }
+#undef HGA_SD
+  return cudaGetLastError();
+}
+
+}  // namespace hga

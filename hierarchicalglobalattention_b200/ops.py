@@ -98,6 +98,43 @@ def summaries(p: HgaParams, k_raw: torch.Tensor, k_rope: torch.Tensor, v: torch.
     return ck, gk, gv
 
 
+def summaries_dual_supported(p: HgaParams) -> bool:
+    """hga_summaries_dual's shape rule: bf16/fp16, head_dim 64 or 128, chunk and group sizes multiples
+    of 16 (chunk <= 128)."""
+    return (p.dtype in (_lib.DTYPE_CODE[torch.bfloat16], _lib.DTYPE_CODE[torch.float16]) and p.head_dim in (64, 128)
+            and p.chunk_size % 16 == 0 and p.group_size % 16 == 0 and p.chunk_size <= 128)
+
+
+def summaries_dual(p: HgaParams, k_raw: torch.Tensor, k_rope: torch.Tensor, v: torch.Tensor,
+                   cos_a: torch.Tensor, sin_a: torch.Tensor, cos_b: torch.Tensor, sin_b: torch.Tensor,
+                   out_b: Tuple[torch.Tensor, torch.Tensor, Optional[torch.Tensor]], n_b: int, *,
+                   round_a: bool = True, rot_row0_a: int = 0, rot_row0_b: int = 0):
+    """Routing summaries (set A, fresh [B,KVH,N,(M,)Dh] tensors; fp32 table A, entries rounded to the
+    model dtype when ``round_a``) and the store seed of the first ``n_b`` closed chunks (set B, into
+    the capacity buffers ``out_b``; fp32 table B) from one read of K/V (see hga_summaries_dual).
+    Returns (chunk_k, group_k) of set A."""
+    _require_cuda(k_raw, k_rope, v, cos_a, sin_a, cos_b, sin_b)
+    B, KVH, S, Dh = k_raw.shape
+    C = p.chunk_size
+    M = C // p.group_size
+    N = (S + C - 1) // C
+    cap = kv_cap_of(k_raw)
+    if kv_cap_of(k_rope) != cap or kv_cap_of(v) != cap:
+        raise _lib.HgaError("k_raw / k_rope / v must share one capacity layout")
+    for t in (cos_a, sin_a, cos_b, sin_b):
+        if t.dtype != torch.float32:
+            raise _lib.HgaError("summaries_dual takes fp32 rotary tables")
+    cos_a, sin_a, cos_b, sin_b = (t.contiguous() for t in (cos_a, sin_a, cos_b, sin_b))
+    ck = torch.empty(B, KVH, N, Dh, device=k_raw.device, dtype=k_raw.dtype)
+    gk = torch.empty(B, KVH, N, M, Dh, device=k_raw.device, dtype=k_raw.dtype)
+    ckb, gkb, gvb = out_b
+    check(lib().hga_summaries_dual(ctypes_params(p), S, 0, ptr(k_raw), ptr(k_rope), ptr(v), cap, ptr(cos_a), ptr(sin_a),
+                                   rot_row0_a, int(round_a), ptr(ck), ptr(gk), N, 0, ptr(cos_b), ptr(sin_b), rot_row0_b,
+                                   n_b, ptr(ckb), ptr(gkb), ptr(gvb), ckb.shape[2], 0, stream_ptr(k_raw.device)),
+          "hga_summaries_dual")
+    return ck, gk
+
+
 def ctypes_params(p: HgaParams):
     import ctypes
     return ctypes.byref(p)

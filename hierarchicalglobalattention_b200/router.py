@@ -212,12 +212,23 @@ class ChunkRouter:
             round_table = True
         else:
             cos_t, sin_t = cos.reshape(-1, Dh)[-S:], sin.reshape(-1, Dh)[-S:]
-        # (1) routing summaries of the chunk-parallel path
-        ck, gk, _ = ops.summaries(hp, k_raw, k_rope, v, cos_t, sin_t, round_table=round_table, with_group_v=False)
+        n_closed = S // C
+        if (populate_store and n_closed and cos_t.dtype == torch.float32 and ops.summaries_dual_supported(hp)):
+            # (1) routing summaries and the store seed's closed-chunk summaries from one read of K/V
+            self._rot_stage_ready()
+            st = store.ensure_capacity(layer, max(n_closed, 1), S)
+            cos32, sin32 = self._rotary(k_raw.device, S)
+            ck, gk = ops.summaries_dual(hp, k_raw, k_rope, v, cos_t, sin_t, cos32, sin32,
+                                        (st.chunk_k, st.group_k, st.group_v), n_closed, round_a=round_table)
+            seeded = True
+        else:
+            # (1) routing summaries of the chunk-parallel path
+            ck, gk, _ = ops.summaries(hp, k_raw, k_rope, v, cos_t, sin_t, round_table=round_table, with_group_v=False)
+            seeded = False
         # (2) two-level routing
         routing = ops.route_prefill(hp, q, ck, gk)
         if populate_store:
-            self._seed_store(layer, hp, k_rope, k_raw, v, S)
+            self._seed_store(layer, hp, k_rope, k_raw, v, S, summaries_done=seeded)
         return RoutedKV(params=hp, seq_len=S, token_k=k_rope, token_v=v, routing=routing, scale=cfg.scale,
                         chunked=True, chunk_size=C, out=out)
 
@@ -256,15 +267,16 @@ class ChunkRouter:
             store.after_seed(layer, S, row=b)
         store.mark_closed(layer, min(seq_lens) // C)
 
-    def _seed_store(self, layer, hp, k_rope, k_raw, v, S):
+    def _seed_store(self, layer, hp, k_rope, k_raw, v, S, summaries_done: bool = False):
         """Store seed of a fresh prefill (chunk_router.py:553-599): summaries of the closed chunks with
-        fixed anchors and fp32 rotary rows, token rows, and the partial active chunk."""
+        fixed anchors and fp32 rotary rows (unless ``summaries_done``: written by hga_summaries_dual),
+        token rows, and the partial active chunk."""
         self._rot_stage_ready()
         cfg, store = self.cfg, self.store
         C = cfg.chunk_size
         n_closed = S // C
         st = store.ensure_capacity(layer, max(n_closed, 1), S)
-        if n_closed:
+        if n_closed and not summaries_done:
             cos32, sin32 = self._rotary(k_raw.device, S)
             ops.summaries(hp, k_raw, k_rope, v, cos32, sin32, seq_len=n_closed * C,
                           out=(st.chunk_k, st.group_k, st.group_v), out_chunk0=0)

@@ -65,6 +65,20 @@ int hga_summaries(const hga_params* p, int64_t seq_len, int64_t pos0,
                   void* chunk_k, void* group_k, void* group_v, int64_t sum_cap, int64_t out_chunk0,
                   cudaStream_t stream);
 
+/* Both summary sets of a fresh prefill from one read of K/V (bf16/fp16, head_dim 64/128, chunk and
+ * group sizes multiples of 16; HGA_E_UNSUPPORTED otherwise).  Set A = hga_summaries of all
+ * N = ceil(seq_len / chunk_size) chunks with fp32 table A (entries rounded to the model dtype
+ * first when round_a != 0: the chunk-parallel path's cos.to(dtype), vectorized.py:265-287) into
+ * chunk_a / group_a (capacity sum_cap_a, from slot out_a0).  Set B = the store seed of the first
+ * n_b closed chunks with fp32 table B (chunk_router.py:553-599, fixed anchors) into chunk_b /
+ * group_b / group_vb (group_vb may be NULL).  Each set equals the corresponding hga_summaries call
+ * bit for bit; the K/V rows are read once instead of twice. */
+int hga_summaries_dual(const hga_params* p, int64_t seq_len, int64_t pos0, const void* k_raw, const void* k_rope,
+                       const void* v, int64_t kv_cap, const float* cos_a, const float* sin_a, int64_t rot_row0_a,
+                       int32_t round_a, void* chunk_a, void* group_a, int64_t sum_cap_a, int64_t out_a0,
+                       const float* cos_b, const float* sin_b, int64_t rot_row0_b, int64_t n_b, void* chunk_b,
+                       void* group_b, void* group_vb, int64_t sum_cap_b, int64_t out_b0, cudaStream_t stream);
+
 /* (2) Two-level router of the chunk-parallel prefill (vectorized.py:296-384).
  * For every (b, h, query chunk n) writes the selected routed chunks and the opened groups that
  * some query row can see, each with t0 = first query row (0..chunk_size-1) of the chunk that sees

@@ -164,3 +164,29 @@ def test_router_empty_pool_and_ragged_tail(cuda):
     bad, _ = HC.check_replay(p, c["S"], res)
     assert not bad
     assert torch.isfinite(out.cpu()).all()
+
+
+@pytest.mark.parametrize("dtype,dh,S", [(torch.bfloat16, 128, 1000), (torch.bfloat16, 64, 257), (torch.float16, 128, 640)])
+def test_summaries_dual_equals_two_single_calls(cuda, dtype, dh, S):
+    """hga_summaries_dual (one read of K/V) writes the routing set and the store seed bit-identical
+    to the two hga_summaries calls it replaces, ragged last chunk included."""
+    from hierarchicalglobalattention_b200 import _lib, ops
+    g = torch.Generator().manual_seed(dh + S)
+    B, KVH, C, gs = 2, 2, 64, 16
+    k_raw, k_rope, v = (torch.randn(B, KVH, S, dh, generator=g).to(dtype).to(cuda) for _ in range(3))
+    hp = _lib.make_params(batch=B, nhead=4, kv_heads=KVH, head_dim=dh, chunk_size=C, group_size=gs, topk_chunks=4,
+                          topk_groups=8, keep_first=1, keep_last=2, theta=1e4, dtype=dtype)
+    cos_a, sin_a = (t.to(cuda) for t in O.module_rotary(1e4, dh, S))
+    cos_b, sin_b = (t.to(cuda) * (1 + 1e-3) for t in O.module_rotary(1e4, dh, S))   # a different table
+    n_b = S // C
+    cap = n_b + 3
+    ref_b = [torch.zeros(B, KVH, cap, dh, dtype=dtype, device=cuda), torch.zeros(B, KVH, cap, 4, dh, dtype=dtype, device=cuda),
+             torch.zeros(B, KVH, cap, 4, dh, dtype=dtype, device=cuda)]
+    got_b = [t.clone() for t in ref_b]
+    ck_a, gk_a, _ = ops.summaries(hp, k_raw, k_rope, v, cos_a, sin_a, round_table=True, with_group_v=False)
+    ops.summaries(hp, k_raw, k_rope, v, cos_b, sin_b, seq_len=n_b * C, out=tuple(ref_b), out_chunk0=0)
+    ck_d, gk_d = ops.summaries_dual(hp, k_raw, k_rope, v, cos_a, sin_a, cos_b, sin_b, tuple(got_b), n_b, round_a=True)
+    torch.cuda.synchronize()
+    assert torch.equal(ck_d, ck_a) and torch.equal(gk_d, gk_a)
+    for a, b in zip(got_b, ref_b):
+        assert torch.equal(a, b)
