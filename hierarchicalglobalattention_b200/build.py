@@ -8,7 +8,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libhga_b200.so")
-SOURCES = ["abi.cu", "prologue.cu", "summaries.cu", "route_prefill.cu", "attend_simt.cu", "attend_tc.cu", "route_tc.cu", "decode.cu", "decode_fast.cu", "shard.cu"]
+SOURCES = ["abi.cu", "prologue.cu", "summaries.cu", "route_prefill.cu", "attend_simt.cu", "attend_tc.cu", "route_tc.cu", "decode.cu", "decode_fast.cu", "shard.cu", "bank.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -17,6 +17,10 @@ cudaError_t launch_summaries_dual(const hga_params& p, int64_t S, int64_t pos0, 
                                   int64_t capA, int64_t outA0, const float* cosB, const float* sinB,
                                   int64_t rowB0, int nB, void* ckB, void* gkB, void* gvB, int64_t capB,
                                   int64_t outB0, cudaStream_t st);
+cudaError_t launch_bank_gather(const hga_params& p, const int32_t* open_gid, int Kg, const void* rec_k,
+                               const void* rec_v, int64_t rec_cap, void* bank_k, void* bank_v, int n_slots,
+                               int32_t* slot_gid, int32_t* gid_slot, int64_t gid_cap, int32_t* slot_stamp, int stamp,
+                               int32_t* open_slot, unsigned long long* counters, cudaStream_t st);
 cudaError_t launch_route_prefill(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout, const void* ck,
                                  const void* gk, int64_t sum_cap, int32_t* sel_chunk, int32_t* sel_t0,
                                  int32_t* open_gid, int32_t* open_t0, float* dbg1, float* dbg2, cudaStream_t st,
@@ -353,6 +357,27 @@ int hga_attend_decode_impl(const hga_params* p, int32_t L, const void* q, const 
   return cuda_status(hga::launch_attend_decode(*p, L, q, seq_pos, hot_k, hot_v, hot_cap, hot_mode, ck, cv, cold_cap,
                                                open_gid, open_t0, Kg, out, stream),
                      "hga_attend_decode");
+}
+
+int hga_gather_h2d(const hga_params* p, const int32_t* open_gid, int32_t Kg, const void* rec_k, const void* rec_v,
+                   int64_t rec_cap, void* bank_k, void* bank_v, int32_t n_slots, int32_t* slot_gid, int32_t* gid_slot,
+                   int64_t gid_cap, int32_t* slot_stamp, int32_t stamp, int32_t* open_slot,
+                   unsigned long long* counters, cudaStream_t stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (Kg <= 0) return HGA_OK;
+  if (!open_gid || !rec_k || !rec_v || !bank_k || !bank_v || !slot_gid || !gid_slot || !slot_stamp || !open_slot)
+    return fail(HGA_E_INVALID, "hga_gather_h2d: NULL pointer");
+  const int rep = p->nhead / p->kv_heads;
+  if (n_slots < rep * Kg) return fail(HGA_E_INVALID, "hga_gather_h2d: n_slots %d < (H/KVH) * Kg = %d", n_slots, rep * Kg);
+  if (gid_cap <= 0 || gid_cap > (1 << 20) || rec_cap < 0) return fail(HGA_E_INVALID, "hga_gather_h2d: gid_cap out of range");
+  if (stamp < 0) return fail(HGA_E_INVALID, "hga_gather_h2d: stamp must be >= 0");
+  if ((p->group_size * p->head_dim * (p->dtype == HGA_DTYPE_F32 ? 4 : 2)) % 16 ||
+      (((uintptr_t)rec_k | (uintptr_t)rec_v | (uintptr_t)bank_k | (uintptr_t)bank_v) & 15))
+    return fail(HGA_E_INVALID, "hga_gather_h2d: groups and buffers must be 16-byte aligned");
+  return cuda_status(hga::launch_bank_gather(*p, open_gid, Kg, rec_k, rec_v, rec_cap, bank_k, bank_v, n_slots, slot_gid,
+                                             gid_slot, gid_cap, slot_stamp, stamp, open_slot, counters, stream),
+                     "hga_gather_h2d");
 }
 
 int hga_append_tokens(const hga_params* p, int32_t L, const int32_t* seq_pos, const void* k_rope, const void* v,

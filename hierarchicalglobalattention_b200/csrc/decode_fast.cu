@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(kAttWarps * 32, (LM == 1 ? 2 : 1)) attend_deco
   windows(n_closed, kf, kl, f_hi, l_lo);
   const size_t bh = (size_t)b * H + h;
   const bool hot_oob = hot_mode == 0 ? (int64_t)(n_closed + 1) * C > hot_cap : (int64_t)(kf + kl + 1) * C > hot_cap;
-  if (hot_oob || (int64_t)n_closed * C > cold_cap) {
+  if (hot_oob || (hot_mode == 0 && (int64_t)n_closed * C > cold_cap)) {
     if (tid == 0) atomicCAS(&g_decode_fast_error, 0, kErrBoundsAttendDecode);
     for (int i = tid; i < L * DH; i += blockDim.x) out[bh * L * DH + i] = Num<T>::from_f(0.f);
     return;

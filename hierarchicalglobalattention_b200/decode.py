@@ -34,8 +34,14 @@ class DecodeContext:
         store = self.router.store
         hot_k, hot_v = store.hot_buffers(self.layer)
         cold_k, cold_v = store.cold_buffers(self.layer)
+        open_gid = self.routing["open_gid"]
+        banked = store.bank_gather(self.layer, self.params, open_gid) if hasattr(store, "bank_gather") else None
+        if banked is not None:
+            # the RAM tier's VRAM bank: this step's opened groups were made resident (misses copied
+            # from the pinned record); the attention reads them from HBM by bank slot
+            cold_k, cold_v, open_gid = banked
         out = ops.attend_decode(self.params, q, self.seq_pos, hot_k, hot_v, store.hot_mode, cold_k, cold_v,
-                                self.routing["open_gid"], self.routing["open_t0"])
+                                open_gid, self.routing["open_t0"])
         self.finish()
         return out
 
@@ -121,6 +127,8 @@ def decode_block(router, layer, q, k_rope, k_raw, v, start_pos):
         z = torch.empty(B, H, 0, device=q.device, dtype=torch.int32)
         routing = {"mid_chunk": z, "mid_t0": z, "open_gid": z, "open_t0": z}
     router._active_len[layer] = (c0 + L) % C
+    # chunk-summary lookups of this block (all HBM-resident: the summary bank spans the context)
+    store.summary_hits += B * H * routing["mid_chunk"].shape[-1]
     ctx = DecodeContext(router, layer, hp, seq_pos, routing, n if c0 + L == C else None)
     router._pending[layer] = ctx
     return RoutedKV(params=hp, seq_len=L, token_k=hot_k, token_v=hot_v, routing=routing, scale=cfg.scale,
@@ -154,6 +162,7 @@ def decode_step(router, layer, q, k_rope, k_raw, v, seq_pos: torch.Tensor, seq_p
     else:
         z = torch.empty(B, H, 0, device=q.device, dtype=torch.int32)
         routing = {"mid_chunk": z, "mid_t0": z, "open_gid": z, "open_t0": z}
+    store.summary_hits += B * H * routing["mid_chunk"].shape[-1]
     rows = [b for b, pos in enumerate(seq_pos_host) if pos % C + L == C]
     ctx = DecodeContext(router, layer, hp, seq_pos, routing, [seq_pos_host[b] // C for b in rows] if rows else None,
                         close_rows=rows if rows else None)

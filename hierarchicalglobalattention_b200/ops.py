@@ -301,6 +301,24 @@ def attend_decode(p: HgaParams, q: torch.Tensor, seq_pos: torch.Tensor, hot_k: t
     return out
 
 
+def gather_h2d(p: HgaParams, open_gid: torch.Tensor, rec_k: torch.Tensor, rec_v: torch.Tensor, bank_k: torch.Tensor,
+               bank_v: torch.Tensor, slot_gid: torch.Tensor, gid_slot: torch.Tensor, slot_stamp: torch.Tensor,
+               stamp: int, counters: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One step of the RAM tier's VRAM token bank (see hga_gather_h2d).  open_gid [B,H,Kg] int32;
+    rec_* [B,KVH,rec_cap,Dh] (pinned host or device); bank_* [B,KVH,slots*group_size,Dh]; maps as
+    documented in the header; counters int64 [2] (hits, misses) or None.  Returns open_slot
+    [B,H,Kg] (bank slots of the entries, -1 padding)."""
+    _require_cuda(open_gid, bank_k, bank_v, slot_gid, gid_slot, slot_stamp)
+    B, H, Kg = open_gid.shape
+    open_gid = open_gid.contiguous()
+    out = torch.empty_like(open_gid)
+    check(lib().hga_gather_h2d(ctypes_params(p), ptr(open_gid), Kg, ptr(rec_k), ptr(rec_v), kv_cap_of(rec_k), ptr(bank_k),
+                               ptr(bank_v), slot_gid.shape[2], ptr(slot_gid), ptr(gid_slot), gid_slot.shape[2],
+                               ptr(slot_stamp), int(stamp), ptr(out), ptr(counters), stream_ptr(open_gid.device)),
+          "hga_gather_h2d")
+    return out
+
+
 def append_tokens(p: HgaParams, seq_pos: torch.Tensor, k_rope: torch.Tensor, v: torch.Tensor,
                   k_raw: Optional[torch.Tensor], hot_k: torch.Tensor, hot_v: torch.Tensor, hot_mode: int,
                   cold_k: Optional[torch.Tensor], cold_v: Optional[torch.Tensor],

@@ -12,15 +12,31 @@ Layout differences that the B200 kernels rely on:
 * chunk and group summaries of every closed chunk stay in HBM (the reference's summary bank
   sized to span the whole context).
 
-The reference's VRAM LRU token bank (``vram_cache_chunks``) and its hit/miss counters are kept as
-attributes for interface compatibility; the zero-copy cold path does not use a bank.
+VRAM token bank (``vram_cache_chunks`` > 0, the reference's bounded LRU bank,
+ram_kv_cache_store.py:266-317): per layer and per (sequence, KV head) an HBM cache of 16-token
+groups of the record with device-side slot maps.  Each decode step, ``hga_gather_h2d`` takes the
+union of the groups a KV head's query heads opened, copies only the groups not in the bank (exact
+LRU replacement) from the pinned record, and the attention reads the opened groups from the bank.
+``vram_cache_chunks`` is an upper bound in chunks per layer (times groups_per_chunk slots per
+sequence and KV head); like the reference the bank is sized down to the free device memory left
+after ``vram_cache_reserve_gb`` (shared over ``num_layers``), and it is bypassed (groups read in
+place from the pinned record) when it cannot hold one step's opened groups.  ``cache_hits`` /
+``cache_misses`` count groups per (sequence, KV head) — the reference counts whole chunks per
+batch.  Chunk and group summaries of every closed chunk are in HBM (the reference's summary bank
+spanning the whole context): every summary lookup is a hit.
+
+``pin_memory=False`` (the reference Qwen patch's default) is accepted: the decode kernels read the
+record from device code, which needs page-locked memory, so the record is pinned regardless and a
+warning says so.
 """
 from __future__ import annotations
 
-from typing import Optional
+import warnings
+from typing import Dict, Optional
 
 import torch
 
+from . import ops
 from .store import VramKVCacheStore
 
 
@@ -38,9 +54,10 @@ class RamKVCacheStore(VramKVCacheStore):
         super().__init__(compute_device=compute_device, policy=policy, kv_heads=kv_heads, head_dim=head_dim,
                          chunk_size=chunk_size, groups_per_chunk=groups_per_chunk, batch_size=batch_size,
                          dtype=dtype, initial_capacity=initial_capacity)
-        self.pin_memory = bool(pin_memory)
-        if not self.pin_memory:
-            raise ValueError("the B200 RAM tier reads the cold record from device code: pin_memory must be True")
+        self.pin_memory = True
+        if not pin_memory:
+            warnings.warn("RamKVCacheStore(pin_memory=False): the B200 decode kernels read the cold record from "
+                          "device code, so it is allocated in page-locked memory anyway", stacklevel=2)
         self.vram_cache_chunks = int(vram_cache_chunks)
         self.vram_summary_chunks = int(vram_summary_chunks)
         self.num_layers = int(num_layers)
@@ -49,6 +66,93 @@ class RamKVCacheStore(VramKVCacheStore):
         self.kl = max(0, int(policy.keep_last))
         if self.kf + self.kl > 4096:
             raise ValueError("keep_first + keep_last windows larger than 4096 chunks belong in the VRAM tier")
+        self._bank: Dict[int, dict] = {}
+        self._bank_slots: Optional[int] = None            # resolved slots per (sequence, KV head)
+        self._counters = torch.zeros(2, dtype=torch.int64, device=self.compute_device)   # hits, misses
+        self._hits0 = self._misses0 = 0
+
+    # -- counters (device-side for the bank, read on access) ------------------------------------
+    @property
+    def cache_hits(self) -> int:
+        return self._hits0 + (int(self._counters[0].item()) if hasattr(self, "_counters") else 0)
+
+    @cache_hits.setter
+    def cache_hits(self, v: int) -> None:
+        self._hits0 = int(v)
+        if hasattr(self, "_counters"):
+            self._counters[0].zero_()
+
+    @property
+    def cache_misses(self) -> int:
+        return self._misses0 + (int(self._counters[1].item()) if hasattr(self, "_counters") else 0)
+
+    @cache_misses.setter
+    def cache_misses(self, v: int) -> None:
+        self._misses0 = int(v)
+        if hasattr(self, "_counters"):
+            self._counters[1].zero_()
+
+    # -- VRAM token bank --------------------------------------------------------------------------
+    def _effective_slots(self) -> int:
+        """Bank slots per (sequence, KV head): vram_cache_chunks * M, reduced to what the free device
+        memory allows after vram_cache_reserve_gb, shared by num_layers layers (the reference's
+        _effective_cap)."""
+        if self._bank_slots is None:
+            want = self.vram_cache_chunks * self.M
+            if want > 0 and self.compute_device.type == "cuda":
+                free, _ = torch.cuda.mem_get_info(self.compute_device)
+                budget = free - self.vram_cache_reserve_gb * (1 << 30)
+                per_slot = self.B * self.kvh * (self.C // self.M) * self.dh * 2 * self._elt() + self.B * self.kvh * 8
+                fit = int(max(0, budget) // max(1, self.num_layers) // per_slot)
+                want = min(want, fit)
+            self._bank_slots = max(0, want)
+        return self._bank_slots
+
+    def _elt(self) -> int:
+        return torch.empty((), dtype=self.dtype).element_size()
+
+    def reset(self) -> None:
+        self._bank.clear()
+        super().reset()
+
+    def bank_for(self, layer: int, need_slots: int) -> Optional[dict]:
+        """The layer's bank (allocated on first use), or None when banking is off or the bank cannot
+        hold ``need_slots`` groups per (sequence, KV head)."""
+        slots = self._effective_slots()
+        if slots <= 0 or slots < need_slots:
+            return None
+        st = self.layer_buffers(layer)
+        gs = self.C // self.M
+        gid_cap = st.tcap // gs
+        bk = self._bank.get(layer)
+        dev = self.compute_device
+        if bk is None:
+            bk = {"k": torch.zeros(self.B, self.kvh, slots * gs, self.dh, device=dev, dtype=self.dtype),
+                  "v": torch.zeros(self.B, self.kvh, slots * gs, self.dh, device=dev, dtype=self.dtype),
+                  "slot_gid": torch.full((self.B, self.kvh, slots), -1, dtype=torch.int32, device=dev),
+                  "slot_stamp": torch.full((self.B, self.kvh, slots), -1, dtype=torch.int32, device=dev),
+                  "gid_slot": torch.full((self.B, self.kvh, gid_cap), -1, dtype=torch.int32, device=dev),
+                  "slots": slots, "stamp": 0}
+            self._bank[layer] = bk
+        elif bk["gid_slot"].shape[2] < gid_cap:
+            # the record grew (capacity doubling): extend the gid -> slot map, keep the bank
+            g = torch.full((self.B, self.kvh, gid_cap), -1, dtype=torch.int32, device=dev)
+            g[:, :, :bk["gid_slot"].shape[2]] = bk["gid_slot"]
+            bk["gid_slot"] = g
+        return bk
+
+    def bank_gather(self, layer: int, hp, open_gid: torch.Tensor):
+        """One decode step's hga_gather_h2d: returns (bank_k, bank_v, open_slot) for the attention,
+        or None (no bank: the attention reads the pinned record in place)."""
+        H, Kg = open_gid.shape[1], open_gid.shape[2]
+        bk = self.bank_for(layer, (H // self.kvh) * Kg)
+        if bk is None or Kg == 0:
+            return None
+        st = self.layer_buffers(layer)
+        open_slot = ops.gather_h2d(hp, open_gid, st.token_k, st.token_v, bk["k"], bk["v"], bk["slot_gid"],
+                                   bk["gid_slot"], bk["slot_stamp"], bk["stamp"], self._counters)
+        bk["stamp"] += 1
+        return bk["k"], bk["v"], open_slot
 
     # -- buffers -----------------------------------------------------------------------------
     def _token_tensor(self, rows: int) -> torch.Tensor:

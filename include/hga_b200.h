@@ -169,7 +169,8 @@ int hga_route_decode(const hga_params* p, int32_t L, const void* q, const int32_
  * flat branch of RoutedKV.attend, :159-162) over the keep_first window, the keep_last window, the
  * opened groups (rows >= t0) and the active chunk (key u visible to row t iff u <= pos%C + t).
  * Window and active-chunk rows come from `hot`, opened groups from `cold` (the complete token
- * record; may be mapped pinned host memory).  hot_mode 0: hot is addressed like cold (the VRAM
+ * record, may be mapped pinned host memory; with hot_mode 1 any buffer that open_gid indexes by
+ * 16-row group, e.g. the VRAM bank of hga_gather_h2d with its open_slot list).  hot_mode 0: hot is addressed like cold (the VRAM
  * tier, hot == cold); hot_mode 1: hot is a slot buffer [B,KVH,(kf+kl+1)*C,Dh] holding first-window
  * chunk c in slot c, last-window chunk c in slot kf + c % kl and the active chunk in slot kf + kl.
  * out [B, H, L, Dh]. */
@@ -192,6 +193,26 @@ int hga_attend_decode_impl(const hga_params* p, int32_t L, const void* q, const 
                            const void* cold_k, const void* cold_v, int64_t cold_cap,
                            const int32_t* open_gid, const int32_t* open_t0, int32_t Kg, void* out,
                            int32_t impl, cudaStream_t stream);
+
+/* hga_gather_h2d: the RAM tier's VRAM token bank, one launch per decode step (the bounded LRU
+ * bank of ram_kv_cache_store.py:266-317, its gathers :547-607 and the KV-head union dedup of
+ * gather_chunk_tokens_kvh :397-438).  Per (sequence, KV head): the opened groups of the KV head's
+ * query heads (open_gid [B,H,Kg], -1 padded) are de-duplicated; groups already in the bank are
+ * stamped `stamp` (hits); the others (misses) replace the least recently used slots (smallest
+ * stamp, then lowest slot; never a slot stamped by this call) and their 16 token rows of K and V are
+ * copied from the record rec_k / rec_v [B,KVH,rec_cap,Dh] (pinned host memory read over the host
+ * link, or device memory) into bank_k / bank_v [B,KVH,n_slots*group_size,Dh].  Device maps:
+ * slot_gid [B,KVH,n_slots] (-1 = empty), gid_slot [B,KVH,gid_cap] (-1 = absent), slot_stamp
+ * [B,KVH,n_slots] (-1 = never used), all owned by the caller and initialised to -1.  open_slot
+ * [B,H,Kg] receives each entry's bank slot (-1 for padding), so hga_attend_decode can read the
+ * opened groups from the bank (cold = bank, cold_cap = n_slots*group_size, open_gid = open_slot).
+ * counters (may be NULL): [0] += unique groups found in the bank, [1] += groups copied.  Requires
+ * n_slots >= (H/KVH) * Kg.  Runs on `stream` (a side stream of the caller's choosing, ordered by
+ * the caller after the routing and before the attention). */
+int hga_gather_h2d(const hga_params* p, const int32_t* open_gid, int32_t Kg, const void* rec_k, const void* rec_v,
+                   int64_t rec_cap, void* bank_k, void* bank_v, int32_t n_slots, int32_t* slot_gid, int32_t* gid_slot,
+                   int64_t gid_cap, int32_t* slot_stamp, int32_t stamp, int32_t* open_slot,
+                   unsigned long long* counters, cudaStream_t stream);
 
 /* hga_append_tokens: write L new K (RoPE applied) / V rows per sequence at seq_pos into the hot
  * rows (and, for hot_mode 1, the cold record), and their pre-RoPE K into active_raw
