@@ -442,13 +442,19 @@ def decode_bench(device, steps: int = 64, warmup: int = 8):
     del hbuf, dbuf
     B16 = B
     # the config's batch in both tiers, then one sequence (VRAM tier), where a step is launch-bound
-    for tier, B in (("ram", B16), ("vram", B16), ("vram_b1", 1)):
+    # ram_bank / ram_bank_full: the RAM tier with its VRAM token bank of 256 chunks (the reference
+    # Qwen patch's default vram_cache_chunks) or of the whole context; hit rate over the timed steps
+    for tier, B in (("ram", B16), ("ram_bank", B16), ("ram_bank_full", B16), ("vram", B16), ("vram_b1", 1)):
         cfg = RouterConfig(nhead=H, kv_heads=KVH, head_dim=Dh, chunk_size=C, group_size=gs,
                            topk_chunks=c["topk_chunks"], topk_groups=c["topk_groups"], theta=c["theta"])
         pol = ChunkPlacementPolicy(keep_first=c["keep_first"], keep_last=c["keep_last"], first_token_level=True)
-        cls = RamKVCacheStore if tier == "ram" else VramKVCacheStore
-        store = cls(compute_device=device, policy=pol, kv_heads=KVH, head_dim=Dh, chunk_size=C,
-                    groups_per_chunk=C // gs, batch_size=B, dtype=dt, initial_capacity=(S + 4 * C) // C)
+        kw = dict(compute_device=device, policy=pol, kv_heads=KVH, head_dim=Dh, chunk_size=C,
+                  groups_per_chunk=C // gs, batch_size=B, dtype=dt, initial_capacity=(S + 4 * C) // C)
+        if tier.startswith("ram"):
+            bank = {"ram": 0, "ram_bank": 256, "ram_bank_full": S // C + 8}[tier]
+            store = RamKVCacheStore(vram_cache_chunks=bank, num_layers=1, vram_cache_reserve_gb=8.0, **kw)
+        else:
+            store = VramKVCacheStore(**kw)
         router = ChunkRouter(cfg, store)
         k_raw = torch.randn(B, KVH, S, Dh, device=device, dtype=dt, generator=g)
         v = torch.randn(B, KVH, S, Dh, device=device, dtype=dt, generator=g)
@@ -465,9 +471,12 @@ def decode_bench(device, steps: int = 64, warmup: int = 8):
         torch.cuda.synchronize()
         pos = S
         vis_groups = 0
+        h0 = m0 = 0
         for i in range(n):
             if i == warmup:
                 torch.cuda.synchronize()
+                if tier.startswith("ram_bank"):
+                    h0, m0 = store.cache_hits, store.cache_misses
                 t_wall = time.perf_counter()
                 e0.record()
             rk = router.decode_block(0, qs[i], ks[i], ks[i], ks[i], pos)
@@ -484,6 +493,15 @@ def decode_bench(device, steps: int = 64, warmup: int = 8):
         summ = B * KVH * (S // C) * Dh * 2 + B * H * c["topk_chunks"] * (C // gs) * Dh * 2
         res[tier] = {"us_per_layer_step": us, "wall_us_per_step": wall_us, "cold_bytes_per_step": cold,
                      "hbm_bytes_per_step": hot + summ + (0 if tier == "ram" else cold)}
+        if tier.startswith("ram_bank"):
+            hits, misses = store.cache_hits - h0, store.cache_misses - m0
+            res[tier].update({"bank_slots_per_seq_kv_head": store._effective_slots(),
+                              "hit_rate": hits / max(1, hits + misses),
+                              "host_link_bytes_per_step": misses * gs * Dh * 2 * 2 // steps,
+                              "unique_groups_per_step": (hits + misses) / steps})
+            del router, store
+            torch.cuda.empty_cache()
+            continue
         # the same steps replayed from a CUDA graph (DecodeStepGraph), continuing the sequences
         from hierarchicalglobalattention_b200.decode_graph import DecodeStepGraph
         graph = DecodeStepGraph(router, [0], [pos] * B, capacity_tokens=pos + n + 1, dtype=dt)
