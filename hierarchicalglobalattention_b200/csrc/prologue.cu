@@ -182,6 +182,109 @@ __global__ void __launch_bounds__(kProWarps * 32) prologue_vec_kernel(
   if (dst_raw) st_vec<T, EPL>(dst_raw, xo);
 }
 
+// One warp per token (batch b, position t): the token's H query rows and KVH key rows get the
+// same arithmetic as prologue_vec_kernel (lane = EPL contiguous elements, RoPE partner by
+// shuffle), but the rotary table entries of the position are read once per token (they depend on
+// the position and the column only) instead of once per head row, four rows' loads are issued
+// before any of them is used, and the row index needs no 64-bit division.  V rows are copied.
+template <typename T, int EPL>
+__global__ void __launch_bounds__(kProWarps * 32) prologue_tok_kernel(
+    hga_params p, int64_t S, const T* __restrict__ qkv, int64_t row_stride, const T* __restrict__ qw,
+    const T* __restrict__ kw, float eps, int norm_mode, const void* __restrict__ cos_t,
+    const void* __restrict__ sin_t, int rope_mode, int64_t rot_row0, int64_t pos0, T* __restrict__ q_out,
+    T* __restrict__ kraw_out, T* __restrict__ krope_out, T* __restrict__ v_out, int64_t kv_cap, int64_t kv_row0) {
+  constexpr int Dh = 32 * EPL;
+  constexpr int UNR = 4;
+  const int H = p.nhead, KVH = p.kv_heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t bt = (int64_t)blockIdx.x * kProWarps + warp;  // b * S + t
+  if (bt >= (int64_t)p.batch * S) return;
+  const int b = (int)(bt / S);
+  const int64_t t = bt - (int64_t)b * S;
+  const int d0 = lane * EPL;
+  const T* src = qkv + bt * row_stride + d0;
+  // the position's rotary entries of this lane's columns
+  float cs[EPL], sn[EPL];
+  const int64_t rr = (pos0 + t - rot_row0) * Dh + d0;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    if (rope_mode == 0) {
+      cs[e] = ((const float*)cos_t)[rr + e];
+      sn[e] = ((const float*)sin_t)[rr + e];
+    } else {
+      cs[e] = Num<T>::to_f(((const T*)cos_t)[rr + e]);
+      sn[e] = Num<T>::to_f(((const T*)sin_t)[rr + e]);
+    }
+  }
+  float wq[EPL], wk[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    wq[e] = qw ? Num<T>::to_f(qw[d0 + e]) : 1.f;
+    wk[e] = kw ? Num<T>::to_f(kw[d0 + e]) : 1.f;
+  }
+  const int nqk = H + KVH;
+  for (int r0 = 0; r0 < nqk; r0 += UNR) {
+    T xin[UNR][EPL];
+#pragma unroll
+    for (int u = 0; u < UNR; ++u)
+      if (r0 + u < nqk) ld_vec<T, EPL>(src + (int64_t)(r0 + u) * Dh, xin[u]);
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const int r = r0 + u;
+      if (r >= nqk) break;  // warp-uniform
+      const bool is_q = r < H;
+      const int kvh = is_q ? 0 : r - H;
+      float x[EPL];
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        x[e] = Num<T>::to_f(xin[u][e]);
+        ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
+      }
+      if (is_q ? qw != nullptr : kw != nullptr) {
+        for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        const float mean = __fdiv_rn(ss, (float)Dh);
+        const float rs = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, eps)));
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          const float wf = is_q ? wq[e] : wk[e];
+          x[e] = norm_mode == 0 ? Num<T>::round(__fmul_rn(__fmul_rn(wf, x[e]), rs))
+                                : Num<T>::round(__fmul_rn(wf, Num<T>::round(__fmul_rn(x[e], rs))));
+        }
+      }
+      T yo[EPL], xo[EPL];
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
+        const float xp = lane < 16 ? -other : other;
+        float y;
+        if (rope_mode == 0) y = __fadd_rn(__fmul_rn(x[e], cs[e]), __fmul_rn(xp, sn[e]));
+        else y = __fadd_rn(Num<T>::round(__fmul_rn(x[e], cs[e])), Num<T>::round(__fmul_rn(xp, sn[e])));
+        yo[e] = Num<T>::from_f(y);
+        xo[e] = Num<T>::from_f(x[e]);
+      }
+      if (is_q) {
+        st_vec<T, EPL>(q_out + (bt * H + r) * Dh + d0, yo);
+      } else {
+        const int64_t kr = (((int64_t)b * KVH + kvh) * kv_cap + kv_row0 + t) * Dh + d0;
+        st_vec<T, EPL>(krope_out + kr, yo);
+        st_vec<T, EPL>(kraw_out + kr, xo);
+      }
+    }
+  }
+  // V rows: layout transform only, all loads first
+  T vin[8][EPL];
+  for (int v0 = 0; v0 < KVH; v0 += 8) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (v0 + u < KVH) ld_vec<T, EPL>(src + (int64_t)(nqk + v0 + u) * Dh, vin[u]);
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (v0 + u < KVH)
+        st_vec<T, EPL>(v_out + (((int64_t)b * KVH + v0 + u) * kv_cap + kv_row0 + t) * Dh + d0, vin[u]);
+  }
+}
+
 cudaError_t launch_prologue(const hga_params& p, int64_t S, const void* qkv, int64_t row_stride, const void* qw,
                             const void* kw, float eps, int norm_mode, const void* cos, const void* sin,
                             int rope_mode, int64_t rot_row0, int64_t pos0, void* q_out, void* kraw_out,
@@ -189,8 +292,9 @@ cudaError_t launch_prologue(const hga_params& p, int64_t S, const void* qkv, int
   const int64_t rows = (int64_t)p.batch * S * (p.nhead + 2 * p.kv_heads);
   const int64_t blocks = (rows + kProWarps - 1) / kProWarps;
   const size_t smem = (size_t)kProWarps * p.head_dim * sizeof(float);
+  const int64_t tok_blocks = ((int64_t)p.batch * S + kProWarps - 1) / kProWarps;
 #define HGA_PRO_VEC(T, EPL)                                                                                     \
-  prologue_vec_kernel<T, EPL><<<(unsigned)blocks, kProWarps * 32, 0, st>>>(                                    \
+  prologue_tok_kernel<T, EPL><<<(unsigned)tok_blocks, kProWarps * 32, 0, st>>>(                                \
       p, S, (const T*)qkv, row_stride, (const T*)qw, (const T*)kw, eps, norm_mode, cos, sin, rope_mode, rot_row0, \
       pos0, (T*)q_out, (T*)kraw_out, (T*)krope_out, (T*)v_out, kv_cap, kv_row0);                                \
   return cudaGetLastError();
