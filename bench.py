@@ -525,52 +525,74 @@ def decode_bench(device, steps: int = 64, warmup: int = 8):
     return res
 
 
-def decode_mixed_bench(device, layers: int = 2, batch: int = 8, steps: int = 32, warmup: int = 4):
-    """configs[4] on one GPU (its per-GPU share, scaled): `batch` sequences whose lengths are drawn
-    uniformly from {8192, 8256, ..., 131072}, cold K/V in pinned host memory, configs[0] routing,
-    `layers` attention layers per step through ChunkRouter.decode_step (per-sequence positions).
-    The 8-GPU config runs 8 such shares with no collective."""
+def decode_mixed_bench(device, layers: int = 2, batch: int = 8, steps: int = 32, warmup: int = 4, rank: int = 0,
+                       world: int = 1):
+    """sequences whose lengths are drawn uniformly from {8192, 8256, ..., 131072} (the
+    first ``batch * world`` of the config's 64), cold K/V in pinned host memory, configs[0] routing,
+    ``layers`` attention layers per step through ChunkRouter.decode_step (per-sequence positions).
+    The sequences are split over the ``world`` ranks by ShardedDecode (contiguous ranges balanced by
+    context length, no collective); each rank times its own steps and the slowest rank sets the
+    aggregate tokens/s (one token per sequence per step)."""
     from hierarchicalglobalattention_b200 import ChunkPlacementPolicy, ChunkRouter, RouterConfig
+    from hierarchicalglobalattention_b200.decode_shard import ShardedDecode
     from hierarchicalglobalattention_b200.store_ram import RamKVCacheStore
     H, KVH, Dh, C = 32, 4, 128, 64
     dt = torch.bfloat16
     g = torch.Generator(device="cpu").manual_seed(4)
-    lens = [int(x) * 64 for x in torch.randint(8192 // 64, 131072 // 64 + 1, (batch,), generator=g)]
+    all_lens = [int(x) * 64 for x in torch.randint(8192 // 64, 131072 // 64 + 1, (64,), generator=g)]
+    gb = min(64, batch * world)
+    glens = all_lens[:gb]
     cfg = RouterConfig(nhead=H, kv_heads=KVH, head_dim=Dh, chunk_size=C, group_size=16, topk_chunks=16,
                        topk_groups=64, theta=1e6)
     pol = ChunkPlacementPolicy(keep_first=2, keep_last=8, first_token_level=True)
-    store = RamKVCacheStore(compute_device=device, policy=pol, kv_heads=KVH, head_dim=Dh, chunk_size=C,
-                            groups_per_chunk=4, batch_size=batch, dtype=dt,
-                            initial_capacity=(max(lens) + (steps + warmup + 2) * 1) // C + 2)
-    router = ChunkRouter(cfg, store)
-    gd = torch.Generator(device=device).manual_seed(5)
+
+    def make_router(nb):
+        # the reference Qwen patch's default VRAM token bank (256 chunks per layer), budgeted for
+        # the config's 48 layers
+        store = RamKVCacheStore(compute_device=device, policy=pol, kv_heads=KVH, head_dim=Dh, chunk_size=C,
+                                groups_per_chunk=4, batch_size=nb, dtype=dt, vram_cache_chunks=256, num_layers=48,
+                                initial_capacity=(max(glens) + steps + warmup + 2) // C + 2)
+        return ChunkRouter(cfg, store)
+
+    sd = ShardedDecode(world, rank, gb, make_router, device=device, weights=glens)
+    lens = glens[sd.lo:sd.hi]
+    nb = len(lens)
+    gd = torch.Generator(device=device).manual_seed(5 + rank)
     Smax = max(lens)
     for layer in range(layers):
-        k = torch.randn(batch, KVH, Smax, Dh, device=device, dtype=dt, generator=gd)
-        router.seed_mixed(layer, k, k, k, lens)
+        k = torch.randn(nb, KVH, Smax, Dh, device=device, dtype=dt, generator=gd)
+        sd.seed(layer, k, k, k, lens, local=True)
         del k
     torch.cuda.synchronize()
     n = warmup + steps
-    qs = torch.randn(n, batch, H, 1, Dh, device=device, dtype=dt, generator=gd)
-    ks = torch.randn(n, batch, KVH, 1, Dh, device=device, dtype=dt, generator=gd)
+    qs = torch.randn(n, nb, H, 1, Dh, device=device, dtype=dt, generator=gd)
+    ks = torch.randn(n, nb, KVH, 1, Dh, device=device, dtype=dt, generator=gd)
     pos = list(lens)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for i in range(n):
         if i == warmup:
             torch.cuda.synchronize()
+            if world > 1:
+                torch.distributed.barrier()
+            torch.cuda.synchronize()
             e0.record()
-        seq = torch.tensor(pos, dtype=torch.int32, device=device)
         for layer in range(layers):
-            rk = router.decode_step(layer, qs[i], ks[i], ks[i], ks[i], seq, pos)
-            rk.attend(qs[i])
+            sd.decode_step(layer, qs[i], ks[i], ks[i], ks[i], pos, local=True)
         pos = [p_ + 1 for p_ in pos]
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
-    return {"workload": f"configs[4] per-GPU share: {batch} sequences, lengths {min(lens)}-{max(lens)} "
-                        f"(uniform in 8192..131072 step 64), {layers} layers, cold K/V in pinned host memory",
-            "us_per_layer_step": ms * 1e3 / layers, "tokens_per_s": batch / (ms / 1e3), "layers": layers,
-            "batch": batch}
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    del sd
+    torch.cuda.empty_cache()
+    return {"workload": f"configs[4]: {gb} sequences over {world} GPU(s) ({batch} per GPU), lengths "
+                        f"{min(glens)}-{max(glens)} (uniform in 8192..131072 step 64), {layers} of the 48 layers, "
+                        f"cold K/V in pinned host memory behind a 256-chunk VRAM token bank per layer, no collective",
+            "us_per_layer_step": ms * 1e3 / layers, "tokens_per_s": gb / (ms / 1e3), "layers": layers,
+            "batch": gb, "n_gpus": world, "scaling": "weak"}
 
 
 CFG0 = dict(d_model=512, nhead=8, kv_heads=2, head_dim=64, theta=1e4, chunk_size=64, group_size=16, keep_first=2,
@@ -760,6 +782,10 @@ def main():
         r = run_sharded(args, rank, world, device)
         st3 = min(args.steps, 5)
         r3 = run_sharded(args, rank, world, device, S=SEQ3, cfg=CFG3, steps=st3, warmup=2)
+        try:
+            dmix = decode_mixed_bench(device, rank=rank, world=world)
+        except Exception as e:  # keep the prefill line
+            dmix = {"error": str(e)[:300]}
         if rank == 0:
             tokens = args.seq * args.steps
             config["parallelism"] = f"shard{world}: query chunks in zigzag blocks, NCCL all-gather of summaries then K/V"
@@ -775,7 +801,8 @@ def main():
                 "gpu_launches": r["launches_per_step"] * args.steps,
                 "cfg3": {"workload": f"configs[3]: S=131072, topk 32/128, sharded over {world} GPUs (strong scaling)",
                          "unit": "tokens/s", "value": SEQ3 * st3 / (r3["dev_ms"] / 1e3),
-                         "ms_per_step": r3["dev_ms"] / st3, "e2e_tokens_per_s": SEQ3 * st3 / (r3["e2e_ms"] / 1e3)}}))
+                         "ms_per_step": r3["dev_ms"] / st3, "e2e_tokens_per_s": SEQ3 * st3 / (r3["e2e_ms"] / 1e3)},
+                "decode_mixed": dmix}))
         torch.distributed.destroy_process_group()
         return
     r = run_ours(args, rank, world, device)

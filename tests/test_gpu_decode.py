@@ -317,3 +317,33 @@ def test_pool_above_nmid_max_is_reported_by_both_routers(cuda):
     for k in outs[0]:
         assert torch.equal(outs[0][k], outs[1][k]), k
         assert bool((outs[0][k] == -1).all()), k
+
+
+@pytest.mark.parametrize("tier", TIERS)
+def test_sharded_decode_ranks_equal_one_batched_run(cuda, tier):
+    """ShardedDecode: the ranks' sequence ranges (emulated here as two instances in one process:
+    no kernel waits on another rank) reproduce the whole batch's decode bit for bit."""
+    from hierarchicalglobalattention_b200.decode_shard import ShardedDecode
+    c, inp = _synthetic(DECODE_SHAPES[0], seed=9)
+    p = c["params"]
+    q, kr, kraw, v = (inp[k][0].to(cuda) for k in ("q", "k_rope", "k_raw", "v"))
+    starts = [700, 1023, 1290, 900, 1500]
+    B = len(starts)
+    Smax = max(starts)
+    pre = {"k_rope": kr, "k_raw": kraw, "v": v}
+    full = {k: pre[k][None, :, :Smax].expand(B, -1, -1, -1).contiguous() for k in pre}
+    routers = [ShardedDecode(1, 0, B, lambda nb: _router(p, nb, c["dtype"], cuda, tier), bind_numa=False)]
+    routers += [ShardedDecode(2, r, B, lambda nb: _router(p, nb, c["dtype"], cuda, tier), bind_numa=False,
+                              weights=starts) for r in range(2)]
+    for sd in routers:
+        sd.seed(0, full["k_rope"], full["k_raw"], full["v"], starts)
+    pos = list(starts)
+    for _ in range(70):
+        idx = torch.tensor(pos, device=cuda)
+        qb = q[:, idx].permute(1, 0, 2).unsqueeze(2).contiguous()
+        kb = kr[:, idx].permute(1, 0, 2).unsqueeze(2).contiguous()
+        krb = kraw[:, idx].permute(1, 0, 2).unsqueeze(2).contiguous()
+        vb = v[:, idx].permute(1, 0, 2).unsqueeze(2).contiguous()
+        outs = [sd.decode_step(0, qb, kb, krb, vb, pos) for sd in routers]
+        assert torch.equal(torch.cat(outs[1:], 0), outs[0])
+        pos = [x + 1 for x in pos]
