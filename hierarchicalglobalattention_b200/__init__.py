@@ -6,7 +6,7 @@ Drop-in for the reference's ``HierarchicalGlobalAttentionRouted`` module, its ``
 ABI of ``libhga_b200.so`` (include/hga_b200.h); PyTorch provides device memory, streams and the
 projection GEMMs.
 """
-from . import _lib, ops  # noqa: F401
+from . import _lib, ops, torch_ops  # noqa: F401  (torch_ops registers torch.ops.hga.*)
 from .config import ChunkPlacementPolicy, RouterConfig
 from .module import HierarchicalGlobalAttentionRouted
 from .router import ChunkRouter, RoutedKV

@@ -190,3 +190,21 @@ def test_summaries_dual_equals_two_single_calls(cuda, dtype, dh, S):
     assert torch.equal(ck_d, ck_a) and torch.equal(gk_d, gk_a)
     for a, b in zip(got_b, ref_b):
         assert torch.equal(a, b)
+
+
+def test_torch_ops_match_the_c_abi_calls(cuda):
+    """torch.ops.hga.* run the same kernels as the ops wrappers (bit-identical results)."""
+    from hierarchicalglobalattention_b200 import ops, torch_ops
+    c = cases.case("pf_qwen_bf16")
+    inp = {k: v.to(cuda) for k, v in cases.make_inputs(c).items()}
+    hp = _params(c)
+    pi, pf = torch_ops.params_lists(hp)
+    ck, gk, _ = ops.summaries(hp, inp["k_raw"], inp["k_rope"], inp["v"], inp["cos"], inp["sin"])
+    ck2, gk2, _ = torch.ops.hga.summaries(pi, pf, inp["k_raw"], inp["k_rope"], inp["v"], inp["cos"], inp["sin"], False)
+    assert torch.equal(ck, ck2) and torch.equal(gk, gk2)
+    r = ops.route_prefill(hp, inp["q"], ck, gk)
+    sc, st, og, ot = torch.ops.hga.route_prefill(pi, pf, inp["q"], ck, gk)
+    assert torch.equal(sc, r["sel_chunk"]) and torch.equal(og, r["open_gid"]) and torch.equal(ot, r["open_t0"])
+    out = ops.attend_prefill(hp, inp["q"], inp["k_rope"], inp["v"], og, ot)
+    out2 = torch.ops.hga.attend_prefill(pi, pf, inp["q"], inp["k_rope"], inp["v"], og, ot)
+    assert torch.equal(out.transpose(1, 2), out2)
