@@ -48,6 +48,7 @@ _SIGNATURES = {
                                           _P]),
     "hga_gather_h2d": (ctypes.c_int, [ctypes.POINTER(HgaParams), _P, _I32, _P, _P, _I64, _P, _P, _I32, _P, _P, _I64,
                                       _P, _I32, _P, _P, _P]),
+    "hga_debug_fault": (ctypes.c_int, [_I32, _I64]),
     "hga_route_prefill": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _P, _I32, _P, _P, _I64, _P, _P, _P, _P,
                                          _P, _P, _P]),
     "hga_route_prefill_impl": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _P, _I32, _P, _P, _I64, _P, _P, _P,

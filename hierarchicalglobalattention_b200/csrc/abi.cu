@@ -37,6 +37,7 @@ cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const QRange& qr, c
                              const void* v, int64_t kv_cap, const int32_t* open_gid, const int32_t* open_t0,
                              int Kg, void* out, int out_layout, cudaStream_t st);
 int tc_error_status(bool clear);
+void attend_tc_set_test_fault(int mode, long long wait_ns);
 int route_tc_error_status(bool clear);
 bool route_tc_supported(const hga_params& p, int64_t S);
 cudaError_t launch_route_tc(const hga_params& p, int64_t S, const QRange& qr, const void* q, int q_layout, const void* ck, const void* gk,
@@ -409,6 +410,12 @@ int hga_shard_unpack(const void* recv, int64_t rank_stride, int64_t part_offset,
   return cuda_status(hga::launch_shard_unpack(recv, rank_stride, part_offset, world, pieces, dst_block, bk, rows,
                                               row_bytes, dst, stream),
                      "hga_shard_unpack");
+}
+
+int hga_debug_fault(int32_t mode, int64_t wait_limit_ns) {
+  if (mode < 0 || mode > 1 || wait_limit_ns < 0) return fail(HGA_E_INVALID, "hga_debug_fault: mode 0/1, wait_limit_ns >= 0");
+  hga::attend_tc_set_test_fault(mode, (long long)wait_limit_ns);
+  return HGA_OK;
 }
 
 int hga_device_status(int32_t* code, int32_t clear) {

@@ -61,6 +61,8 @@ struct Args {
   const int32_t* open_gid;
   const int32_t* open_t0;
   __nv_bfloat16* out;
+  unsigned long long wait_ns;  // limit of every bounded wait
+  int fault;                   // test-only: 1 = the CTA of the last query chunk, heads 0-1, batch 0, does not load K of its tile 1
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -349,12 +351,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int64_t kvrow = ((int64_t)b * a.KVH + kvh) * a.kv_cap;
       // K of tile i+1 is issued before V of tile i: Q.K^T(i-1), which frees K's stage, completes
       // before P.V(i-2), which frees V's
-      int armed_k = 0, armed_v = 0;  // loads issued per kind (their barriers' phases, for the drain)
+      int armed[2][2] = {{0, 0}, {0, 0}};  // loads issued per [kind][stage]: their barriers' phases, for the drain
+      const bool skip_k1 = a.fault == 1 && blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && blockIdx.z == 0 && ntiles > 2;
       auto load = [&](int i, bool is_v) -> bool {
         const int st = i & 1;
+        if (skip_k1 && !is_v && i == 1) return true;  // test-only fault: tile 1's K never arrives
         uint64_t* empty = is_v ? v_empty : k_empty;
         uint64_t* full = is_v ? v_full : k_full;
-        if (i >= 2 && !mbar_wait(empty + st, ((i >> 1) - 1) & 1, abort_flag, is_v ? 9 : 1)) return false;
+        if (i >= 2 && !mbar_wait(empty + st, ((i >> 1) - 1) & 1, abort_flag, is_v ? 9 : 1, a.wait_ns)) return false;
         unsigned char* dst = smem + SmemLayout::kStage + st * SmemLayout::kStageBytes + (is_v ? 16384 : 0);
         const CUtensorMap* map = is_v ? &tm_v : &tm_k;
         mbar_expect_tx(full + st, 16384);
@@ -363,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           tma_load_2d(dst + u * 2048, map, 0, row, full + st);
           tma_load_2d(dst + 8192 + u * 2048, map, 64, row, full + st);
         }
-        (is_v ? armed_v : armed_k) += 1;
+        armed[is_v][st] += 1;
         return true;
       };
       bool go = ntiles > 0 && load(0, false);
@@ -373,10 +377,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       // drain: a CTA that gives up must not release its shared memory under loads still in flight
       for (int st = 0; st < 2; ++st) {
-        const int nk = armed_k > st ? (armed_k - 1 - st) / 2 + 1 : 0;  // loads armed on stage st
-        const int nv = armed_v > st ? (armed_v - 1 - st) / 2 + 1 : 0;
-        if (nk) mbar_drain(k_full + st, (nk - 1) & 1);
-        if (nv) mbar_drain(v_full + st, (nv - 1) & 1);
+        if (armed[0][st]) mbar_drain(k_full + st, (armed[0][st] - 1) & 1);
+        if (armed[1][st]) mbar_drain(v_full + st, (armed[1][st] - 1) & 1);
       }
     }
   } else if (warp == 1) {
@@ -386,13 +388,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t id_qk = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
       const uint32_t id_pv = idesc_bf16(true);
       const uint32_t q_addr = smem_u32(q_s);
-      bool ok = mbar_wait(q_full, 0, abort_flag, 2);
+      bool ok = mbar_wait(q_full, 0, abort_flag, 2, a.wait_ns);
       fence_after();
       for (int i = 0; ok && i <= ntiles; ++i) {
         if (i < ntiles) {
           const int st = i & 1;
-          if (!mbar_wait(k_full + st, (i >> 1) & 1, abort_flag, 3)) break;
-          if (i >= 2 && !mbar_wait(pv_done, (i - 2) & 1, abort_flag, 4)) break;
+          if (!mbar_wait(k_full + st, (i >> 1) & 1, abort_flag, 3, a.wait_ns)) break;
+          if (i >= 2 && !mbar_wait(pv_done, (i - 2) & 1, abort_flag, 4, a.wait_ns)) break;
           fence_after();
           const uint32_t k_addr = smem_u32(smem + SmemLayout::kStage + st * SmemLayout::kStageBytes);
           const uint32_t d = tmem + (st ? kColS1 : kColS0);
@@ -405,8 +407,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         if (i >= 1) {
           const int j = i - 1, st = j & 1;
-          if (!mbar_wait(p_full + st, (j >> 1) & 1, abort_flag, 5)) break;
-          if (!mbar_wait(v_full + st, (j >> 1) & 1, abort_flag, 10)) break;
+          if (!mbar_wait(p_full + st, (j >> 1) & 1, abort_flag, 5, a.wait_ns)) break;
+          if (!mbar_wait(v_full + st, (j >> 1) & 1, abort_flag, 10, a.wait_ns)) break;
           fence_after();
           const uint32_t v_addr = smem_u32(smem + SmemLayout::kStage + st * SmemLayout::kStageBytes + 16384);
           const uint32_t p_col = tmem + (st ? kColS1 : kColS0);
@@ -452,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         cnt[u] = rvalid ? c : 0;
         if (__any_sync(0xffffffffu, cnt[u] > 0)) live |= 1u << u;
       }
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 6));
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 6, a.wait_ns));
       if (!ok) break;
       fence_after();
       const uint32_t s_addr = tmem + lane_addr + (st ? kColS1 : kColS0);
@@ -491,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         if (__any_sync(0xffffffffu, rescale_o)) {
           // O holds the sum over tiles < i: wait for the last P.V, then rescale (alpha = 1 elsewhere)
-          ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (i - 1) & 1, abort_flag, 7));
+          ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (i - 1) & 1, abort_flag, 7, a.wait_ns));
           if (!ok) break;
           fence_after();
           const uint32_t o_addr = tmem + lane_addr + kColO;
@@ -519,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(p_full + st);
     }
     // epilogue
-    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, 0, abort_flag, 8));
+    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, 0, abort_flag, 8, a.wait_ns));
     if (ok) {
       fence_after();
       const int h = head_sel ? h1 : h0;
@@ -556,6 +558,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 }  // namespace tc
+
+// test-only failure injection (hga_debug_fault): read by the next launch
+static int g_test_fault = 0;
+static long long g_test_wait_ns = 0;
+void attend_tc_set_test_fault(int mode, long long wait_ns) {
+  g_test_fault = mode;
+  g_test_wait_ns = wait_ns;
+}
 
 bool attend_tc_supported(const hga_params& p) {
   return p.dtype == HGA_DTYPE_BF16 && p.head_dim == 128 && p.chunk_size == 64 && p.group_size == 16 &&
@@ -596,6 +606,9 @@ cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const QRange& qr, c
   a.scale_log2 = p.scale * 1.4426950408889634f;
   a.open_gid = open_gid; a.open_t0 = open_t0;
   a.out = (__nv_bfloat16*)out;
+  a.wait_ns = g_test_wait_ns > 0 ? (unsigned long long)g_test_wait_ns : kWaitLimitNs;
+  a.fault = g_test_fault;
+  g_test_fault = 0;  // one launch
   const int smem = SmemLayout::kTotal + 1024;
   cudaError_t e = cudaFuncSetAttribute(attend_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;

@@ -63,14 +63,15 @@ __device__ __forceinline__ unsigned long long global_ns() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   // try_wait may suspend the thread for a hardware-defined time: check the clock and the CTA's
   // abort flag after every attempt so the limit holds regardless of that time
   while (!mbar_try(bar, parity)) {
     if (*abort_flag) return false;
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicCAS(&g_tc_error, 0, code);
       return false;

@@ -241,6 +241,15 @@ int hga_shard_unpack(const void* recv, int64_t rank_stride, int64_t part_offset,
  * Synchronous (reads device memory); clear != 0 resets the words. */
 int hga_device_status(int32_t* code, int32_t clear);
 
+/* Test hook of the bounded waits' failure path (no reference counterpart).  Sets, for the next
+ * tensor-core hga_attend_prefill launch only, the limit of its bounded mbarrier waits
+ * (wait_limit_ns; 0 = the default 2 s) and, with mode 1, makes the CTA of the last query chunk,
+ * query heads 0-1, batch row 0 skip its tile-1 K load, so that a wait of that CTA runs out: it
+ * records the wait's code (hga_device_status), lets its copies and MMAs in flight land, releases
+ * its TMEM and returns without writing its rows.  Nothing faults or hangs; every later launch
+ * runs normally.  Not thread-safe; for tests. */
+int hga_debug_fault(int32_t mode, int64_t wait_limit_ns);
+
 #ifdef __cplusplus
 }
 #endif

@@ -60,3 +60,36 @@ def test_tc_no_routing_windows_only(cuda):
         p, c, inp, res, outs = _run(600, 1, 2, 1, kf, kl, tc_, tg, 1, 1, 9, cuda)
         mx, rel = HC.attn_errors(outs[2], outs[1], torch.bfloat16)
         assert mx < 2e-2 and rel < 5e-3, (kf, kl, mx, rel)
+
+
+def test_bounded_wait_runs_out_without_a_fault(cuda):
+    """The failure path of the bounded waits: one CTA's K load is withheld (hga_debug_fault), its
+    wait runs out after 1 ms, it records the code, drains and releases its TMEM; every other CTA
+    finishes, and the next launch is clean and equal to a normal one."""
+    from hierarchicalglobalattention_b200 import _lib, ops
+    c = cases.case("pf_qwen_bf16")
+    inp = {k: v.to(cuda) for k, v in cases.make_inputs(c).items()}
+    p = c["params"]
+    hp = _lib.make_params(batch=c["B"], nhead=p.nhead, kv_heads=p.kv_heads, head_dim=p.head_dim,
+                          chunk_size=p.chunk_size, group_size=p.group_size, topk_chunks=p.topk_chunks,
+                          topk_groups=p.topk_groups, keep_first=p.keep_first, keep_last=p.keep_last, theta=p.theta,
+                          dtype=c["dtype"])
+    ck, gk, _ = ops.summaries(hp, inp["k_raw"], inp["k_rope"], inp["v"], inp["cos"], inp["sin"])
+    r = ops.route_prefill(hp, inp["q"], ck, gk)
+    torch.cuda.synchronize()
+    _lib.device_status(clear=True)
+    ref = ops.attend_prefill(hp, inp["q"], inp["k_rope"], inp["v"], r["open_gid"], r["open_t0"], impl=2)
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) == 0
+    assert _lib.lib().hga_debug_fault(1, 1_000_000) == 0
+    bad = ops.attend_prefill(hp, inp["q"], inp["k_rope"], inp["v"], r["open_gid"], r["open_t0"], impl=2)
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) in (1, 3)       # the withheld K's consumer or producer gave up
+    keep = torch.ones(bad.shape[:3], dtype=torch.bool, device=cuda)
+    S, C = bad.shape[2], p.chunk_size
+    keep[0, 0:2, (S - 1) // C * C:] = False                # CTA (last chunk, heads 0-1, batch 0) wrote nothing
+    assert torch.equal(bad[keep], ref[keep])
+    again = ops.attend_prefill(hp, inp["q"], inp["k_rope"], inp["v"], r["open_gid"], r["open_t0"], impl=2)
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) == 0
+    assert torch.equal(again, ref)
