@@ -59,6 +59,8 @@ _SIGNATURES = {
                                         _P]),
     "hga_attend_decode": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I32, _P, _P, _P, _P, _I64, _I32, _P, _P, _I64,
                                          _P, _P, _I32, _P, _P]),
+    "hga_attend_decode_dca": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I32, _P, _P, _P, _P, _I64, _I32, _P, _P,
+                                             _I64, _P, _P, _P, _I32, _P, _P, _I32, _I32, _P, _P]),
     "hga_route_prefill_range": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _I64, _I64, _P, _I32, _P, _P, _I64,
                                                _P, _P, _P, _P, _P, _P, _I32, _P]),
     "hga_attend_prefill_range": (ctypes.c_int, [ctypes.POINTER(HgaParams), _I64, _I64, _I64, _P, _I32, _P, _P, _I64,

@@ -50,6 +50,11 @@ cudaError_t launch_attend_decode(const hga_params& p, int L, const void* q, cons
                                  const void* hv, int64_t hot_cap, int hot_mode, const void* ckk, const void* cvv,
                                  int64_t cold_cap, const int32_t* og, const int32_t* ot, int Kg, void* out,
                                  cudaStream_t st);
+cudaError_t launch_attend_decode_dca(const hga_params& p, int L, const void* q, const int32_t* seq_pos, const void* hk,
+                                     const void* hv, int64_t hot_cap, int hot_mode, const void* ckk, const void* cvv,
+                                     int64_t cold_cap, const int32_t* og, const int32_t* ot, const int32_t* open_pos,
+                                     int Kg, const float* dca_cos, const float* dca_sin, int dca_chunk, int dca_ceil,
+                                     void* out, cudaStream_t st);
 cudaError_t launch_shard_unpack(const void* recv, int64_t rank_stride, int64_t part_offset, int world, int pieces,
                                 const int32_t* dst_block, int64_t bk, int64_t rows, int64_t row_bytes, void* dst,
                                 cudaStream_t st);
@@ -358,6 +363,30 @@ int hga_attend_decode_impl(const hga_params* p, int32_t L, const void* q, const 
   return cuda_status(hga::launch_attend_decode(*p, L, q, seq_pos, hot_k, hot_v, hot_cap, hot_mode, ck, cv, cold_cap,
                                                open_gid, open_t0, Kg, out, stream),
                      "hga_attend_decode");
+}
+
+int hga_attend_decode_dca(const hga_params* p, int32_t L, const void* q, const int32_t* seq_pos, const void* hot_k,
+                          const void* hot_v, int64_t hot_cap, int32_t hot_mode, const void* cold_k, const void* cold_v,
+                          int64_t cold_cap, const int32_t* open_gid, const int32_t* open_t0, const int32_t* open_pos,
+                          int32_t Kg, const float* dca_cos, const float* dca_sin, int32_t dca_chunk, int32_t dca_ceil,
+                          void* out, cudaStream_t stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (L <= 0 || L > p->chunk_size) return fail(HGA_E_INVALID, "hga_attend_decode_dca: 1 <= L <= chunk_size");
+  if (!q || !seq_pos || !hot_k || !hot_v || !out || !dca_cos || !dca_sin)
+    return fail(HGA_E_INVALID, "hga_attend_decode_dca: NULL tensor");
+  if (Kg > 0 && (!open_gid || !open_t0 || !cold_k || !cold_v))
+    return fail(HGA_E_INVALID, "hga_attend_decode_dca: NULL open lists / cold record");
+  if (hot_mode != 0 && hot_mode != 1) return fail(HGA_E_INVALID, "hga_attend_decode_dca: hot_mode must be 0 or 1");
+  if (dca_chunk <= 0 || dca_ceil < dca_chunk)
+    return fail(HGA_E_INVALID, "hga_attend_decode_dca: need dca_chunk > 0 and dca_ceil >= dca_chunk");
+  if (p->head_dim % 2) return fail(HGA_E_INVALID, "hga_attend_decode_dca: head_dim must be even");
+  const void* ck = cold_k ? cold_k : hot_k;
+  const void* cv = cold_v ? cold_v : hot_v;
+  return cuda_status(hga::launch_attend_decode_dca(*p, L, q, seq_pos, hot_k, hot_v, hot_cap, hot_mode, ck, cv, cold_cap,
+                                                   open_gid, open_t0, open_pos, Kg, dca_cos, dca_sin, dca_chunk,
+                                                   dca_ceil, out, stream),
+                     "hga_attend_decode_dca");
 }
 
 int hga_gather_h2d(const hga_params* p, const int32_t* open_gid, int32_t Kg, const void* rec_k, const void* rec_v,

@@ -211,13 +211,35 @@ __device__ __forceinline__ int64_t hot_row(int chunk, int u, int C, int mode, in
   return (int64_t)slot * C + u;
 }
 
-template <typename T>
+// Dual Chunk Attention (DCA = true; the Qwen3 wrapper's dca_chunk > 0 attention,
+// ExistingModelFineTuning/Qwen3LongContext/qwen_routed_attention.py:247-283): q holds the
+// un-roped queries and every query row is roped three ways in fp32 from the tables dca_cos /
+// dca_sin [dca_ceil + 1][Dh] (rows = remapped positions): intra at qp = (pos + t) % dca_chunk,
+// successor at min(qp + dca_chunk, dca_ceil), inter at dca_ceil.  A key scores against the intra
+// query when it lies in the query's DCA chunk, the successor one in the chunk just before, else
+// the inter one.  Key positions come from the key layout (windows and the active chunk) and, for
+// opened groups, from open_pos (the routing's group ids; it differs from open_gid when the cold
+// rows are addressed by bank slot).  The reference fills masked scores with -1e4 instead of
+// excluding them; every row sees at least its own token, so those terms are exp(<= -1e4 + O(score))
+// = 0 in fp32 and exclusion is the same softmax.
+struct DcaArgs {
+  const float* cos;
+  const float* sin;
+  int chunk, ceil;
+  const int32_t* open_pos;
+};
+
+template <typename T, bool DCA>
 __global__ void __launch_bounds__(128) attend_decode_kernel(
-    hga_params p, int L, const T* __restrict__ q, const int32_t* __restrict__ seq_pos, const T* __restrict__ hot_k,
-    const T* __restrict__ hot_v, int64_t hot_cap, int hot_mode, const T* cold_k, const T* cold_v, int64_t cold_cap,
-    const int32_t* __restrict__ open_gid, const int32_t* __restrict__ open_t0, int Kg, T* __restrict__ out) {
+    hga_params p, int Lfull, int Lt, const T* __restrict__ q, const int32_t* __restrict__ seq_pos,
+    const T* __restrict__ hot_k, const T* __restrict__ hot_v, int64_t hot_cap, int hot_mode, const T* cold_k,
+    const T* cold_v, int64_t cold_cap, const int32_t* __restrict__ open_gid, const int32_t* __restrict__ open_t0, int Kg,
+    T* __restrict__ out, DcaArgs dca) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int h = blockIdx.x, b = blockIdx.y;
+  // rows [row0, row0 + L) of the block (a row tile per blockIdx.z when the block's rows do not fit
+  // one CTA's shared memory)
+  const int row0 = blockIdx.z * Lt, L = min(Lt, Lfull - row0);
   const int H = p.nhead, KVH = p.kv_heads, Dh = p.head_dim, C = p.chunk_size, gs = p.group_size;
   const int kvh = h / (H / KVH);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = 4;
@@ -227,27 +249,47 @@ __global__ void __launch_bounds__(128) attend_decode_kernel(
   int f_hi, l_lo;
   windows(n_closed, kf, kl, f_hi, l_lo);
   const size_t bh = (size_t)b * H + h;
+  const size_t qoff = (bh * Lfull + row0) * Dh;
   const bool hot_oob = hot_mode == 0 ? (int64_t)(n_closed + 1) * C > hot_cap : (int64_t)(kf + kl + 1) * C > hot_cap;
   if (hot_oob || (hot_mode == 0 && (int64_t)n_closed * C > cold_cap)) {
     if (tid == 0) atomicCAS(&g_decode_error, 0, kErrBoundsAttendDecode);
-    for (int i = tid; i < L * Dh; i += blockDim.x) out[bh * L * Dh + i] = Num<T>::from_f(0.f);
+    for (int i = tid; i < L * Dh; i += blockDim.x) out[qoff + i] = Num<T>::from_f(0.f);
     return;
   }
   // key segments: (source 0 hot / 1 cold, chunk, first row, length, tmin, causal offset)
   const int ld = Dh + 1;
-  float* qs = (float*)smem;                 // [L][ld]
-  float* ks = qs + L * ld;                  // [32][ld]
+  constexpr int NQ = DCA ? 3 : 1;
+  float* qs = (float*)smem;                 // [NQ][L][ld] (DCA: intra, successor, inter ropings)
+  float* ks = qs + NQ * L * ld;             // [32][ld]
   float* vs = ks + 32 * ld;                 // [32][ld]
   float* os = vs + 32 * ld;                 // [nw][L][Dh] per-warp partial outputs
   float* ms = os + nw * L * Dh;             // [nw][L]
   float* ls = ms + nw * L;                  // [nw][L]
   float* pw = ls + nw * L;                  // [nw][32]
-  int* kinfo = (int*)(pw + nw * 32);        // [32][3]: source, row, tmin
-  const int nfirst = f_hi * C, nlast = (n_closed - l_lo) * C, nact = c0 + L;
+  int* kinfo = (int*)(pw + nw * 32);        // [32][4]: source, row, tmin, absolute position
+  const int nfirst = f_hi * C, nlast = (n_closed - l_lo) * C, nact = c0 + row0 + L;
   int nopen = 0;
   for (int j = 0; j < Kg; ++j) nopen += (open_gid[bh * Kg + j] >= 0 && open_t0[bh * Kg + j] >= 0);
   const int nkeys = nfirst + nlast + nopen * gs + nact;
-  for (int i = tid; i < L * Dh; i += blockDim.x) qs[(i / Dh) * ld + i % Dh] = Num<T>::to_f(q[bh * L * Dh + i]);
+  if constexpr (DCA) {
+    // x * cos + rotate_half(x) * sin, each product and the sum rounded to fp32 like the reference
+    const int half = Dh / 2;
+    for (int i = tid; i < L * Dh; i += blockDim.x) {
+      const int t = i / Dh, d = i % Dh;
+      const float x = Num<T>::to_f(q[qoff + i]);
+      const float y = Num<T>::to_f(q[qoff + t * Dh + (d < half ? d + half : d - half)]);
+      const float r = d < half ? -y : y;
+      const int qp = (pos + row0 + t) % dca.chunk;
+      const int rows[3] = {qp, min(qp + dca.chunk, dca.ceil), dca.ceil};
+#pragma unroll
+      for (int v = 0; v < 3; ++v) {
+        const float c = dca.cos[(size_t)rows[v] * Dh + d], sn = dca.sin[(size_t)rows[v] * Dh + d];
+        qs[(v * L + t) * ld + d] = __fadd_rn(__fmul_rn(x, c), __fmul_rn(r, sn));
+      }
+    }
+  } else {
+    for (int i = tid; i < L * Dh; i += blockDim.x) qs[(i / Dh) * ld + i % Dh] = Num<T>::to_f(q[qoff + i]);
+  }
   for (int i = tid; i < nw * L * Dh; i += blockDim.x) os[i] = 0.f;
   for (int i = tid; i < nw * L; i += blockDim.x) { ms[i] = -INFINITY; ls[i] = 0.f; }
   __syncthreads();
@@ -256,38 +298,40 @@ __global__ void __launch_bounds__(128) attend_decode_kernel(
   for (int k0 = 0; k0 < nkeys; k0 += 32) {
     if (tid < 32) {
       const int k = k0 + tid;
-      int src = 0, tmin = 1 << 30;
+      int src = 0, tmin = 1 << 30, kpos = 0;
       int64_t row = 0;
       if (k < nkeys) {
         if (k < nfirst) {
-          row = hot_row(k / C, k % C, C, hot_mode, kf, kl, false); tmin = 0;
+          row = hot_row(k / C, k % C, C, hot_mode, kf, kl, false); tmin = 0; kpos = k;
         } else if (k < nfirst + nlast) {
           const int kk = k - nfirst;
-          row = hot_row(l_lo + kk / C, kk % C, C, hot_mode, kf, kl, false); tmin = 0;
+          row = hot_row(l_lo + kk / C, kk % C, C, hot_mode, kf, kl, false); tmin = 0; kpos = l_lo * C + kk;
         } else if (k < nfirst + nlast + nopen * gs) {
           const int kk = k - nfirst - nlast;
           // the opened entries are a prefix of the list
           const int j = kk / gs;
           row = (int64_t)open_gid[bh * Kg + j] * gs + kk % gs; tmin = open_t0[bh * Kg + j]; src = 1;
+          if constexpr (DCA) kpos = dca.open_pos[bh * Kg + j] * gs + kk % gs;
           if (row >= cold_cap) {  // a list entry past the record: skipped (never visible)
             atomicCAS(&g_decode_error, 0, kErrBoundsAttendDecode);
             row = 0; tmin = 1 << 30;
           }
         } else {
           const int u = k - nfirst - nlast - nopen * gs;
-          row = hot_row(n_closed, u, C, hot_mode, kf, kl, true); tmin = u - c0;
+          row = hot_row(n_closed, u, C, hot_mode, kf, kl, true); tmin = u - c0; kpos = n_closed * C + u;
         }
       }
-      kinfo[tid * 3 + 0] = src;
-      kinfo[tid * 3 + 1] = (int)row;
-      kinfo[tid * 3 + 2] = tmin;
+      kinfo[tid * 4 + 0] = src;
+      kinfo[tid * 4 + 1] = (int)row;
+      kinfo[tid * 4 + 2] = tmin;
+      kinfo[tid * 4 + 3] = kpos;
     }
     __syncthreads();
     for (int i = tid; i < 32 * Dh; i += blockDim.x) {
       const int r = i / Dh, d = i % Dh;
-      const size_t off = (kinfo[r * 3] ? cold_base : hot_base) + (size_t)kinfo[r * 3 + 1];
-      const T* kp = kinfo[r * 3] ? cold_k : hot_k;
-      const T* vp = kinfo[r * 3] ? cold_v : hot_v;
+      const size_t off = (kinfo[r * 4] ? cold_base : hot_base) + (size_t)kinfo[r * 4 + 1];
+      const T* kp = kinfo[r * 4] ? cold_k : hot_k;
+      const T* vp = kinfo[r * 4] ? cold_v : hot_v;
       const bool ok = k0 + r < nkeys;
       ks[r * ld + d] = ok ? Num<T>::to_f(kp[off * Dh + d]) : 0.f;
       vs[r * ld + d] = ok ? Num<T>::to_f(vp[off * Dh + d]) : 0.f;
@@ -297,11 +341,17 @@ __global__ void __launch_bounds__(128) attend_decode_kernel(
     for (int t = 0; t < L; ++t) {
       const int key = lane;  // lane j scores key j; warp w only keeps keys j % nw == w
       const bool mine = (key % nw) == warp;
-      const bool vis = mine && (k0 + key < nkeys) && t >= kinfo[key * 3 + 2];
+      const bool vis = mine && (k0 + key < nkeys) && row0 + t >= kinfo[key * 4 + 2];
       float s = -INFINITY;
       if (vis) {
+        int qv = 0;
+        if constexpr (DCA) {
+          const int cq = (pos + row0 + t) / dca.chunk, ck = kinfo[key * 4 + 3] / dca.chunk;
+          qv = ck == cq ? 0 : (ck == cq - 1 ? 1 : 2);
+        }
+        const float* qrow = qs + (qv * L + t) * ld;
         float acc = 0.f;
-        for (int d = 0; d < Dh; ++d) acc = fmaf(qs[t * ld + d], ks[key * ld + d], acc);
+        for (int d = 0; d < Dh; ++d) acc = fmaf(qrow[d], ks[key * ld + d], acc);
         s = acc * p.scale;
       }
       float mx = s;
@@ -339,7 +389,7 @@ __global__ void __launch_bounds__(128) attend_decode_kernel(
       l += ls[w * L + t] * f;
       o += os[(w * L + t) * Dh + d] * f;
     }
-    out[bh * L * Dh + i] = Num<T>::from_f(l > 0.f ? o / l : 0.f);
+    out[qoff + i] = Num<T>::from_f(l > 0.f ? o / l : 0.f);
   }
 }
 
@@ -424,16 +474,23 @@ template <typename T>
 static cudaError_t launch_attend_decode_t(const hga_params& p, int L, const void* q, const int32_t* seq_pos,
                                           const void* hk, const void* hv, int64_t hot_cap, int hot_mode, const void* ckk,
                                           const void* cvv, int64_t cold_cap, const int32_t* og, const int32_t* ot,
-                                          int Kg, void* out, cudaStream_t st) {
-  const int ld = p.head_dim + 1, nw = 4;
-  const size_t smem = ((size_t)L * ld + 64 * ld + (size_t)nw * L * p.head_dim + 2 * nw * L + nw * 32) * 4 + 32 * 3 * 4 + 64;
+                                          int Kg, void* out, const DcaArgs* dca, cudaStream_t st) {
+  const int ld = p.head_dim + 1, nw = 4, nq = dca ? 3 : 1;
+  auto smem_of = [&](int lt) {
+    return ((size_t)nq * lt * ld + 64 * ld + (size_t)nw * lt * p.head_dim + 2 * nw * lt + nw * 32) * 4 + 32 * 4 * 4 +
+           64;
+  };
+  int Lt = L;  // rows per CTA: the whole block unless its rows need more than 227 KB
+  while (Lt > 1 && smem_of(Lt) > 227 * 1024) Lt = (Lt + 1) / 2;
+  const size_t smem = smem_of(Lt);
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
-  auto kern = attend_decode_kernel<T>;
+  auto kern = dca ? attend_decode_kernel<T, true> : attend_decode_kernel<T, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.nhead, p.batch);
-  kern<<<grid, 128, smem, st>>>(p, L, (const T*)q, seq_pos, (const T*)hk, (const T*)hv, hot_cap, hot_mode,
-                                (const T*)ckk, (const T*)cvv, cold_cap, og, ot, Kg, (T*)out);
+  dim3 grid(p.nhead, p.batch, (L + Lt - 1) / Lt);
+  kern<<<grid, 128, smem, st>>>(p, L, Lt, (const T*)q, seq_pos, (const T*)hk, (const T*)hv, hot_cap, hot_mode,
+                                (const T*)ckk, (const T*)cvv, cold_cap, og, ot, Kg, (T*)out,
+                                dca ? *dca : DcaArgs{nullptr, nullptr, 1, 0, nullptr});
   return cudaGetLastError();
 }
 
@@ -442,7 +499,17 @@ cudaError_t launch_attend_decode(const hga_params& p, int L, const void* q, cons
                                  int64_t cold_cap, const int32_t* og, const int32_t* ot, int Kg, void* out,
                                  cudaStream_t st) {
   HGA_DISPATCH(p.dtype, launch_attend_decode_t, p, L, q, seq_pos, hk, hv, hot_cap, hot_mode, ckk, cvv, cold_cap, og,
-               ot, Kg, out, st)
+               ot, Kg, out, nullptr, st)
+}
+
+cudaError_t launch_attend_decode_dca(const hga_params& p, int L, const void* q, const int32_t* seq_pos, const void* hk,
+                                     const void* hv, int64_t hot_cap, int hot_mode, const void* ckk, const void* cvv,
+                                     int64_t cold_cap, const int32_t* og, const int32_t* ot, const int32_t* open_pos,
+                                     int Kg, const float* dca_cos, const float* dca_sin, int dca_chunk, int dca_ceil,
+                                     void* out, cudaStream_t st) {
+  const DcaArgs a{dca_cos, dca_sin, dca_chunk, dca_ceil, open_pos ? open_pos : og};
+  HGA_DISPATCH(p.dtype, launch_attend_decode_t, p, L, q, seq_pos, hk, hv, hot_cap, hot_mode, ckk, cvv, cold_cap, og,
+               ot, Kg, out, &a, st)
 }
 
 template <typename T>

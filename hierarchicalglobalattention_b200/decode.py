@@ -45,6 +45,21 @@ class DecodeContext:
         self.finish()
         return out
 
+    def attend_dca(self, q_raw: torch.Tensor, dca_chunk: int, dca_ceil: int, theta: float) -> torch.Tensor:
+        """Dual Chunk Attention of the block (qwen_routed_attention.py:247-283): q_raw [B,H,L,Dh]
+        before RoPE; the store holds keys roped at their intra-chunk positions."""
+        store = self.router.store
+        hot_k, hot_v = store.hot_buffers(self.layer)
+        cold_k, cold_v = store.cold_buffers(self.layer)
+        open_gid = open_pos = self.routing["open_gid"]
+        banked = store.bank_gather(self.layer, self.params, open_gid) if hasattr(store, "bank_gather") else None
+        if banked is not None:
+            cold_k, cold_v, open_gid = banked
+        out = ops.attend_decode_dca(self.params, q_raw, self.seq_pos, hot_k, hot_v, store.hot_mode, cold_k, cold_v,
+                                    open_gid, self.routing["open_t0"], dca_chunk, dca_ceil, theta, open_pos=open_pos)
+        self.finish()
+        return out
+
     def finish(self) -> None:
         if self.done:
             return

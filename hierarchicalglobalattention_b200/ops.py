@@ -301,6 +301,47 @@ def attend_decode(p: HgaParams, q: torch.Tensor, seq_pos: torch.Tensor, hot_k: t
     return out
 
 
+def dca_rope_table(dca_ceil: int, head_dim: int, theta: float, device) -> Tuple[torch.Tensor, torch.Tensor]:
+    """fp32 rotate-half RoPE cos / sin [dca_ceil + 1, Dh] of positions 0..dca_ceil, evaluated like
+    the Qwen3 wrapper's _dca_rope (qwen_routed_attention.py:66-81) in fp32 on the host (torch's
+    CPU cos / sin, so the rows are the same on every device), then copied to ``device`` and cached."""
+    key = (str(device), int(dca_ceil), int(head_dim), float(theta))
+    t = _DCA_TABLES.get(key)
+    if t is None:
+        half = head_dim // 2
+        inv = 1.0 / (theta ** (torch.arange(half, dtype=torch.float32) / half))
+        f = torch.arange(dca_ceil + 1, dtype=torch.float32).unsqueeze(-1) * inv
+        emb = torch.cat((f, f), dim=-1)
+        t = (emb.cos().to(device).contiguous(), emb.sin().to(device).contiguous())
+        _DCA_TABLES[key] = t
+    return t
+
+
+_DCA_TABLES: dict = {}
+
+
+def attend_decode_dca(p: HgaParams, q: torch.Tensor, seq_pos: torch.Tensor, hot_k: torch.Tensor, hot_v: torch.Tensor,
+                      hot_mode: int, cold_k: Optional[torch.Tensor], cold_v: Optional[torch.Tensor],
+                      open_gid: torch.Tensor, open_t0: torch.Tensor, dca_chunk: int, dca_ceil: int, theta: float,
+                      open_pos: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Dual Chunk Attention of one decode block (see hga_attend_decode_dca): q [B,H,L,Dh] un-roped;
+    the store holds the intra-chunk-roped keys.  Returns [B,H,L,Dh]."""
+    _require_cuda(q, seq_pos, hot_k, hot_v, open_gid, open_t0)
+    q = q.contiguous()
+    B, H, L, Dh = q.shape
+    out = torch.empty_like(q) if out is None else out
+    cos, sin = dca_rope_table(dca_ceil, Dh, theta, q.device)
+    hot_cap = kv_cap_of(hot_k)
+    cold_cap = kv_cap_of(cold_k) if cold_k is not None else hot_cap
+    Kg = open_gid.shape[-1]
+    check(lib().hga_attend_decode_dca(ctypes_params(p), L, ptr(q), ptr(seq_pos), ptr(hot_k), ptr(hot_v), hot_cap,
+                                      hot_mode, ptr(cold_k), ptr(cold_v), cold_cap, ptr(open_gid), ptr(open_t0),
+                                      ptr(open_pos.contiguous()) if open_pos is not None else None, Kg, ptr(cos),
+                                      ptr(sin), int(dca_chunk), int(dca_ceil), ptr(out), stream_ptr(q.device)),
+          "hga_attend_decode_dca")
+    return out
+
+
 def gather_h2d(p: HgaParams, open_gid: torch.Tensor, rec_k: torch.Tensor, rec_v: torch.Tensor, bank_k: torch.Tensor,
                bank_v: torch.Tensor, slot_gid: torch.Tensor, gid_slot: torch.Tensor, slot_stamp: torch.Tensor,
                stamp: int, counters: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -15,8 +15,11 @@ own ``position_embeddings`` (model-dtype products), fused into one prologue kern
 concatenated QKV projection GEMM.  RoPE theta is read from ``config.rope_parameters`` (transformers
 5) or ``config.rope_theta`` (older releases), default 1e6.
 
-Not carried over (outside the token-only routed hot path): the Dual Chunk Attention variant
-(``dca_chunk > 0``) and the file-system cache tier (``cache_location="fs"``); both raise.
+Dual Chunk Attention (``dca_chunk > 0``, qwen_routed_attention.py:210-283): keys stored roped at
+their intra-chunk position ``pos % dca_chunk``, routed with intra-roped queries through the
+incremental path, attended by the DCA decode kernel (three fp32 ropings of each query chosen per
+key by DCA chunk).  Not carried over: the file-system cache tier (``cache_location="fs"``), which
+raises.
 """
 from __future__ import annotations
 
@@ -27,6 +30,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .config import ChunkPlacementPolicy, RouterConfig
+from . import ops
 from .module import routed_attention
 from .router import ChunkRouter
 from .store import VramKVCacheStore
@@ -45,6 +49,40 @@ def rope_theta_of(config: Any, default: float = 1_000_000.0) -> float:
     return float(v) if v is not None else float(default)
 
 
+def dca_rotate(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """rotate-half RoPE in x's dtype (qwen_routed_attention.py:84-88; HF apply_rotary_pos_emb)."""
+    half = x.shape[-1] // 2
+    return x * cos + torch.cat((-x[..., half:], x[..., :half]), dim=-1) * sin
+
+
+def dca_forward(router: ChunkRouter, layer: int, q: torch.Tensor, k_raw: torch.Tensor, v: torch.Tensor,
+                start_pos: int, dca_chunk: int, dca_ceil: int, theta: float) -> torch.Tensor:
+    """Dual Chunk Attention of one forward call on normalised, pre-RoPE tensors
+    (QwenRoutedAttention._dca_forward, qwen_routed_attention.py:210-245): q [B,H,S,Dh], k_raw / v
+    [B,KVH,S,Dh] at positions [start_pos, start_pos + S).  Keys are roped at pos % dca_chunk (the
+    store keeps them so), routed with equally roped queries through the incremental path, and
+    each chunk piece is attended by the DCA kernel before the next is routed.  Returns the heads
+    [B,H,S,Dh]."""
+    B, H, S, Dh = q.shape
+    C = router.cfg.chunk_size
+    pos = torch.arange(start_pos, start_pos + S, device=q.device)
+    tc, ts = ops.dca_rope_table(dca_ceil, Dh, theta, q.device)
+    cos, sin = tc[pos % dca_chunk].to(q.dtype), ts[pos % dca_chunk].to(q.dtype)
+    k_dca = dca_rotate(k_raw, cos, sin)
+    q_sel = dca_rotate(q, cos, sin)
+    out = torch.empty_like(q)
+    p, done = start_pos, 0
+    while done < S:
+        take = min(C - (p % C), S - done)
+        sl = slice(done, done + take)
+        rk = router.decode_block(layer, q_sel[:, :, sl], k_dca[:, :, sl].contiguous(), k_raw[:, :, sl].contiguous(),
+                                 v[:, :, sl].contiguous(), p, return_positions=True)
+        out[:, :, sl] = rk.attend_dca(q[:, :, sl], pos[sl], dca_chunk, dca_ceil, theta)
+        p += take
+        done += take
+    return out
+
+
 class QwenRoutedAttention(nn.Module):
     """Replacement for ``Qwen3MoeAttention`` / ``Qwen3Attention`` routing through a shared
     ``ChunkRouter``; adds no parameters."""
@@ -55,8 +93,6 @@ class QwenRoutedAttention(nn.Module):
                  vram_cache_reserve_gb: float = 1.5, ram_budget_gb: float = 12.0,
                  fs_cache_dir: Optional[str] = None, dca_chunk: int = 0, dca_local: int = 0) -> None:
         super().__init__()
-        if dca_chunk > 0:
-            raise NotImplementedError("Dual Chunk Attention (dca_chunk > 0) is not part of the B200 routed path")
         if cache_location not in ("vram", "ram"):
             raise NotImplementedError(f"cache_location={cache_location!r}: the B200 path provides 'vram' and 'ram'")
         self.orig = orig
@@ -73,7 +109,13 @@ class QwenRoutedAttention(nn.Module):
         self.vram_cache_reserve_gb = vram_cache_reserve_gb
         self.ram_budget_gb = ram_budget_gb
         self.fs_cache_dir = fs_cache_dir
-        self.dca_chunk, self.dca_local = 0, 0
+        if dca_chunk > 0 and dca_chunk % chunk_size != 0:
+            # a routing chunk must lie inside one DCA chunk (qwen_routed_attention.py:137-141)
+            raise ValueError(f"dca_chunk ({dca_chunk}) must be a multiple of chunk_size ({chunk_size})")
+        self.dca_chunk = max(0, int(dca_chunk))
+        # local window added to the chunk length: default a fifth of the chunk (at least 1)
+        self.dca_local = (int(dca_local) if dca_local > 0 else max(1, self.dca_chunk // 5)) if self.dca_chunk else 0
+        self.dca_ceil = self.dca_chunk + self.dca_local
         self._cfg = RouterConfig(nhead=self.num_heads, kv_heads=self.num_kv_heads, head_dim=self.head_dim,
                                  chunk_size=chunk_size, group_size=group_size, topk_chunks=topk_chunks,
                                  topk_groups=topk_groups, theta=rope_theta_of(config))
@@ -116,6 +158,8 @@ class QwenRoutedAttention(nn.Module):
         router = self._get_router(past_key_values, B, x.dtype, x.device)
         if self.layer_idx == 0 and start_pos == 0:
             router.reset()
+        if self.dca_chunk > 0:
+            return self._dca_forward(x, start_pos, router), None
         cos, sin = position_embeddings
         # rows of the model's own table (batch row 0: every sequence of the batch is at the same positions)
         cos = cos.reshape(-1, S, Dh)[0].to(x.dtype).contiguous()
@@ -128,6 +172,43 @@ class QwenRoutedAttention(nn.Module):
         out_heads = routed_attention(router, self.layer_idx, hp, qkv, cos, sin, start_pos, start_pos, qn, kn, eps,
                                      norm_mode=1, rope_mode=1, round_table=False)
         return o.o_proj(out_heads.view(B, S, H * Dh)), None
+
+    # ------------------------------------------------------------------------------------------
+    def _dca_forward(self, x: torch.Tensor, start_pos: int, router: ChunkRouter) -> torch.Tensor:
+        """Dual Chunk Attention (QwenRoutedAttention._dca_forward / _dca_attend,
+        qwen_routed_attention.py:210-283).  The prologue kernel runs twice on the fused projection:
+        with the model-dtype RoPE rows of the intra-chunk positions (selection queries, stored
+        keys, pre-RoPE keys, values) and with an identity table (cos 1, sin 0: the normalised
+        queries unchanged, which the DCA attention ropes three ways itself).  Blocks go through
+        the incremental router chunk by chunk, each attended before the next is routed."""
+        o = self.orig
+        B, S, _ = x.shape
+        H, Dh, C, L_c = self.num_heads, self.head_dim, self.chunk_size, self.dca_chunk
+        theta = self._cfg.theta
+        qkv = self._qkv(x)
+        hp = self._cfg.hga_params(self._policy, B, x.dtype)
+        qn = o.q_norm.weight.detach().to(x.dtype).contiguous()
+        kn = o.k_norm.weight.detach().to(x.dtype).contiguous()
+        eps = float(getattr(o.q_norm, "variance_epsilon", getattr(o.q_norm, "eps", 1e-6)))
+        pos = torch.arange(start_pos, start_pos + S, device=x.device)
+        tc, ts = ops.dca_rope_table(self.dca_ceil, Dh, theta, x.device)
+        cos, sin = tc[pos % L_c].to(x.dtype), ts[pos % L_c].to(x.dtype)
+        q_sel, k_raw, k_dca, v = ops.qkv_prologue(hp, qkv, cos, sin, q_norm_w=qn, k_norm_w=kn, eps=eps, norm_mode=1,
+                                                  rope_mode=1, rot_row0=start_pos, pos0=start_pos)
+        one, zero = torch.ones_like(cos), torch.zeros_like(sin)
+        q_raw = ops.qkv_prologue(hp, qkv, one, zero, q_norm_w=qn, k_norm_w=kn, eps=eps, norm_mode=1, rope_mode=1,
+                                 rot_row0=start_pos, pos0=start_pos)[0]
+        out_heads = torch.empty(B, S, H, Dh, device=x.device, dtype=x.dtype)
+        p, done = start_pos, 0
+        while done < S:
+            take = min(C - (p % C), S - done)
+            sl = slice(done, done + take)
+            rk = router.decode_block(self.layer_idx, q_sel[:, :, sl], k_dca[:, :, sl], k_raw[:, :, sl], v[:, :, sl], p,
+                                     return_positions=True)
+            out_heads[:, sl] = rk.attend_dca(q_raw[:, :, sl], pos[sl], L_c, self.dca_ceil, theta).transpose(1, 2)
+            p += take
+            done += take
+        return o.o_proj(out_heads.view(B, S, H * Dh))
 
     # ------------------------------------------------------------------------------------------
     def _make_store(self, B: int, dtype: torch.dtype, device: torch.device):

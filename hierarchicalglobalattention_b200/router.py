@@ -59,6 +59,16 @@ class RoutedKV:
                                       self.routing["open_t0"], seq_len=self.seq_len, out=self.out)
         return self.decode.attend(q)
 
+    def attend_dca(self, q_raw: torch.Tensor, qpos: torch.Tensor, dca_chunk: int, dca_ceil: int,
+                   theta: float) -> torch.Tensor:
+        """Dual Chunk Attention over the routed keys (QwenRoutedAttention._dca_attend,
+        qwen_routed_attention.py:247-283): ``q_raw`` [B,H,L,Dh] before RoPE, ``qpos`` the block's
+        absolute positions (consecutive, from the segment's start).  Incremental segments only
+        (route_query_block(..., return_positions=True))."""
+        if self.decode is None:
+            raise ValueError("attend_dca needs a segment routed with return_positions=True")
+        return self.decode.attend_dca(q_raw, dca_chunk, dca_ceil, theta)
+
 
 class ChunkRouter:
     """Router over a tiered store; chunk-parallel prefill and incremental decode."""
@@ -180,7 +190,21 @@ class ChunkRouter:
         S = q.shape[2]
         first_chunk, last_chunk = start_pos // C, (start_pos + S - 1) // C
         if return_positions:
-            raise NotImplementedError("return_positions (the DCA attend variant) is not part of the B200 hot path")
+            # the Dual Chunk Attention caller: every block goes through the incremental path and
+            # the caller attends each segment with RoutedKV.attend_dca, in order
+            segs, p, done = [], start_pos, 0
+            while done < S:
+                take = min(C - (p % C), S - done)
+                sl = slice(done, done + take)
+                segs.append((self.decode_block(layer, q[:, :, sl], k_rope[:, :, sl], k_raw[:, :, sl], v[:, :, sl], p),
+                             done, done + take))
+                p += take
+                done += take
+            if len(segs) > 1 and self.store.hot_mode != 0:
+                raise ValueError("return_positions over several chunks needs the VRAM tier (closing a chunk "
+                                 "recycles the RAM tier's window slots before the caller attends); feed the "
+                                 "block chunk by chunk")
+            return segs
         if first_chunk == last_chunk:
             return [(self.decode_block(layer, q, k_rope, k_raw, v, start_pos), 0, S)]
         if start_pos == 0:
@@ -293,8 +317,6 @@ class ChunkRouter:
     def decode_block(self, layer, q, k_rope, k_raw, v, start_pos, return_positions: bool = False) -> RoutedKV:
         """Incremental routing of L <= chunk_size new tokens inside the active chunk
         (chunk_router.py:279-407).  q [B,H,L,Dh]; k_rope/k_raw/v [B,KVH,L,Dh]."""
-        if return_positions:
-            raise NotImplementedError("return_positions (the DCA attend variant) is not part of the B200 hot path")
         from .decode import decode_block
         return decode_block(self, layer, q, k_rope, k_raw, v, start_pos)
 

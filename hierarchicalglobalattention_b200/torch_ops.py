@@ -13,6 +13,7 @@ Operators (the C entry point each wraps):
   hga::attend_prefill (hga_attend_prefill)   -> out [B,S,H,Dh]
   hga::route_decode   (hga_route_decode)     -> mid_chunk, mid_t0, open_gid, open_t0
   hga::attend_decode  (hga_attend_decode)    -> out [B,H,L,Dh]
+  hga::attend_decode_dca (hga_attend_decode_dca) -> out [B,H,L,Dh]
   hga::gather_h2d     (hga_gather_h2d)       -> open_slot (mutates the bank and its maps)
 """
 from __future__ import annotations
@@ -110,6 +111,21 @@ def attend_decode(pi: List[int], pf: List[float], q: Tensor, seq_pos: Tensor, ho
 
 @attend_decode.register_fake
 def _(pi, pf, q, seq_pos, hot_k, hot_v, hot_mode, cold_k, cold_v, open_gid, open_t0):
+    return torch.empty_like(q)
+
+
+@torch.library.custom_op("hga::attend_decode_dca", mutates_args=())
+def attend_decode_dca(pi: List[int], pf: List[float], q: Tensor, seq_pos: Tensor, hot_k: Tensor, hot_v: Tensor,
+                      hot_mode: int, cold_k: Optional[Tensor], cold_v: Optional[Tensor], open_gid: Tensor,
+                      open_t0: Tensor, open_pos: Optional[Tensor], dca_chunk: int, dca_ceil: int,
+                      theta: float) -> Tensor:
+    return ops.attend_decode_dca(_params(pi, pf), q, seq_pos, hot_k, hot_v, hot_mode, cold_k, cold_v, open_gid,
+                                 open_t0, dca_chunk, dca_ceil, theta, open_pos=open_pos)
+
+
+@attend_decode_dca.register_fake
+def _(pi, pf, q, seq_pos, hot_k, hot_v, hot_mode, cold_k, cold_v, open_gid, open_t0, open_pos, dca_chunk, dca_ceil,
+      theta):
     return torch.empty_like(q)
 
 

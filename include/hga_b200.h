@@ -180,6 +180,25 @@ int hga_attend_decode(const hga_params* p, int32_t L, const void* q, const int32
                       const int32_t* open_gid, const int32_t* open_t0, int32_t Kg, void* out,
                       cudaStream_t stream);
 
+/* hga_attend_decode_dca: the Dual Chunk Attention variant of hga_attend_decode (the Qwen3
+ * wrapper's dca_chunk > 0 path, QwenRoutedAttention._dca_attend, qwen_routed_attention.py:247-283,
+ * whose key positions the reference threads back through route_query_block(return_positions=True),
+ * chunk_router.py:463-516).  Same key layout, visibility and buffers as hga_attend_decode; the
+ * stored keys are the intra-chunk-roped ones (position pos % dca_chunk).  q [B,H,L,Dh] holds the
+ * queries BEFORE RoPE; each row is roped three ways in fp32 from dca_cos / dca_sin
+ * [dca_ceil + 1][Dh] (fp32 rotate-half tables, row = position): intra at qp = pos % dca_chunk,
+ * successor at min(qp + dca_chunk, dca_ceil), inter at dca_ceil, dca_ceil = dca_chunk +
+ * dca_local.  A key is scored with the intra query when it lies in the query's DCA chunk
+ * (position / dca_chunk equal), the successor query in the chunk just before, else the inter one;
+ * fp32 softmax and P.V.  open_pos [B,H,Kg] gives the opened groups' ids for their positions (the
+ * routing's open_gid; NULL = open_gid itself, i.e. open_gid is not a bank-slot list). */
+int hga_attend_decode_dca(const hga_params* p, int32_t L, const void* q, const int32_t* seq_pos,
+                          const void* hot_k, const void* hot_v, int64_t hot_cap, int32_t hot_mode,
+                          const void* cold_k, const void* cold_v, int64_t cold_cap,
+                          const int32_t* open_gid, const int32_t* open_t0, const int32_t* open_pos, int32_t Kg,
+                          const float* dca_cos, const float* dca_sin, int32_t dca_chunk, int32_t dca_ceil,
+                          void* out, cudaStream_t stream);
+
 /* The two decode entry points above with an explicit kernel choice: impl 0 = automatic (the
  * fast kernels when the shape allows), 1 = the portable kernels, 2 = the fast kernels (routing:
  * L == 1 and head_dim 64/128; attention: bf16/fp16, group_size 16, head_dim 64/128, L <= 8;

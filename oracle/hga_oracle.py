@@ -662,7 +662,8 @@ def dca_apply(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Te
     return x * cos + torch.cat((-x[..., half:], x[..., :half]), dim=-1) * sin
 
 
-def dca_sequence(p: OracleParams, q_raw, k_raw, v, dca_chunk: int, dca_local: int, calls):
+def dca_sequence(p: OracleParams, q_raw, k_raw, v, dca_chunk: int, dca_local: int, calls,
+                 acc_bound: float = _ACC_BOUND, tie_rule: str = "torch"):
     """The wrapper's Dual Chunk Attention over a sequence fed as forward ``calls`` [(lo, hi)]
     (qwen_routed_attention.py:210-283).
 
@@ -701,7 +702,8 @@ def dca_sequence(p: OracleParams, q_raw, k_raw, v, dca_chunk: int, dca_local: in
         sc = sc.masked_fill(~seen, DCA_NEG)
         return torch.einsum("bhlr,bhrd->bhld", torch.softmax(sc, -1), vals.float()).to(vals.dtype)
 
-    return decode_sequence(p, q_sel, k_dca, k_raw, v, p.chunk_size, calls=calls, attend=attend)
+    return decode_sequence(p, q_sel, k_dca, k_raw, v, p.chunk_size, calls=calls, attend=attend, acc_bound=acc_bound,
+                           tie_rule=tie_rule)
 
 
 # ---------------------------------------------------------------------------------------------

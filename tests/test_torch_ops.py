@@ -12,7 +12,7 @@ def _p():
 
 
 def test_ops_are_registered():
-    for name in ("summaries", "route_prefill", "attend_prefill", "route_decode", "attend_decode", "gather_h2d"):
+    for name in ("summaries", "route_prefill", "attend_prefill", "route_decode", "attend_decode", "attend_decode_dca", "gather_h2d"):
         assert hasattr(torch.ops.hga, name), name
     assert "Tensor(a3!) bank_k" in str(torch.ops.hga.gather_h2d.default._schema) or "bank_k" in str(
         torch.ops.hga.gather_h2d.default._schema)
@@ -36,4 +36,6 @@ def test_fake_shapes_on_meta():
     mc, mt, og2, ot2 = torch.ops.hga.route_decode(pi, pf, qd, pos, ck, gk, 10)
     assert mc.shape == (B, H, 4) and og2.shape == (B, H, 8)
     assert torch.ops.hga.attend_decode(pi, pf, qd, pos, k, k, 0, None, None, og2, ot2).shape == qd.shape
+    assert torch.ops.hga.attend_decode_dca(pi, pf, qd, pos, k, k, 0, None, None, og2, ot2, None, 256, 300,
+                                           1e6).shape == qd.shape
     assert hga.ops is not None
