@@ -19,26 +19,6 @@ namespace rtc {
 
 using namespace tc;
 
-
-// Phase timestamps for development builds (-DHGA_ROUTE_PROFILE): thread 0 of the first 4096 CTAs
-// records %globaltimer after each block-wide barrier.  Compiled out otherwise.
-#ifdef HGA_ROUTE_PROFILE
-__device__ unsigned long long g_rprof[4096][16];
-#define HGA_RPROF_W(k)                                                                                \
-  do {                                                                                                \
-    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);              \
-    if ((threadIdx.x & 31) == 0 && cta < 4096) g_rprof[cta][k] = global_ns();                         \
-  } while (0)
-#define HGA_RPROF(k)                                                                                  \
-  do {                                                                                                \
-    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);              \
-    if (threadIdx.x == 0 && cta < 4096) g_rprof[cta][k] = global_ns();                                \
-  } while (0)
-#else
-#define HGA_RPROF(k) do { } while (0)
-#define HGA_RPROF_W(k) do { } while (0)
-#endif
-
 struct Args {
   int S, H, KVH, N, Kc, Kg, Kgr, keep_first, keep_last, q_layout;
   int chunk0, nl, sq;  // query chunks [chunk0, chunk0 + nl); q and the lists hold only those
@@ -250,7 +230,6 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
   const int row0 = n * C;
   const int nvalid = (a.S - row0) < C ? (a.S - row0) : C;
   const int N = a.N, NP = a.NP;
-  HGA_RPROF(0);
   uint32_t* pooled = reinterpret_cast<uint32_t*>(smem + L::kFixed);      // [2][NP]
   uint32_t* t0c = pooled + 2 * NP;                                        // [2][NP]
   unsigned char* flags = reinterpret_cast<unsigned char*>(t0c + 2 * NP);  // [2][NP]
@@ -308,7 +287,6 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
   }
   fence_before();
   __syncthreads();
-  HGA_RPROF(1);
   fence_after();
   const uint32_t tmem = ms->tmem;
   unsigned char* q_s = smem + L::kQ;
@@ -367,7 +345,6 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
       const int st = i & 1;
       // tcgen05.ld is warp-collective: keep the branch around it warp-uniform
       if (!__all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 15))) break;
-      if (warp == 2 && i < 4) HGA_RPROF_W(12 + i);
       fence_after();
       const uint32_t sa = tmem + lane_addr + st * 128;
       const int cmax = (npool - 128 * i) < 128 ? (npool - 128 * i) : 128;
@@ -461,7 +438,6 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
     }
   }
   __syncthreads();
-  HGA_RPROF(2);
 
   // ================================ chunk choice (one warp per head) ==========================
   if (warp == 2 || warp == 3) {
@@ -470,10 +446,8 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
     unsigned char* fl = flags + hs * NP;
     for (int c = lane; c < npool; c += 32) keys[c] = keys[c] ? ((keys[c] << 16) | (0xffffu - c)) : 0u;
     __syncwarp();
-    if (hs == 0) HGA_RPROF_W(8);
     if (npool <= 512) warp_topk_small(keys, npool, a.Kc, fl);
     else warp_select_u32(keys, npool, a.Kc, fl);
-    if (hs == 0) HGA_RPROF_W(9);
     const int prev = n - 1;
     const bool prev_in = n > 0 && prev >= pool_lo && prev < l_lo;
     if (prev_in) {
@@ -497,7 +471,6 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
       if (lane == 0) t0c[hs * NP + pr] = 0;
       __syncwarp();
     }
-    if (hs == 0) HGA_RPROF_W(10);
     int k = 0;
     const size_t o = (hs ? out1 : out0) * a.Kc;
     for (int base = 0; base < npool; base += 32) {
@@ -515,10 +488,8 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
       k += __popc(bal);
     }
     if (lane == 0) ms->ksel[hs] = k;
-    if (hs == 0) HGA_RPROF_W(11);
   }
   __syncthreads();
-  HGA_RPROF(3);
   const bool do_l2 = a.Kg > 0 && a.Kgr > 0 && !ms->abort;
 
   // ================================ level 2 ===================================================
@@ -557,7 +528,6 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     fence_before();
     __syncthreads();
-    HGA_RPROF(4);
     fence_after();
     if (warp == 1 && lane == 0) {
       const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((256u >> 3) << 17) | ((128u >> 4) << 24);
@@ -687,7 +657,6 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
       }
     }
     __syncthreads();
-    HGA_RPROF(5);
     if (warp == 2 || warp == 3) {
       const int hs = warp - 2;
       const int th = 4 * ms->ksel[hs];
@@ -721,7 +690,6 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
   }
   fence_before();
   __syncthreads();
-  HGA_RPROF(6);
   if (warp == 1) {
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
@@ -790,11 +758,5 @@ cudaError_t launch_route_tc(const hga_params& p, int64_t S, const QRange& qr, co
 }
 
 HGA_DEFINE_ERROR_READER(route_tc_error_status)
-
-#ifdef HGA_ROUTE_PROFILE
-extern "C" int hga_route_profile_read(unsigned long long* out) {
-  return cudaMemcpyFromSymbol(out, rtc::g_rprof, sizeof(rtc::g_rprof)) == cudaSuccess ? 0 : -1;
-}
-#endif
 
 }  // namespace hga
