@@ -10,8 +10,9 @@
 // For every row a unit's visible keys form a prefix (causal: keys j <= t - 16u; otherwise all or
 // none), so masking is one count per (row, unit).
 // Per 64-key tile (4 units):
-//   TMA warp      : 16-row boxes of K and V per unit into a 2-stage SW128 smem ring; K and V of a
-//                   stage have separate full/empty barriers (K is free once Q.K^T has read it)
+//   TMA warp      : 16-row boxes of K and V per unit into a 2-stage SW128 smem ring (one lane per
+//                   box, so a tile's boxes are issued together); K and V of a stage have separate
+//                   full/empty barriers (K is free once Q.K^T has read it)
 //   MMA warp      : S = Q.K^T  (M128 N64, A/B from smem, D in TMEM, double-buffered)
 //                   O += P.V   (A = P from TMEM, B = V from smem as MN-major, D = O in TMEM)
 //   4 softmax warps: one thread per query row (TMEM lane), exp2 domain.  Tile 0 (the causal
@@ -340,6 +341,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   unsigned char* q_s = smem + SmemLayout::kQ;
   if (warp == 0) {
     // ------------------------------- TMA producer -------------------------------------------
+    // The whole warp runs the loop: lane 0 arms the barriers, lanes 0-7 issue a tile's eight 2 KB
+    // boxes (four units x two 64-column halves, one box each), so they are in flight together
     if (lane == 0) {
       mbar_expect_tx(q_full, 32768);
       for (int hh = 0; hh < 2; ++hh)
@@ -348,39 +351,44 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (a.q_layout == 1) tma_load_3d(dst, &tm_q, kb * 64, h0 + hh, b * a.sq + lrow0, q_full);
           else tma_load_2d(dst, &tm_q, kb * 64, (b * a.H + h0 + hh) * a.sq + lrow0, q_full);
         }
-      const int64_t kvrow = ((int64_t)b * a.KVH + kvh) * a.kv_cap;
-      // K of tile i+1 is issued before V of tile i: Q.K^T(i-1), which frees K's stage, completes
-      // before P.V(i-2), which frees V's
-      int armed[2][2] = {{0, 0}, {0, 0}};  // loads issued per [kind][stage]: their barriers' phases, for the drain
-      const bool skip_k1 = a.fault == 1 && blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && blockIdx.z == 0 && ntiles > 2;
-      auto load = [&](int i, bool is_v) -> bool {
-        const int st = i & 1;
-        if (skip_k1 && !is_v && i == 1) return true;  // test-only fault: tile 1's K never arrives
-        uint64_t* empty = is_v ? v_empty : k_empty;
-        uint64_t* full = is_v ? v_full : k_full;
-        if (i >= 2 && !mbar_wait(empty + st, ((i >> 1) - 1) & 1, abort_flag, is_v ? 9 : 1, a.wait_ns)) return false;
-        unsigned char* dst = smem + SmemLayout::kStage + st * SmemLayout::kStageBytes + (is_v ? 16384 : 0);
-        const CUtensorMap* map = is_v ? &tm_v : &tm_k;
-        mbar_expect_tx(full + st, 16384);
-        for (int u = 0; u < kUnitsPerTile; ++u) {
-          const int row = (int)(kvrow + units[i * kUnitsPerTile + u].pos);
-          tma_load_2d(dst + u * 2048, map, 0, row, full + st);
-          tma_load_2d(dst + 8192 + u * 2048, map, 64, row, full + st);
-        }
-        armed[is_v][st] += 1;
-        return true;
-      };
-      bool go = ntiles > 0 && load(0, false);
-      for (int i = 0; go && i < ntiles; ++i) {
-        if (i + 1 < ntiles) go = load(i + 1, false);
-        if (go) go = load(i, true);
-      }
-      // drain: a CTA that gives up must not release its shared memory under loads still in flight
-      for (int st = 0; st < 2; ++st) {
-        if (armed[0][st]) mbar_drain(k_full + st, (armed[0][st] - 1) & 1);
-        if (armed[1][st]) mbar_drain(v_full + st, (armed[1][st] - 1) & 1);
-      }
     }
+    const int64_t kvrow = ((int64_t)b * a.KVH + kvh) * a.kv_cap;
+    // K of tile i+1 is issued before V of tile i: Q.K^T(i-1), which frees K's stage, completes
+    // before P.V(i-2), which frees V's
+    int armed_k0 = 0, armed_k1 = 0, armed_v0 = 0, armed_v1 = 0;  // loads issued per kind and stage: the drain's phases
+    const bool skip_k1 = a.fault == 1 && blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && blockIdx.z == 0 && ntiles > 2;
+    auto load = [&](int i, bool is_v) -> bool {
+      const int st = i & 1;
+      if (skip_k1 && !is_v && i == 1) return true;  // test-only fault: tile 1's K never arrives
+      uint64_t* empty = is_v ? v_empty : k_empty;
+      uint64_t* full = is_v ? v_full : k_full;
+      if (i >= 2 &&
+          !__all_sync(0xffffffffu, mbar_wait(empty + st, ((i >> 1) - 1) & 1, abort_flag, is_v ? 9 : 1, a.wait_ns)))
+        return false;
+      unsigned char* dst = smem + SmemLayout::kStage + st * SmemLayout::kStageBytes + (is_v ? 16384 : 0);
+      const CUtensorMap* map = is_v ? &tm_v : &tm_k;
+      if (lane == 0) mbar_expect_tx(full + st, 16384);
+      if (lane < 2 * kUnitsPerTile) {
+        const int u = lane >> 1, hf = lane & 1;
+        const int row = (int)(kvrow + units[i * kUnitsPerTile + u].pos);
+        tma_load_2d(dst + hf * 8192 + u * 2048, map, hf * 64, row, full + st);
+      }
+      if (is_v) (st ? armed_v1 : armed_v0) += 1;
+      else (st ? armed_k1 : armed_k0) += 1;
+      return true;
+    };
+    bool go = ntiles > 0 && load(0, false);
+    for (int i = 0; go && i < ntiles; ++i) {
+      if (i + 1 < ntiles) go = load(i + 1, false);
+      if (go) go = load(i, true);
+    }
+    // drain: a CTA that gives up must not release its shared memory under loads still in flight
+    if (lane == 0)
+      for (int st = 0; st < 2; ++st) {
+        const int nk = st ? armed_k1 : armed_k0, nv = st ? armed_v1 : armed_v0;
+        if (nk > 0) mbar_drain(k_full + st, (nk - 1) & 1);
+        if (nv > 0) mbar_drain(v_full + st, (nv - 1) & 1);
+      }
   } else if (warp == 1) {
     // ------------------------------- MMA issuer ---------------------------------------------
     if (lane == 0) {
@@ -497,13 +505,14 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (!ok) break;
           fence_after();
           const uint32_t o_addr = tmem + lane_addr + kColO;
-          for (int c0 = 0; c0 < 128; c0 += 32) {
-            uint32_t o[32];
-            HGA_LD32(o_addr + c0, o);
+#pragma unroll 1
+          for (int c0 = 0; c0 < 128; c0 += 16) {
+            uint32_t o[16];
+            HGA_LD16(o_addr + c0, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            HGA_ST32(o_addr + c0, o);
+            for (int c = 0; c < 16; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            HGA_ST16(o_addr + c0, o);
           }
           tmem_wait_st();
         }
@@ -533,18 +542,19 @@ __global__ void __launch_bounds__(kThreads, 2)
         dst = a.out_layout == 1 ? a.out + (((int64_t)b * a.sq + tt) * a.H + h) * 128
                                 : a.out + (((int64_t)b * a.H + h) * a.sq + tt) * 128;
       }
-      for (int c0 = 0; c0 < 128; c0 += 32) {
-        uint32_t o[32];
-        HGA_LD32(o_addr + c0, o);
+#pragma unroll 1
+      for (int c0 = 0; c0 < 128; c0 += 16) {
+        uint32_t o[16];
+        HGA_LD16(o_addr + c0, o);
         tmem_wait_ld();
         if (dst) {
-          uint32_t w[16];
+          uint32_t w[8];
 #pragma unroll
-          for (int c = 0; c < 16; ++c)
+          for (int c = 0; c < 8; ++c)
             w[c] = pack_bf16(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
           uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) d4[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+          d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
       }
     }
@@ -608,7 +618,8 @@ cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const QRange& qr, c
   a.out = (__nv_bfloat16*)out;
   a.wait_ns = g_test_wait_ns > 0 ? (unsigned long long)g_test_wait_ns : kWaitLimitNs;
   a.fault = g_test_fault;
-  g_test_fault = 0;  // one launch
+  g_test_fault = 0;  // the fault and its wait limit hold for one launch
+  g_test_wait_ns = 0;
   const int smem = SmemLayout::kTotal + 1024;
   cudaError_t e = cudaFuncSetAttribute(attend_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;

@@ -84,7 +84,10 @@ def test_bounded_wait_runs_out_without_a_fault(cuda):
     assert _lib.lib().hga_debug_fault(1, 1_000_000) == 0
     bad = ops.attend_prefill(hp, inp["q"], inp["k_rope"], inp["v"], r["open_gid"], r["open_t0"], impl=2)
     torch.cuda.synchronize()
-    assert _lib.device_status(clear=True) in (1, 3)       # the withheld K's consumer or producer gave up
+    # one of the stalled CTA's waits ran out first (codes 1-10 name the wait; which one wins the
+    # race between its warps varies), never a drain (0x7f)
+    code = _lib.device_status(clear=True)
+    assert 1 <= code <= 10, code
     keep = torch.ones(bad.shape[:3], dtype=torch.bool, device=cuda)
     S, C = bad.shape[2], p.chunk_size
     keep[0, 0:2, (S - 1) // C * C:] = False                # CTA (last chunk, heads 0-1, batch 0) wrote nothing
