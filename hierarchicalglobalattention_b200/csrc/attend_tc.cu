@@ -10,11 +10,14 @@
 // For every row a unit's visible keys form a prefix (causal: keys j <= t - 16u; otherwise all or
 // none), so masking is one count per (row, unit).
 // Per 64-key tile (4 units):
-//   TMA warp      : 16-row boxes of K and V per unit into a 2-stage SW128 smem ring (one lane per
-//                   box, so a tile's boxes are issued together); K and V of a stage have separate
-//                   full/empty barriers (K is free once Q.K^T has read it)
-//   MMA warp      : S = Q.K^T  (M128 N64, A/B from smem, D in TMEM, double-buffered)
-//                   O += P.V   (A = P from TMEM, B = V from smem as MN-major, D = O in TMEM)
+//   TMA warp      : K and V of the tile into a 2-stage SW128 smem ring: one 64-row box per
+//                   64-column half when the 4 units are consecutive rows (current chunk,
+//                   windows), else one 16-row box per unit and half, one lane per box; K and V of
+//                   a stage have separate full/empty barriers (K is free once Q.K^T has read it)
+//   MMA warp      : S = Q.K^T  (M128 N64, A/B from smem, D in TMEM)
+//                   O += P.V   (A = P from its own TMEM columns, B = V from smem as MN-major)
+//                   Q.K^T of tile i+1 overwrites S as soon as the softmax warps have read tile i
+//                   into registers; P.V(i) reads P, which the softmax writes only after P.V(i-1)
 //   4 softmax warps: one thread per query row (TMEM lane), exp2 domain.  Tile 0 (the causal
 //                   current chunk) sets the row max; later tiles are exponentiated against it and
 //                   take a max pass (and a lazy O rescale) only when a p could exceed 2^8.  Units
@@ -34,7 +37,10 @@ constexpr int kUnitsPerTile = 4;
 constexpr int kMaxUnits = 328;  // current 4 + windows <= 64 + opened union <= 256, rounded up to whole tiles
 constexpr int kMaxKg = 128;
 constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColS0 = 0, kColS1 = 64, kColO = 128;
+// TMEM columns: S (fp32 scores of one tile), P (its probabilities as packed bf16 pairs, the A
+// operand of P.V), O (fp32 accumulator).  P has its own columns, so Q.K^T of the next tile can
+// overwrite S as soon as the softmax warps have read it into registers.
+constexpr uint32_t kColS = 0, kColP = 64, kColO = 128;
 
 struct Unit {
   int pos;    // first token row of the unit inside the (b, kvh) row block
@@ -170,7 +176,8 @@ __device__ __forceinline__ void tile_exp(const uint32_t (&r)[64], const int (&cn
 
 __global__ void __launch_bounds__(kThreads, 2)
     attend_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                     const __grid_constant__ CUtensorMap tm_v, const Args a) {
+                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_k64,
+                     const __grid_constant__ CUtensorMap tm_v64, const Args a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int ln = blockIdx.x, hp = blockIdx.y, b = blockIdx.z;
@@ -195,8 +202,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* k_empty = bars + 3;   // [2]  released when Q.K^T is done, its V only after P.V, so the
   uint64_t* v_full = bars + 5;    // [2]  next K load overlaps the softmax of the current tile
   uint64_t* v_empty = bars + 7;   // [2]
-  uint64_t* s_full = bars + 9;    // [2]
-  uint64_t* p_full = bars + 11;   // [2]
+  uint64_t* s_full = bars + 9;    // Q.K^T of a tile is in S
+  uint64_t* s_free = bars + 10;   // the softmax warps have read S (128 arrivals)
+  uint64_t* p_full = bars + 11;   // P of a tile is in TMEM (128 arrivals)
   uint64_t* pv_done = bars + 13;  // one completion per P.V (its waits are never more than one phase behind)
   uint64_t* o_done = bars + 14;   // single completion after the last P.V (the epilogue's wait)
   uint64_t* drain = bars + 15;    // the MMA issuer's last commit: every MMA it issued has completed
@@ -218,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(k_empty + i, 1);
       mbar_init(v_full + i, 1);
       mbar_init(v_empty + i, 1);
-      mbar_init(s_full + i, 1);
+      mbar_init(i ? s_free : s_full, i ? 128 : 1);
       mbar_init(p_full + i, 128);
     }
     mbar_init(pv_done, 1);
@@ -366,12 +374,16 @@ __global__ void __launch_bounds__(kThreads, 2)
           !__all_sync(0xffffffffu, mbar_wait(empty + st, ((i >> 1) - 1) & 1, abort_flag, is_v ? 9 : 1, a.wait_ns)))
         return false;
       unsigned char* dst = smem + SmemLayout::kStage + st * SmemLayout::kStageBytes + (is_v ? 16384 : 0);
-      const CUtensorMap* map = is_v ? &tm_v : &tm_k;
       if (lane == 0) mbar_expect_tx(full + st, 16384);
-      if (lane < 2 * kUnitsPerTile) {
+      // a tile of four consecutive units (the current chunk, the windows) is one 64-row box per
+      // half; the smem image is the same as four 16-row boxes (the swizzle follows the address)
+      const Unit* tu = units + i * kUnitsPerTile;
+      const bool contiguous = tu[1].pos == tu[0].pos + 16 && tu[2].pos == tu[0].pos + 32 && tu[3].pos == tu[0].pos + 48;
+      if (contiguous) {
+        if (lane < 2) tma_load_2d(dst + lane * 8192, is_v ? &tm_v64 : &tm_k64, lane * 64, (int)(kvrow + tu[0].pos), full + st);
+      } else if (lane < 2 * kUnitsPerTile) {
         const int u = lane >> 1, hf = lane & 1;
-        const int row = (int)(kvrow + units[i * kUnitsPerTile + u].pos);
-        tma_load_2d(dst + hf * 8192 + u * 2048, map, hf * 64, row, full + st);
+        tma_load_2d(dst + hf * 8192 + u * 2048, is_v ? &tm_v : &tm_k, hf * 64, (int)(kvrow + tu[u].pos), full + st);
       }
       if (is_v) (st ? armed_v1 : armed_v0) += 1;
       else (st ? armed_k1 : armed_k0) += 1;
@@ -402,24 +414,25 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (i < ntiles) {
           const int st = i & 1;
           if (!mbar_wait(k_full + st, (i >> 1) & 1, abort_flag, 3, a.wait_ns)) break;
-          if (i >= 2 && !mbar_wait(pv_done, (i - 2) & 1, abort_flag, 4, a.wait_ns)) break;
+          // S is free once the softmax warps have read the previous tile's scores
+          if (i >= 1 && !mbar_wait(s_free, (i - 1) & 1, abort_flag, 4, a.wait_ns)) break;
           fence_after();
           const uint32_t k_addr = smem_u32(smem + SmemLayout::kStage + st * SmemLayout::kStageBytes);
-          const uint32_t d = tmem + (st ? kColS1 : kColS0);
+          const uint32_t d = tmem + kColS;
           for (int kb = 0; kb < 2; ++kb)
             for (int kk = 0; kk < 4; ++kk)
               mma_ss(d, sdesc(q_addr + kb * 16384 + kk * 32, 16, 1024), sdesc(k_addr + kb * 8192 + kk * 32, 16, 1024),
                      id_qk, (kb | kk) != 0);
-          mma_commit(s_full + st);
+          mma_commit(s_full);
           mma_commit(k_empty + st);
         }
         if (i >= 1) {
           const int j = i - 1, st = j & 1;
-          if (!mbar_wait(p_full + st, (j >> 1) & 1, abort_flag, 5, a.wait_ns)) break;
+          if (!mbar_wait(p_full, j & 1, abort_flag, 5, a.wait_ns)) break;
           if (!mbar_wait(v_full + st, (j >> 1) & 1, abort_flag, 10, a.wait_ns)) break;
           fence_after();
           const uint32_t v_addr = smem_u32(smem + SmemLayout::kStage + st * SmemLayout::kStageBytes + 16384);
-          const uint32_t p_col = tmem + (st ? kColS1 : kColS0);
+          const uint32_t p_col = tmem + kColP;
           for (int kk = 0; kk < 4; ++kk)
             mma_ts(tmem + kColO, p_col + kk * 8, sdesc(v_addr + kk * 2048, 8192, 1024), id_pv,
                    (j > 0 || kk > 0) ? 1u : 0u);
@@ -447,7 +460,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     float l_run = 0.f;
     bool ok = true;
     for (int i = 0; i < ntiles && ok; ++i) {
-      const int st = i & 1;
       // visibility of the tile's units for this row: a visible prefix of cnt[u] keys (the causal
       // current-chunk tile, i == 0) or all / none of them; `live` marks the units some row of this
       // warp sees (the others are neither loaded nor exponentiated)
@@ -462,15 +474,19 @@ __global__ void __launch_bounds__(kThreads, 2)
         cnt[u] = rvalid ? c : 0;
         if (__any_sync(0xffffffffu, cnt[u] > 0)) live |= 1u << u;
       }
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, abort_flag, 6, a.wait_ns));
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full, i & 1, abort_flag, 6, a.wait_ns));
       if (!ok) break;
       fence_after();
-      const uint32_t s_addr = tmem + lane_addr + (st ? kColS1 : kColS0);
+      const uint32_t s_addr = tmem + lane_addr + kColS;
       uint32_t r[64];
 #pragma unroll
       for (int u = 0; u < kUnitsPerTile; ++u)
         if (live >> u & 1) HGA_LD16(s_addr + u * 16, (r + u * 16));
       if (live) tmem_wait_ld();
+      // the scores are in registers: the next tile's Q.K^T may overwrite S
+      fence_before();
+      mbar_arrive(s_free);
+      bool pv_waited = i == 0;  // P.V(i-1) has completed (P's columns and O may be written)
       // Tile 0 (the causal current chunk, where every valid row sees at least its own key) sets
       // the running max.  Later tiles are exponentiated against the running max directly; only
       // when a p could exceed 2^8 (the row's tile sum is above 2^8, or not finite) does the warp
@@ -503,6 +519,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           // O holds the sum over tiles < i: wait for the last P.V, then rescale (alpha = 1 elsewhere)
           ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (i - 1) & 1, abort_flag, 7, a.wait_ns));
           if (!ok) break;
+          pv_waited = true;
           fence_after();
           const uint32_t o_addr = tmem + lane_addr + kColO;
 #pragma unroll 1
@@ -524,10 +541,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       float ps0, ps1;
       unf2(ps, ps0, ps1);
       l_run += ps0 + ps1;
-      HGA_ST32(s_addr, pk);
+      if (!pv_waited) {  // P.V(i-1) still reads P's columns
+        ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (i - 1) & 1, abort_flag, 4, a.wait_ns));
+        if (!ok) break;
+        fence_after();
+      }
+      HGA_ST32(tmem + lane_addr + kColP, pk);
       tmem_wait_st();
       fence_before();
-      mbar_arrive(p_full + st);
+      mbar_arrive(p_full);
     }
     // epilogue
     if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, 0, abort_flag, 8, a.wait_ns));
@@ -597,6 +619,9 @@ cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const QRange& qr, c
   const cuuint64_t dkv[2] = {128, rows_kv}, skv[1] = {256};
   const cuuint32_t bkv[2] = {64, 16};
   if (!make_map(&mk, k_rope, 2, dkv, skv, bkv) || !make_map(&mv, v, 2, dkv, skv, bkv)) return cudaErrorInvalidValue;
+  CUtensorMap mk64, mv64;
+  const cuuint32_t bkv64[2] = {64, 64};
+  if (!make_map(&mk64, k_rope, 2, dkv, skv, bkv64) || !make_map(&mv64, v, 2, dkv, skv, bkv64)) return cudaErrorInvalidValue;
   if (q_layout == 1) {
     const cuuint64_t dq[3] = {128, (cuuint64_t)p.nhead, (cuuint64_t)(p.batch * qr.sq)};
     const cuuint64_t sq[2] = {256, (cuuint64_t)p.nhead * 256};
@@ -624,7 +649,7 @@ cudaError_t launch_attend_tc(const hga_params& p, int64_t S, const QRange& qr, c
   cudaError_t e = cudaFuncSetAttribute(attend_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(qr.count, p.nhead / 2, p.batch);
-  attend_tc_kernel<<<grid, kThreads, smem, st>>>(mq, mk, mv, a);
+  attend_tc_kernel<<<grid, kThreads, smem, st>>>(mq, mk, mv, mk64, mv64, a);
   return cudaGetLastError();
 }
 
