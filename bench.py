@@ -845,8 +845,9 @@ def main():
         try:
             d = decode_bench(device)
             line["decode"] = {"workload": "configs[2]: batched decode step, B=16 x 32768 cached tokens, one layer",
-                              "unit": "us/layer-step", "value": d["ram"]["us_per_layer_step"],
-                              "tier": "ram (cold K/V in pinned host memory)", **d}
+                              "unit": "us/layer-step", "value": d["ram_bank"]["us_per_layer_step"],
+                              "tier": "ram (cold K/V in pinned host memory) behind the 256-chunk VRAM token "
+                                      "bank, the reference Qwen patch's default; ram = no bank", **d}
             if not args.no_cpu_baseline:
                 line["decode"]["cpu_baseline"] = cpu_decode_sample()
         except Exception as e:
