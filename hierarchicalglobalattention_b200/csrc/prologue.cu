@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(kProWarps * 32) prologue_vec_kernel(
 // the position and the column only) instead of once per head row, four rows' loads are issued
 // before any of them is used, and the row index needs no 64-bit division.  V rows are copied.
 template <typename T, int EPL>
-__global__ void __launch_bounds__(kProWarps * 32) prologue_tok_kernel(
+__global__ void __launch_bounds__(kProWarps * 32, 4) prologue_tok_kernel(
     hga_params p, int64_t S, const T* __restrict__ qkv, int64_t row_stride, const T* __restrict__ qw,
     const T* __restrict__ kw, float eps, int norm_mode, const void* __restrict__ cos_t,
     const void* __restrict__ sin_t, int rope_mode, int64_t rot_row0, int64_t pos0, T* __restrict__ q_out,
@@ -243,7 +243,9 @@ __global__ void __launch_bounds__(kProWarps * 32) prologue_tok_kernel(
       }
       if (is_q ? qw != nullptr : kw != nullptr) {
         for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-        const float mean = __fdiv_rn(ss, (float)Dh);
+        // ss / Dh: Dh is a power of two, so the product with its exact reciprocal is the same
+        // correctly rounded quotient
+        const float mean = __fmul_rn(ss, 1.f / (float)Dh);
         const float rs = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, eps)));
 #pragma unroll
         for (int e = 0; e < EPL; ++e) {
