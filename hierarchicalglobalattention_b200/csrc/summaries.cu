@@ -195,17 +195,26 @@ __global__ void __launch_bounds__(256) summaries_dual_kernel(
 #pragma unroll
     for (int e = 0; e < 8; ++e) sr[e] = so[e] = sv[e] = 0.f;
     const int t0 = blk * 16;
-#pragma unroll 4
-    for (int u = 0; u < 16; ++u) {
-      const int t = t0 + u;
-      if (t < len) {
-        const size_t off = base + (size_t)(row0 + t) * DH;
-        const uint4 ur = __ldg(reinterpret_cast<const uint4*>(k_raw + off));
-        const uint4 uo = __ldg(reinterpret_cast<const uint4*>(k_rope + off));
-        const uint4 uv = __ldg(reinterpret_cast<const uint4*>(v + off));
-        const T* hr = reinterpret_cast<const T*>(&ur);
-        const T* ho = reinterpret_cast<const T*>(&uo);
-        const T* hv = reinterpret_cast<const T*>(&uv);
+    // eight rows' loads (24 x 16 bytes) in flight before they are added, in row order; rows past
+    // the sequence load the chunk's first row (in bounds) and are not added
+#pragma unroll
+    for (int u0 = 0; u0 < 16; u0 += 8) {
+      if (t0 + u0 >= len) break;
+      uint4 ur[8], uo[8], uv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int t = t0 + u0 + u;
+        const size_t off = base + (size_t)(row0 + (t < len ? t : 0)) * DH;
+        ur[u] = __ldg(reinterpret_cast<const uint4*>(k_raw + off));
+        uo[u] = __ldg(reinterpret_cast<const uint4*>(k_rope + off));
+        uv[u] = __ldg(reinterpret_cast<const uint4*>(v + off));
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (t0 + u0 + u >= len) break;
+        const T* hr = reinterpret_cast<const T*>(&ur[u]);
+        const T* ho = reinterpret_cast<const T*>(&uo[u]);
+        const T* hv = reinterpret_cast<const T*>(&uv[u]);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           sr[e] = __fadd_rn(sr[e], Num<T>::to_f(hr[e]));
