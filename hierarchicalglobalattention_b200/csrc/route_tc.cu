@@ -578,10 +578,13 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
       // one bitonic clean); otherwise from a radix select on the 16-bit score.
       const bool active = rvalid && nreal > 0;
       const bool all = a.Kgr >= a.Kc * M || nreal <= a.Kgr;
-      uint16_t* pm = reinterpret_cast<uint16_t*>(q_s);           // [2][64][KT], see below
+      // [2][64][KTP], see below; rows padded by 16 bytes so that 16-byte stores of 32 rows spread
+      // over all banks (an unpadded row of 64 u16 puts every row at the same banks)
+      constexpr int KTP = KT + 8;
+      uint16_t* pm = reinterpret_cast<uint16_t*>(q_s);
       auto put = [&](uint32_t k32) {  // record a requested key in the pooling matrix
         const int j = 0xffff - (int)(k32 & 0xffffu);
-        pm[(size_t)(hs * 64 + t) * KT + j] = (uint16_t)(k32 >> 16);
+        pm[(size_t)(hs * 64 + t) * KTP + j] = (uint16_t)(k32 >> 16);
       };
       const bool sorted_path = KT == 64 && a.Kgr <= 32 && active && !all;
       uint32_t T = 0u;    // radix path: requested iff score > T, or == T for the first `need` (lowest j)
@@ -592,7 +595,9 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
           sort_desc<32>(r + 32);
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = max(r[i], r[KT - 1 - i]);
-          clean_desc<32>(r);  // r[0..31]: the 32 highest keys, descending
+          // r[0..31]: the set of the 32 highest keys (a bitonic sequence); sorted only when fewer
+          // than 32 of them are requested
+          if (a.Kgr < 32) clean_desc<32>(r);
         }
       }
       if (!sorted_path && active && !all) {
@@ -612,7 +617,7 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
       // then one thread per (head, candidate) reduces the candidate's column over the 64 rows.
       // every row thread writes its whole row (zeros where nothing is requested); the matrix
       // reuses the Q area, which the level-2 MMA (waited for above) no longer reads
-      uint4* prow = reinterpret_cast<uint4*>(pm + (size_t)(hs * 64 + t) * KT);
+      uint4* prow = reinterpret_cast<uint4*>(pm + (size_t)(hs * 64 + t) * KTP);
       if (sorted_path) {
 #pragma unroll
         for (int c = 0; c < KT / 8; ++c) prow[c] = make_uint4(0, 0, 0, 0);
@@ -644,11 +649,11 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
       asm volatile("bar.sync 2, 128;" ::: "memory");
       for (int i = row; i < 2 * KT; i += 128) {
         const int hh = i / KT, j = i % KT;
-        const uint16_t* src = pm + (size_t)hh * 64 * KT + j;  // column j: consecutive lanes, consecutive j
+        const uint16_t* src = pm + (size_t)hh * 64 * KTP + j;  // column j: consecutive lanes, consecutive j
         uint32_t mx = 0u, first = 0xffffffffu;
 #pragma unroll 16
         for (int t2 = 63; t2 >= 0; --t2) {
-          const uint32_t v = src[(size_t)t2 * KT];
+          const uint32_t v = src[(size_t)t2 * KTP];
           mx = max(mx, v);
           first = v ? (uint32_t)t2 : first;
         }
