@@ -538,7 +538,88 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
                  idesc, (kb | kk) != 0);
       mma_commit(s2_full);
     }
-    if (warp >= 2 && warp < 6) {
+    // With eight row warps and at most 32 requests per row, two threads score a row: warps w and
+    // w + 4 take its candidates [0, 32) and [32, 64), each sorts its 32 keys, and the first thread
+    // of the row merges the partner's sorted keys (passed through the freed level-2 tile) into the
+    // row's top-32 set.
+    constexpr int KT = 4 * KL;  // candidate columns per head (Kc * M <= 4 * KL)
+    constexpr int KTP = KT + 8;
+    uint16_t* pm = reinterpret_cast<uint16_t*>(q_s);  // pooling matrix [2][64][KTP], see below
+    const bool split = kRowWarps == 8 && KT == 64 && (a.Kgr <= 32 || a.Kgr >= a.Kc * M);
+    if (split && warp >= 2) {
+      const int quarter = warp & 3, part = (warp - 2) >> 2;
+      const int row = quarter * 32 + lane;
+      const int hs = row >> 6, t = row & 63;
+      const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+      const int th = 4 * ms->ksel[hs];
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(s2_full, 0, abort_flag, 16));
+      fence_after();
+      uint32_t r[32];
+      if (ok) {
+        HGA_LD32(tmem + lane_addr + hs * 128 + part * 32, r);
+        tmem_wait_ld();
+      }
+      const bool rvalid = ok && t < nvalid;
+      const size_t dbg_row = ((hs ? out1 : out0) * C + t) * (size_t)(a.Kc * M);
+      int nreal = 0;
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = part * 32 + jj;
+        uint32_t key = 0u;
+        if (rvalid && j < th) {
+          if (t >= ms->selt0[hs][j >> 2]) {
+            const uint32_t sb = bf16_score_bits(r[jj], a.scale);
+            key = ord16_bits(sb);
+            if (a.dbg_l2) a.dbg_l2[dbg_row + j] = __uint_as_float(sb);
+          } else if (a.dbg_l2) {
+            a.dbg_l2[dbg_row + j] = kNeg;
+          }
+        }
+        r[jj] = key ? ((key << 16) | (0xffffu - j)) : 0u;  // unique: equal scores -> lower j first
+        nreal += key != 0u;
+      }
+      sort_desc<32>(r);
+      uint32_t* xk = reinterpret_cast<uint32_t*>(tile_s);  // [128 rows][33]: the second part's keys, count
+      if (part == 1) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) xk[row * 33 + i] = r[i];
+        xk[row * 33 + 32] = (uint32_t)nreal;
+      }
+      asm volatile("bar.sync 3, 256;" ::: "memory");
+      if (part == 0) {
+        nreal += (int)xk[row * 33 + 32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = max(r[i], xk[row * 33 + 31 - i]);  // the top-32 set
+        const bool active = rvalid && nreal > 0;
+        // every requested key is in the top-32 set: all non-zero keys when at most Kgr are
+        // valid (or Kgr covers every candidate), else the Kgr highest
+        const bool all = a.Kgr >= a.Kc * M || nreal <= a.Kgr;
+        if (active && !all && a.Kgr < 32) clean_desc<32>(r);
+        uint4* prow = reinterpret_cast<uint4*>(pm + (size_t)(hs * 64 + t) * KTP);
+#pragma unroll
+        for (int c = 0; c < KT / 8; ++c) prow[c] = make_uint4(0, 0, 0, 0);
+        if (active) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (r[i] && (all || i < a.Kgr)) pm[(size_t)(hs * 64 + t) * KTP + (0xffff - (int)(r[i] & 0xffffu))] =
+                (uint16_t)(r[i] >> 16);
+        }
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        for (int i = row; i < 2 * KT; i += 128) {
+          const int hh = i / KT, j = i % KT;
+          const uint16_t* src = pm + (size_t)hh * 64 * KTP + j;  // column j: consecutive lanes, consecutive j
+          uint32_t mx = 0u, first = 0xffffffffu;
+#pragma unroll 16
+          for (int t2 = 63; t2 >= 0; --t2) {
+            const uint32_t v = src[(size_t)t2 * KTP];
+            mx = max(mx, v);
+            first = v ? (uint32_t)t2 : first;
+          }
+          ms->gpool[hh][j] = mx;
+          ms->gt0[hh][j] = mx ? first : 0xffffffffu;
+        }
+      }
+    } else if (!split && warp >= 2 && warp < 6) {
       const int quarter = warp & 3;
       const int row = quarter * 32 + lane;
       const int hs = row >> 6, t = row & 63;
@@ -546,7 +627,6 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
       const int th = 4 * ms->ksel[hs];
       const bool ok = __all_sync(0xffffffffu, mbar_wait(s2_full, 0, abort_flag, 16));
       fence_after();
-      constexpr int KT = 4 * KL;  // candidate columns per head (Kc * M <= 4 * KL)
       uint32_t r[KT];
       if (ok) {
         const uint32_t sa = tmem + lane_addr + hs * 128;
@@ -578,10 +658,8 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
       // one bitonic clean); otherwise from a radix select on the 16-bit score.
       const bool active = rvalid && nreal > 0;
       const bool all = a.Kgr >= a.Kc * M || nreal <= a.Kgr;
-      // [2][64][KTP], see below; rows padded by 16 bytes so that 16-byte stores of 32 rows spread
-      // over all banks (an unpadded row of 64 u16 puts every row at the same banks)
-      constexpr int KTP = KT + 8;
-      uint16_t* pm = reinterpret_cast<uint16_t*>(q_s);
+      // pm rows are padded by 16 bytes so that 16-byte stores of 32 rows spread over all banks (an
+      // unpadded row of 64 u16 puts every row at the same banks)
       auto put = [&](uint32_t k32) {  // record a requested key in the pooling matrix
         const int j = 0xffff - (int)(k32 & 0xffffu);
         pm[(size_t)(hs * 64 + t) * KTP + j] = (uint16_t)(k32 >> 16);
