@@ -170,7 +170,10 @@ class VramKVCacheStore(KVCacheStore):
 
     # -- KVCacheStore API -----------------------------------------------------------------------
     def reset(self) -> None:
-        self._layers.clear()
+        # the layers keep their buffers for the next sequence (no re-allocation, no zero fill: every
+        # row already holds finite values, which is all the kernels need past the valid length)
+        for st in self._layers.values():
+            st.n_closed = 0
         self.cache_hits = self.cache_misses = 0
         self.summary_hits = self.summary_misses = 0
 
