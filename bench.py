@@ -173,11 +173,13 @@ def visible_pairs(routed, S, C, kf, kl, gs):
 
 def pipelined_e2e(step_fn, x_host: torch.Tensor, out_like_host: torch.Tensor, steps: int, device) -> float:
     """End-to-end time of `steps` forwards, each with its input copied from pinned host memory and
-    its output copied back, the copies of neighbouring steps overlapping the compute on a copy
-    stream (double-buffered device inputs and pinned outputs, as a serving loop runs it).
+    its output copied back, the copies of neighbouring steps overlapping the compute
+    (double-buffered device inputs and pinned outputs, as a serving loop runs it).  Uploads and
+    downloads run on two copy streams, so the host link carries both directions at once.
     Returns milliseconds between the first upload's start and the last download's end."""
     main = torch.cuda.current_stream(device)
-    copy = torch.cuda.Stream(device)
+    copy = torch.cuda.Stream(device)   # uploads
+    down = torch.cuda.Stream(device)   # downloads
     xbuf = [torch.empty(x_host.shape, dtype=x_host.dtype, device=device) for _ in range(2)]
     obuf = [out_like_host, torch.empty_like(out_like_host).pin_memory()]
     up = [torch.cuda.Event() for _ in range(2)]
@@ -200,11 +202,11 @@ def pipelined_e2e(step_fn, x_host: torch.Tensor, out_like_host: torch.Tensor, st
         main.wait_event(up[cur])
         y = step_fn(xbuf[cur])
         used[cur].record(main)
-        y.record_stream(copy)
-        with torch.cuda.stream(copy):
-            copy.wait_event(used[cur])
+        y.record_stream(down)
+        with torch.cuda.stream(down):
+            down.wait_event(used[cur])
             obuf[cur].copy_(y, non_blocking=True)
-    e_en.record(copy)
+    e_en.record(down)
     torch.cuda.synchronize()
     return e_st.elapsed_time(e_en)
 
