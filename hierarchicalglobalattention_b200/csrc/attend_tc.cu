@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* s_full = bars + 9;    // Q.K^T of a tile is in S
   uint64_t* s_free = bars + 10;   // the softmax warps have read S (128 arrivals)
   uint64_t* p_full = bars + 11;   // P of a tile is in TMEM (128 arrivals)
+  uint64_t* table_ready = bars + 12;  // the opened units are in the table (one arrival)
   uint64_t* pv_done = bars + 13;  // one completion per P.V (its waits are never more than one phase behind)
   uint64_t* o_done = bars + 14;   // single completion after the last P.V (the epilogue's wait)
   uint64_t* drain = bars + 15;    // the MMA issuer's last commit: every MMA it issued has completed
@@ -227,8 +228,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(v_full + i, 1);
       mbar_init(v_empty + i, 1);
       mbar_init(i ? s_free : s_full, i ? 128 : 1);
-      mbar_init(p_full + i, 128);
     }
+    mbar_init(p_full, 128);
+    mbar_init(table_ready, 1);
     mbar_init(pv_done, 1);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
@@ -240,15 +242,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  // stage both heads' open lists in smem (coalesced); visible entries are a prefix of each list
-  const size_t tile0 = (((size_t)b * a.H + h0) * a.nl + ln) * a.Kg;
-  const size_t tile1 = (((size_t)b * a.H + h1) * a.nl + ln) * a.Kg;
-  for (int i = tid; i < a.Kg; i += kThreads) {
-    gidA[i] = a.open_gid[tile0 + i];
-    t0A[i] = a.open_t0[tile0 + i];
-    gidB[i] = a.open_gid[tile1 + i];
-    t0B[i] = a.open_t0[tile1 + i];
-  }
+  // the shared units (current chunk and windows) need no routing: written now, so their tiles
+  // load while the softmax warps build the rest of the table from the open lists
   for (int u = tid; u < n_shared; u += kThreads) {
     Unit e;
     if (u < 4) {
@@ -260,93 +255,113 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     units[u] = e;
   }
-  __syncthreads();
-  if (warp == 2) {
-    int la = 0, lb = 0;
-    for (int base = 0; base < a.Kg; base += 32) {
-      const int j = base + lane;
-      const bool va = j < a.Kg && gidA[j] >= 0 && t0A[j] < nvalid;
-      const bool vb = j < a.Kg && gidB[j] >= 0 && t0B[j] < nvalid;
-      la += __popc(__ballot_sync(0xffffffffu, va));
-      lb += __popc(__ballot_sync(0xffffffffu, vb));
-    }
-    if (lane == 0) { *la_s = la; *lb_s = lb; }
-  }
-  __syncthreads();
-  const int la = *la_s, lb = *lb_s;
-  // opened groups in three runs: both heads (in head 0's order), head 0 only, head 1 only.  A
-  // warp's rows belong to one head, so a run of single-head units leaves the other head's warps
-  // whole tiles with nothing visible, which they skip.
-  if (warp == 2) {
-    int both = 0;
-    for (int pass = 0; pass < 2; ++pass) {
-      int written = 0;
-      for (int base = 0; base < la; base += 32) {
-        const int j = base + lane;
-        int g = 0, t1 = 1 << 20;
-        if (j < la) {
-          g = gidA[j];
-          int lo = 0, hi = lb - 1;
-          while (lo <= hi) {
-            const int mid = (lo + hi) >> 1;
-            const int x = gidB[mid];
-            if (x == g) { t1 = t0B[mid]; break; }
-            if (x < g) lo = mid + 1; else hi = mid - 1;
-          }
-        }
-        const bool take = j < la && ((t1 < (1 << 20)) == (pass == 0));
-        const unsigned bal = __ballot_sync(0xffffffffu, take);
-        if (take) {
-          const int slot = n_shared + (pass ? both : 0) + written + __popc(bal & ((1u << lane) - 1u));
-          Unit e; e.pos = g * gs; e.tmin0 = t0A[j]; e.tmin1 = t1; e.causal = 0;
-          units[slot] = e;
-        }
-        written += __popc(bal);
-      }
-      if (pass == 0) both = written;
-    }
-  }
-  if (warp == 3) {
-    int written = 0;
-    for (int base = 0; base < lb; base += 32) {
-      const int j = base + lane;
-      bool keep = false;
-      int g = 0;
-      if (j < lb) {
-        g = gidB[j];
-        keep = true;
-        int lo = 0, hi = la - 1;
-        while (lo <= hi) {
-          const int mid = (lo + hi) >> 1;
-          const int x = gidA[mid];
-          if (x == g) { keep = false; break; }
-          if (x < g) lo = mid + 1; else hi = mid - 1;
-        }
-      }
-      const unsigned bal = __ballot_sync(0xffffffffu, keep);
-      if (keep) {
-        const int slot = n_shared + la + written + __popc(bal & ((1u << lane) - 1u));
-        Unit e; e.pos = g * gs; e.tmin0 = 1 << 20; e.tmin1 = t0B[j]; e.causal = 0;
-        units[slot] = e;
-      }
-      written += __popc(bal);
-    }
-    if (lane == 0) *n_units_s = n_shared + la + written;
-  }
-  __syncthreads();
-  const int n_units = *n_units_s;
-  const int ntiles = (n_units + kUnitsPerTile - 1) / kUnitsPerTile;
-  // pad the last tile with never-visible copies of unit 0 (finite data, zero probability)
-  for (int u = n_units + tid; u < ntiles * kUnitsPerTile; u += kThreads) {
-    Unit e = units[0]; e.tmin0 = e.tmin1 = 1 << 20; e.causal = 0;
-    units[u] = e;
-  }
   fence_before();
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_base_s;
-
+  const int ns_tiles = n_shared / kUnitsPerTile;  // n_shared is a multiple of 4
+  // number of tiles, read once the table is complete (the producer and the MMA issuer wait for it
+  // only when they pass the shared tiles)
+  auto table_tiles = [&]() { return (*n_units_s + kUnitsPerTile - 1) / kUnitsPerTile; };
   unsigned char* q_s = smem + SmemLayout::kQ;
+  if (warp >= 2) {
+    // stage both heads' open lists in smem (coalesced); visible entries are a prefix of each list
+    const int st_tid = tid - 64;
+    const size_t tile0 = (((size_t)b * a.H + h0) * a.nl + ln) * a.Kg;
+    const size_t tile1 = (((size_t)b * a.H + h1) * a.nl + ln) * a.Kg;
+    for (int i = st_tid; i < a.Kg; i += 128) {
+      gidA[i] = a.open_gid[tile0 + i];
+      t0A[i] = a.open_t0[tile0 + i];
+      gidB[i] = a.open_gid[tile1 + i];
+      t0B[i] = a.open_t0[tile1 + i];
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (warp == 2) {
+      int la = 0, lb = 0;
+      for (int base = 0; base < a.Kg; base += 32) {
+        const int j = base + lane;
+        const bool va = j < a.Kg && gidA[j] >= 0 && t0A[j] < nvalid;
+        const bool vb = j < a.Kg && gidB[j] >= 0 && t0B[j] < nvalid;
+        la += __popc(__ballot_sync(0xffffffffu, va));
+        lb += __popc(__ballot_sync(0xffffffffu, vb));
+      }
+      if (lane == 0) { *la_s = la; *lb_s = lb; }
+    }
+    if (warp <= 3) {
+      asm volatile("bar.sync 2, 64;" ::: "memory");
+      const int la = *la_s, lb = *lb_s;
+    // opened groups in three runs: both heads (in head 0's order), head 0 only, head 1 only.  A
+    // warp's rows belong to one head, so a run of single-head units leaves the other head's warps
+    // whole tiles with nothing visible, which they skip.
+    if (warp == 2) {
+      int both = 0;
+      for (int pass = 0; pass < 2; ++pass) {
+        int written = 0;
+        for (int base = 0; base < la; base += 32) {
+          const int j = base + lane;
+          int g = 0, t1 = 1 << 20;
+          if (j < la) {
+            g = gidA[j];
+            int lo = 0, hi = lb - 1;
+            while (lo <= hi) {
+              const int mid = (lo + hi) >> 1;
+              const int x = gidB[mid];
+              if (x == g) { t1 = t0B[mid]; break; }
+              if (x < g) lo = mid + 1; else hi = mid - 1;
+            }
+          }
+          const bool take = j < la && ((t1 < (1 << 20)) == (pass == 0));
+          const unsigned bal = __ballot_sync(0xffffffffu, take);
+          if (take) {
+            const int slot = n_shared + (pass ? both : 0) + written + __popc(bal & ((1u << lane) - 1u));
+            Unit e; e.pos = g * gs; e.tmin0 = t0A[j]; e.tmin1 = t1; e.causal = 0;
+            units[slot] = e;
+          }
+          written += __popc(bal);
+        }
+        if (pass == 0) both = written;
+      }
+    }
+    if (warp == 3) {
+      int written = 0;
+      for (int base = 0; base < lb; base += 32) {
+        const int j = base + lane;
+        bool keep = false;
+        int g = 0;
+        if (j < lb) {
+          g = gidB[j];
+          keep = true;
+          int lo = 0, hi = la - 1;
+          while (lo <= hi) {
+            const int mid = (lo + hi) >> 1;
+            const int x = gidA[mid];
+            if (x == g) { keep = false; break; }
+            if (x < g) lo = mid + 1; else hi = mid - 1;
+          }
+        }
+        const unsigned bal = __ballot_sync(0xffffffffu, keep);
+        if (keep) {
+          const int slot = n_shared + la + written + __popc(bal & ((1u << lane) - 1u));
+          Unit e; e.pos = g * gs; e.tmin0 = 1 << 20; e.tmin1 = t0B[j]; e.causal = 0;
+          units[slot] = e;
+        }
+        written += __popc(bal);
+      }
+      if (lane == 0) *n_units_s = n_shared + la + written;
+    }
+      asm volatile("bar.sync 2, 64;" ::: "memory");  // warp 2's units are written
+      if (warp == 3) {
+        // pad the last tile with never-visible copies of unit 0 (finite data, zero probability)
+        const int nu = *n_units_s, nt = (nu + kUnitsPerTile - 1) / kUnitsPerTile;
+        for (int u = nu + lane; u < nt * kUnitsPerTile; u += 32) {
+          Unit e = units[0]; e.tmin0 = e.tmin1 = 1 << 20; e.causal = 0;
+          units[u] = e;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(table_ready);
+      }
+    }
+  }
   if (warp == 0) {
     // ------------------------------- TMA producer -------------------------------------------
     // The whole warp runs the loop: lane 0 arms the barriers, lanes 0-7 issue a tile's eight 2 KB
@@ -364,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // K of tile i+1 is issued before V of tile i: Q.K^T(i-1), which frees K's stage, completes
     // before P.V(i-2), which frees V's
     int armed_k0 = 0, armed_k1 = 0, armed_v0 = 0, armed_v1 = 0;  // loads issued per kind and stage: the drain's phases
-    const bool skip_k1 = a.fault == 1 && blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && blockIdx.z == 0 && ntiles > 2;
+    const bool skip_k1 = a.fault == 1 && blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && blockIdx.z == 0 && ns_tiles > 2;
     auto load = [&](int i, bool is_v) -> bool {
       const int st = i & 1;
       if (skip_k1 && !is_v && i == 1) return true;  // test-only fault: tile 1's K never arrives
@@ -389,10 +404,21 @@ __global__ void __launch_bounds__(kThreads, 2)
       else (st ? armed_k1 : armed_k0) += 1;
       return true;
     };
-    bool go = ntiles > 0 && load(0, false);
-    for (int i = 0; go && i < ntiles; ++i) {
-      if (i + 1 < ntiles) go = load(i + 1, false);
+    int nt = -1;  // tiles of the whole table, known once it is complete
+    auto has_tile = [&](int i) -> bool {  // false past the last tile, or when the wait for the table gave up
+      if (i < ns_tiles) return true;
+      if (nt < 0) {
+        if (!__all_sync(0xffffffffu, mbar_wait(table_ready, 0, abort_flag, 11, a.wait_ns))) return false;
+        nt = table_tiles();
+      }
+      return i < nt;
+    };
+    bool go = load(0, false);  // tile 0 (the current chunk) always exists
+    for (int i = 0; go; ++i) {
+      const bool more = has_tile(i + 1);
+      if (more) go = load(i + 1, false);
       if (go) go = load(i, true);
+      if (!more) break;
     }
     // drain: a CTA that gives up must not release its shared memory under loads still in flight
     if (lane == 0)
@@ -410,8 +436,17 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t q_addr = smem_u32(q_s);
       bool ok = mbar_wait(q_full, 0, abort_flag, 2, a.wait_ns);
       fence_after();
-      for (int i = 0; ok && i <= ntiles; ++i) {
-        if (i < ntiles) {
+      int nt = -1;  // tiles of the whole table, known once it is complete
+      for (int i = 0; ok; ++i) {
+        bool si = i < ns_tiles;
+        if (!si) {
+          if (nt < 0) {
+            if (!mbar_wait(table_ready, 0, abort_flag, 11, a.wait_ns)) break;
+            nt = table_tiles();
+          }
+          si = i < nt;
+        }
+        if (si) {
           const int st = i & 1;
           if (!mbar_wait(k_full + st, (i >> 1) & 1, abort_flag, 3, a.wait_ns)) break;
           // S is free once the softmax warps have read the previous tile's scores
@@ -438,8 +473,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                    (j > 0 || kk > 0) ? 1u : 0u);
           mma_commit(pv_done);
           mma_commit(v_empty + st);
-          if (j == ntiles - 1) mma_commit(o_done);
+          if (!si) mma_commit(o_done);  // P.V of the last tile
         }
+        if (!si) break;
       }
       // drain: wait until every MMA this thread issued has completed (it reads smem and TMEM that
       // are released below), also when the loop was left on a timeout
@@ -458,7 +494,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     const float sl2 = a.scale_log2;
     float m_run = -INFINITY;  // running max in the scaled log2 domain
     float l_run = 0.f;
-    bool ok = true;
+    // the table (built by warps 2 and 3) gives the tile count
+    bool ok = __all_sync(0xffffffffu, mbar_wait(table_ready, 0, abort_flag, 11, a.wait_ns));
+    const int ntiles = ok ? table_tiles() : 0;
     for (int i = 0; i < ntiles && ok; ++i) {
       // visibility of the tile's units for this row: a visible prefix of cnt[u] keys (the causal
       // current-chunk tile, i == 0) or all / none of them; `live` marks the units some row of this
