@@ -100,3 +100,35 @@ def test_module_qwen_shape_bf16_sparse_vs_oracle(cuda, S):
     frac_bad = (row_err > 0.05).float().mean().item()
     mean_rel = (d.sum() / ref.float().abs().sum()).item()
     assert frac_bad < 0.05 and mean_rel < 2e-2, (frac_bad, mean_rel, row_err.max().item())
+
+
+@pytest.mark.parametrize("tier", ["vram", "ram"])
+def test_store_reuse_across_sequences(cuda, tier):
+    """A store reset keeps its buffers (no re-allocation or zero fill): a longer sequence, then a
+    shorter one, then a prefill followed by decode blocks, give the outputs of fresh modules."""
+    import hierarchicalglobalattention_b200 as hga
+    torch.manual_seed(3)
+    kw = dict(d_model=512, nhead=8, kv_heads=2, head_dim=64, chunk_size=64, group_size=16, topk_chunks=4,
+              topk_groups=8, keep_first=1, keep_last=2, theta=1e4, cache_location=tier)
+    m = hga.HierarchicalGlobalAttentionRouted(**kw).to(cuda).to(torch.bfloat16)
+    xs = [torch.randn(1, S, 512, device=cuda, dtype=torch.bfloat16) for S in (1500, 700)]
+
+    def fresh(x):
+        f = hga.HierarchicalGlobalAttentionRouted(**kw).to(cuda).to(torch.bfloat16)
+        f.load_state_dict(m.state_dict())
+        return f(x)[0]
+
+    with torch.no_grad():
+        for x in xs:
+            assert torch.equal(m(x)[0], fresh(x))
+        # prefill 640 tokens, then 3-token blocks on the reused store, against a fresh module
+        x = torch.randn(1, 700, 512, device=cuda, dtype=torch.bfloat16)
+        f = hga.HierarchicalGlobalAttentionRouted(**kw).to(cuda).to(torch.bfloat16)
+        f.load_state_dict(m.state_dict())
+        outs = []
+        for mod in (m, f):
+            o = [mod(x[:, :640], cache_position=torch.arange(640, device=cuda))[0]]
+            for s in range(640, 700, 3):
+                o.append(mod(x[:, s:s + 3], cache_position=torch.arange(s, s + 3, device=cuda))[0])
+            outs.append(torch.cat(o, dim=1))
+        assert torch.equal(outs[0], outs[1])
