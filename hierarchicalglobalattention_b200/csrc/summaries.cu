@@ -167,7 +167,7 @@ namespace hga {
 // rotated and written (16-byte stores).  bf16 / fp16, head_dim 64 or 128, chunk and group sizes
 // multiples of 16, chunk_size <= 128.
 template <typename T, int DH>
-__global__ void __launch_bounds__(256) summaries_dual_kernel(
+__global__ void __launch_bounds__(256, 4) summaries_dual_kernel(
     hga_params p, int64_t S, int64_t pos0, const T* __restrict__ k_raw, const T* __restrict__ k_rope,
     const T* __restrict__ v, int64_t kv_cap, int N, int cpb,
     const float* __restrict__ cosA, const float* __restrict__ sinA, int64_t rowA0, int roundA, T* ckA, T* gkA,
@@ -195,14 +195,15 @@ __global__ void __launch_bounds__(256) summaries_dual_kernel(
 #pragma unroll
     for (int e = 0; e < 8; ++e) sr[e] = so[e] = sv[e] = 0.f;
     const int t0 = blk * 16;
-    // eight rows' loads (24 x 16 bytes) in flight before they are added, in row order; rows past
-    // the sequence load the chunk's first row (in bounds) and are not added
+    // four rows' loads (12 x 16 bytes) in flight before they are added, in row order (few
+    // registers: four CTAs per SM hold the whole grid in one wave); rows past the sequence load
+    // the chunk's first row (in bounds) and are not added
 #pragma unroll
-    for (int u0 = 0; u0 < 16; u0 += 8) {
+    for (int u0 = 0; u0 < 16; u0 += 4) {
       if (t0 + u0 >= len) break;
-      uint4 ur[8], uo[8], uv[8];
+      uint4 ur[4], uo[4], uv[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < 4; ++u) {
         const int t = t0 + u0 + u;
         const size_t off = base + (size_t)(row0 + (t < len ? t : 0)) * DH;
         ur[u] = __ldg(reinterpret_cast<const uint4*>(k_raw + off));
@@ -210,7 +211,7 @@ __global__ void __launch_bounds__(256) summaries_dual_kernel(
         uv[u] = __ldg(reinterpret_cast<const uint4*>(v + off));
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < 4; ++u) {
         if (t0 + u0 + u >= len) break;
         const T* hr = reinterpret_cast<const T*>(&ur[u]);
         const T* ho = reinterpret_cast<const T*>(&uo[u]);
