@@ -169,6 +169,52 @@ __device__ uint32_t warp_topk_small(const uint32_t* keys, int n, int k, unsigned
   return last;
 }
 
+// Chunk choice of one head for pools of at most 512 chunks, all in registers: lane l holds the
+// pooled keys of chunks l + 32m (score << 16 | 0xffff - c, 0 = not requested), the k largest are
+// chosen by k rounds of warp max-reductions over per-lane sorted copies, then chunk `pr` (the
+// previous chunk, -1 if outside the pool) is forced in, replacing the lowest-ranked choice when k
+// are chosen.  Returns the lane's chosen chunks as a bit mask over m.
+__device__ uint32_t warp_choose_small(const uint32_t* pooled, int npool, int k, int pr) {
+  const int lane = threadIdx.x & 31;
+  uint32_t v[16], w[16];
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    const int c = lane + 32 * m;
+    const uint32_t raw = c < npool ? pooled[c] : 0u;
+    v[m] = raw ? ((raw << 16) | (0xffffu - (uint32_t)c)) : 0u;
+    w[m] = v[m];
+  }
+  sort_desc<16>(w);
+  uint32_t last = 0u;
+  for (int it = 0; it < k; ++it) {
+    const uint32_t best = __reduce_max_sync(0xffffffffu, w[0]);
+    if (best == 0u) break;
+    last = best;
+    if (w[0] == best) {  // keys are unique: exactly one lane pops
+#pragma unroll
+      for (int m = 0; m < 15; ++m) w[m] = w[m + 1];
+      w[15] = 0u;
+    }
+  }
+  uint32_t mask = 0u;
+#pragma unroll
+  for (int m = 0; m < 16; ++m) mask |= (v[m] != 0u && v[m] >= last ? 1u : 0u) << m;
+  if (pr >= 0) {
+    const bool mine = (pr & 31) == lane;
+    const bool pr_sel = __shfl_sync(0xffffffffu, (mask >> (pr >> 5)) & 1u, pr & 31) != 0u;
+    if (!pr_sel) {
+      const int nsel = __reduce_add_sync(0xffffffffu, __popc(mask));
+      if (nsel >= k) {  // drop the lowest-ranked choice: the k-th key, `last`
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+          if (v[m] == last) mask &= ~(1u << m);
+      }
+      if (mine) mask |= 1u << (pr >> 5);
+    }
+  }
+  return mask;
+}
+
 // Warp-wide radix select over keys[0..n) (unique 32-bit keys, 0 = absent): flags the k largest.
 // Keys are cached in registers (up to 64 per lane, n <= 2048); larger n streams from smem.
 __device__ void warp_select_u32(const uint32_t* keys, int n, int k, unsigned char* flag) {
@@ -444,12 +490,33 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
     const int hs = warp - 2;
     uint32_t* keys = pooled + hs * NP;
     unsigned char* fl = flags + hs * NP;
-    for (int c = lane; c < npool; c += 32) keys[c] = keys[c] ? ((keys[c] << 16) | (0xffffu - c)) : 0u;
-    __syncwarp();
-    if (npool <= 512) warp_topk_small(keys, npool, a.Kc, fl);
-    else warp_select_u32(keys, npool, a.Kc, fl);
     const int prev = n - 1;
     const bool prev_in = n > 0 && prev >= pool_lo && prev < l_lo;
+    if (npool <= 512) {
+      // registers only: choose, force the previous chunk, write the chosen list in chunk order
+      const uint32_t mask = warp_choose_small(keys, npool, a.Kc, prev_in ? prev - pool_lo : -1);
+      int k = 0;
+      const size_t o = (hs ? out1 : out0) * a.Kc;
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        const int c = lane + 32 * m;
+        const bool s = (mask >> m) & 1u;
+        const unsigned bal = __ballot_sync(0xffffffffu, s);
+        if (s) {
+          const int slot = k + __popc(bal & ((1u << lane) - 1u));
+          const int t0 = (prev_in && c == prev - pool_lo) ? 0 : (int)t0c[hs * NP + c];
+          ms->sel[hs][slot] = pool_lo + c;
+          ms->selt0[hs][slot] = t0;
+          a.sel_chunk[o + slot] = pool_lo + c;
+          a.sel_t0[o + slot] = t0;
+        }
+        k += __popc(bal);
+      }
+      if (lane == 0) ms->ksel[hs] = k;
+    } else {
+    for (int c = lane; c < npool; c += 32) keys[c] = keys[c] ? ((keys[c] << 16) | (0xffffu - c)) : 0u;
+    __syncwarp();
+    warp_select_u32(keys, npool, a.Kc, fl);
     if (prev_in) {
       const int pr = prev - pool_lo;
       int nsel = 0;
@@ -488,6 +555,7 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
       k += __popc(bal);
     }
     if (lane == 0) ms->ksel[hs] = k;
+    }
   }
   __syncthreads();
   const bool do_l2 = a.Kg > 0 && a.Kgr > 0 && !ms->abort;
