@@ -440,34 +440,11 @@ __global__ void __launch_bounds__(threads_for<KL>(), 2)
       }
       asm volatile("bar.sync 1, %0;" ::"r"(32 * kRowWarps) : "memory");
       if (half == 0) {
-        uint32_t mask = 0u;
-        const uint32_t thr = lst[KL - 1];
-        uint32_t other[KL];
+        // both lists are sorted descending: the top KL of their union is the bitonic max of one
+        // against the other reversed, sorted by one clean
 #pragma unroll
-        for (int j = 0; j < KL; ++j) {
-          other[j] = mbuf[j * 128 + row];
-          mask |= (other[j] > thr ? 1u : 0u) << j;
-        }
-        const int rounds = __reduce_max_sync(0xffffffffu, __popc(mask));
-        for (int it = 0; it < rounds; ++it) {
-          uint32_t x = 0u;
-          if (mask) {
-            const int c0 = __ffs(mask) - 1;
-            mask &= mask - 1u;
-#pragma unroll
-            for (int j = 0; j < KL; ++j) x = j == c0 ? other[j] : x;
-          }
-          if (x > lst[KL - 1]) {
-            uint32_t nl[KL];
-#pragma unroll
-            for (int j = 0; j < KL; ++j) {
-              const uint32_t prev_j = j == 0 ? 0xffffffffu : lst[j - 1];
-              nl[j] = lst[j] > x ? lst[j] : (prev_j > x ? x : prev_j);
-            }
-#pragma unroll
-            for (int j = 0; j < KL; ++j) lst[j] = nl[j];
-          }
-        }
+        for (int j = 0; j < KL; ++j) lst[j] = max(lst[j], mbuf[(KL - 1 - j) * 128 + row]);
+        clean_desc<KL>(lst);
       }
     }
     // requests = top k1 of the row's list -> pooled max score and first requesting row per chunk
