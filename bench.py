@@ -11,6 +11,7 @@ Prints ONE JSON line (rank 0): the prefill line, plus `decode` and 
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -171,6 +172,23 @@ def visible_pairs(routed, S, C, kf, kl, gs):
     return int(pairs)
 
 
+@contextlib.contextmanager
+def near_gpu(device):
+    """Run the block on the CPUs of the GPU's NUMA node (sysfs local_cpulist), so that pinned host
+    buffers allocated in it are placed on that node and the host-link copies stay node-local; the
+    process's affinity is restored afterwards."""
+    from hierarchicalglobalattention_b200.decode_shard import gpu_local_cpus
+    saved = os.sched_getaffinity(0)
+    cpus = gpu_local_cpus(device) if device.type == "cuda" else None
+    cpus = (cpus & saved) if cpus else None
+    try:
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        yield
+    finally:
+        os.sched_setaffinity(0, saved)
+
+
 def pipelined_e2e(step_fn, x_host: torch.Tensor, out_like_host: torch.Tensor, steps: int, device) -> float:
     """End-to-end time of `steps` forwards, each with its input copied from pinned host memory and
     its output copied back, the copies of neighbouring steps overlapping the compute
@@ -181,7 +199,8 @@ def pipelined_e2e(step_fn, x_host: torch.Tensor, out_like_host: torch.Tensor, st
     copy = torch.cuda.Stream(device)   # uploads
     down = torch.cuda.Stream(device)   # downloads
     xbuf = [torch.empty(x_host.shape, dtype=x_host.dtype, device=device) for _ in range(2)]
-    obuf = [out_like_host, torch.empty_like(out_like_host).pin_memory()]
+    with near_gpu(device):
+        obuf = [out_like_host, torch.empty_like(out_like_host).pin_memory()]
     up = [torch.cuda.Event() for _ in range(2)]
     used = [torch.cuda.Event() for _ in range(2)]
     e_st, e_en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -218,9 +237,10 @@ def run_ours(args, rank, world, device):
     S = args.seq
     m = build_module(device, dtype)
     g = torch.Generator(device="cpu").manual_seed(1234 + rank)
-    x_host = torch.randn(1, S, CFG1["d_model"], generator=g).to(dtype).pin_memory()
+    with near_gpu(device):  # the step's pinned input and output on the GPU's NUMA node
+        x_host = torch.randn(1, S, CFG1["d_model"], generator=g).to(dtype).pin_memory()
+        out_host = torch.empty(1, S, CFG1["d_model"], dtype=dtype).pin_memory()
     x = x_host.to(device)
-    out_host = torch.empty(1, S, CFG1["d_model"], dtype=dtype).pin_memory()
 
     # instrument the attention launch with CUDA events on its stream
     att_events = []
@@ -283,12 +303,13 @@ def run_sharded(args, rank, world, device, S=None, cfg=None, steps=None, warmup=
     m = build_module(device, dtype, cfg=cfg)
     g = torch.Generator(device="cpu").manual_seed(1234)
     x_full = torch.randn(1, S, CFG1["d_model"], generator=g).to(dtype)
-    x_host = torch.cat([x_full[:, lo:hi] for lo, hi in rank_rows(S, CFG1["chunk_size"], world, rank)],
-                       dim=1).contiguous().pin_memory()
+    with near_gpu(device):  # the rank's pinned input and output on its GPU's NUMA node
+        x_host = torch.cat([x_full[:, lo:hi] for lo, hi in rank_rows(S, CFG1["chunk_size"], world, rank)],
+                           dim=1).contiguous().pin_memory()
+        out_host = torch.empty(1, x_host.shape[1], CFG1["d_model"], dtype=dtype).pin_memory()
     del x_full
     x = x_host.to(device)
     sp = ShardedPrefill(world, rank)
-    out_host = torch.empty(1, x_host.shape[1], CFG1["d_model"], dtype=dtype).pin_memory()
     with torch.no_grad():
         for _ in range(warmup):
             sp.forward(m, x, S)
