@@ -15,6 +15,8 @@
 // One warp per (token, projected head row); the row is staged in smem for the rotate-half partner.
 #include "hga_common.cuh"
 
+#include <type_traits>
+
 namespace hga {
 
 constexpr int kProWarps = 8;
@@ -187,6 +189,37 @@ __global__ void __launch_bounds__(kProWarps * 32) prologue_vec_kernel(
 // shuffle), but the rotary table entries of the position are read once per token (they depend on
 // the position and the column only) instead of once per head row, four rows' loads are issued
 // before any of them is used, and the row index needs no 64-bit division.  V rows are copied.
+// bf16 pairs on sm_100: two fp32 products / sums in one instruction (each rounded like its scalar
+// form), two roundings to bf16 in one conversion
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf2(uint64_t v) {  // round both to bf16, lo in bits 0-15
+  float lo, hi;
+  upk2(v, lo, hi);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint64_t unbf2(uint32_t w) {  // bf16 pair back to fp32
+  return pk2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
 template <typename T, int EPL>
 __global__ void __launch_bounds__(kProWarps * 32, 4) prologue_tok_kernel(
     hga_params p, int64_t S, const T* __restrict__ qkv, int64_t row_stride, const T* __restrict__ qw,
@@ -247,23 +280,53 @@ __global__ void __launch_bounds__(kProWarps * 32, 4) prologue_tok_kernel(
         // correctly rounded quotient
         const float mean = __fmul_rn(ss, 1.f / (float)Dh);
         const float rs = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, eps)));
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+          const uint64_t r2 = pk2(rs, rs);
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) {
-          const float wf = is_q ? wq[e] : wk[e];
-          x[e] = norm_mode == 0 ? Num<T>::round(__fmul_rn(__fmul_rn(wf, x[e]), rs))
-                                : Num<T>::round(__fmul_rn(wf, Num<T>::round(__fmul_rn(x[e], rs))));
+          for (int e = 0; e < EPL; e += 2) {
+            const uint64_t wv = is_q ? pk2(wq[e], wq[e + 1]) : pk2(wk[e], wk[e + 1]);
+            const uint64_t xv = pk2(x[e], x[e + 1]);
+            const uint64_t y = norm_mode == 0 ? mul2(mul2(wv, xv), r2) : mul2(wv, unbf2(bf2(mul2(xv, r2))));
+            upk2(unbf2(bf2(y)), x[e], x[e + 1]);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            const float wf = is_q ? wq[e] : wk[e];
+            x[e] = norm_mode == 0 ? Num<T>::round(__fmul_rn(__fmul_rn(wf, x[e]), rs))
+                                  : Num<T>::round(__fmul_rn(wf, Num<T>::round(__fmul_rn(x[e], rs))));
+          }
         }
       }
       T yo[EPL], xo[EPL];
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        // pairs: x is bf16-exact here, so its packed form is the k_raw row and the shuffled partner
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) {
-        const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
-        const float xp = lane < 16 ? -other : other;
-        float y;
-        if (rope_mode == 0) y = __fadd_rn(__fmul_rn(x[e], cs[e]), __fmul_rn(xp, sn[e]));
-        else y = __fadd_rn(Num<T>::round(__fmul_rn(x[e], cs[e])), Num<T>::round(__fmul_rn(xp, sn[e])));
-        yo[e] = Num<T>::from_f(y);
-        xo[e] = Num<T>::from_f(x[e]);
+        for (int e = 0; e < EPL; e += 2) {
+          uint32_t xb;
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(xb) : "f"(x[e + 1]), "f"(x[e]));
+          const uint32_t ob = __shfl_xor_sync(0xffffffffu, xb, 16);
+          float o0, o1;
+          upk2(unbf2(ob), o0, o1);
+          const uint64_t xv = pk2(x[e], x[e + 1]);
+          const uint64_t xp = lane < 16 ? pk2(-o0, -o1) : pk2(o0, o1);
+          const uint64_t cv = pk2(cs[e], cs[e + 1]), sv = pk2(sn[e], sn[e + 1]);
+          const uint32_t yb = rope_mode == 0 ? bf2(add2(mul2(xv, cv), mul2(xp, sv)))
+                                             : bf2(add2(unbf2(bf2(mul2(xv, cv))), unbf2(bf2(mul2(xp, sv)))));
+          memcpy(&yo[e], &yb, 4);
+          memcpy(&xo[e], &xb, 4);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
+          const float xp = lane < 16 ? -other : other;
+          float y;
+          if (rope_mode == 0) y = __fadd_rn(__fmul_rn(x[e], cs[e]), __fmul_rn(xp, sn[e]));
+          else y = __fadd_rn(Num<T>::round(__fmul_rn(x[e], cs[e])), Num<T>::round(__fmul_rn(xp, sn[e])));
+          yo[e] = Num<T>::from_f(y);
+          xo[e] = Num<T>::from_f(x[e]);
+        }
       }
       if (is_q) {
         st_vec<T, EPL>(q_out + (bt * H + r) * Dh + d0, yo);
