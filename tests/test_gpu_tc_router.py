@@ -15,6 +15,8 @@ CASES = [
     (1000, 2, 8, 2, 0, 0, 3, 6, 0),        # prev forcing, ragged tail, Kg < Kc*M (pooled group choice)
     (8192, 1, 8, 2, 2, 8, 32, 128, 1),     # configs[3] routing parameters (Kc 32, Kg_request 64)
     (300, 1, 2, 1, 1, 1, 20, 32, 1),       # Kc > pool for early chunks
+    (2048, 1, 8, 2, 1, 4, 16, 100, 1),     # top-16 lists with 50 requests of 64: one thread per row, radix select
+    (1500, 1, 4, 1, 1, 2, 4, 64, 1),       # requests cover every candidate (Kg_request >= Kc * M)
 ]
 
 
