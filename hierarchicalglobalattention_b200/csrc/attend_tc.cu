@@ -23,6 +23,9 @@
 //                   take a max pass (and a lazy O rescale) only when a p could exceed 2^8.  Units
 //                   that no row of a warp sees are neither loaded from TMEM nor exponentiated.
 //                   TMEM loads/stores are warp-collective, so these decisions are per warp.
+// Set-up: the shared units (current chunk, windows) need no routing and are written first, so
+// their tiles load and score while warps 2-3 build the opened part of the unit table from the
+// two heads' lists; the producer and MMA warps wait for the table only past the shared tiles.
 // ~105 KB smem and 256 TMEM columns per CTA, so two CTAs share an SM and hide each other's
 // serial phases.  Every mbarrier wait is bounded; on timeout the CTA records an error code
 // (hga_device_status), lets its copies and MMAs in flight land (bounded), releases its TMEM and
@@ -32,7 +35,7 @@
 namespace hga {
 namespace tc {
 
-constexpr int kThreads = 192;  // warp0 TMA, warp1 MMA, warps2-5 softmax/epilogue
+constexpr int kThreads = 192;  // warp0 TMA, warp1 MMA, warps2-5 unit table (2-3), softmax, epilogue
 constexpr int kUnitsPerTile = 4;
 constexpr int kMaxUnits = 328;  // current 4 + windows <= 64 + opened union <= 256, rounded up to whole tiles
 constexpr int kMaxKg = 128;
