@@ -274,11 +274,19 @@ template <> struct VCols<64> { using type = uint32_t; };
 constexpr int kAttWarps = 8;
 constexpr int kUnit = 16;  // tokens per unit (the routing group)
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 template <typename T, int DH, int LM>
 __global__ void __launch_bounds__(kAttWarps * 32, (LM == 1 ? 2 : 1)) attend_decode_fast_kernel(
     hga_params p, int L, const T* __restrict__ q, const int32_t* __restrict__ seq_pos, const T* hot_k, const T* hot_v,
     int64_t hot_cap, int hot_mode, const T* cold_k, const T* cold_v, int64_t cold_cap,
-    const int32_t* __restrict__ open_gid, const int32_t* __restrict__ open_t0, int Kg, T* __restrict__ out) {
+    const int32_t* __restrict__ open_gid, const int32_t* __restrict__ open_t0, int Kg, int cold_direct,
+    T* __restrict__ out) {
   static_assert(sizeof(T) == 2, "16-bit K/V only");
   constexpr int HALF = DH / 2;
   constexpr int KLD = HALF / 8;   // 16-byte loads per lane for its half key row
@@ -293,6 +301,11 @@ __global__ void __launch_bounds__(kAttWarps * 32, (LM == 1 ? 2 : 1)) attend_deco
   float* sm = so + kAttWarps * LM * DH;                   // [warps][LM]
   float* sl = sm + kAttWarps * LM;                        // [warps][LM]
   unsigned char* kst = (unsigned char*)(sl + kAttWarps * LM) + (size_t)(threadIdx.x >> 5) * kUnit * RS;
+  // per warp: the V rows of the unit in flight [16][DH], then the CTA's copy of the open lists
+  unsigned char* vst = (unsigned char*)(sl + kAttWarps * LM) + (size_t)kAttWarps * kUnit * RS +
+                       (size_t)(threadIdx.x >> 5) * kUnit * DH * 2;
+  int32_t* lgid = (int32_t*)((unsigned char*)(sl + kAttWarps * LM) + (size_t)kAttWarps * kUnit * (RS + DH * 2));
+  int32_t* lt0 = lgid + Kg;
 
   const int h = blockIdx.x, b = blockIdx.y;
   const int H = p.nhead, KVH = p.kv_heads, C = p.chunk_size, M = C / kUnit;
@@ -312,10 +325,15 @@ __global__ void __launch_bounds__(kAttWarps * 32, (LM == 1 ? 2 : 1)) attend_deco
   }
 
   // the opened entries are a prefix of the list (entries that no row sees are not written)
+  for (int j = tid; j < Kg; j += blockDim.x) {
+    lgid[j] = open_gid[bh * Kg + j];
+    lt0[j] = open_t0[bh * Kg + j];
+  }
+  __syncthreads();
   int nopen = 0;
   for (int base = 0; base < Kg; base += 32) {
     const int j = base + lane;
-    const bool ok = j < Kg && open_gid[bh * Kg + j] >= 0 && open_t0[bh * Kg + j] >= 0;
+    const bool ok = j < Kg && lgid[j] >= 0 && lt0[j] >= 0;
     nopen += __popc(__ballot_sync(0xffffffffu, ok));
   }
   const int nfirst_u = f_hi * M, nlast_u = (n_closed - l_lo) * M;
@@ -338,55 +356,100 @@ __global__ void __launch_bounds__(kAttWarps * 32, (LM == 1 ? 2 : 1)) attend_deco
   const size_t cold_base = ((size_t)b * KVH + kvh) * cold_cap;
   const int key = lane >> 1, half = lane & 1;
 
-  for (int u = warp; u < U; u += kAttWarps) {
-    const T* kb;
-    const T* vb;
-    int64_t row;
-    int t0 = 0, act0 = -1;
+  // unit u -> its first row, K/V base, first visible row t0 and active-chunk offset (ok = false:
+  // an opened group past the record, reported and skipped); direct = read with plain loads when it
+  // is scored (opened groups in host memory: asynchronous copies from there are much slower)
+  auto unit_at = [&](int u, int64_t& row, const T*& kb, const T*& vb, int& t0, int& act0, bool& direct) -> bool {
+    t0 = 0;
+    act0 = -1;
+    direct = false;
+    kb = hot_k; vb = hot_v;
     if (u < nfirst_u) {
       row = hot_base + slot_row(u / M, (u % M) * kUnit, C, hot_mode, kf, kl, false);
-      kb = hot_k; vb = hot_v;
     } else if (u < nfirst_u + nlast_u) {
       const int uu = u - nfirst_u;
       row = hot_base + slot_row(l_lo + uu / M, (uu % M) * kUnit, C, hot_mode, kf, kl, false);
-      kb = hot_k; vb = hot_v;
     } else if (u < nfirst_u + nlast_u + nopen) {
       const int j = u - nfirst_u - nlast_u;
-      const int gid = open_gid[bh * Kg + j];
-      if ((int64_t)(gid + 1) * kUnit > cold_cap) {  // warp-uniform
-        if (lane == 0) atomicCAS(&g_decode_fast_error, 0, kErrBoundsAttendDecode);
-        continue;
-      }
+      const int gid = lgid[j];
+      if ((int64_t)(gid + 1) * kUnit > cold_cap) return false;
       row = cold_base + (int64_t)gid * kUnit;
-      t0 = open_t0[bh * Kg + j];
+      t0 = lt0[j];
       kb = cold_k; vb = cold_v;
+      direct = cold_direct != 0;
     } else {
       act0 = (u - nfirst_u - nlast_u - nopen) * kUnit;
       row = hot_base + slot_row(n_closed, act0, C, hot_mode, kf, kl, true);
-      kb = hot_k; vb = hot_v;
     }
-    // K: the unit's 16 rows are one contiguous block; lanes read consecutive 16-byte pieces (whole
-    // lines per instruction, which matters most for rows in host memory) and stage them in shared
-    // memory, from which each lane pair reads its key.
-    uint4 kr[KLD];
+    return true;
+  };
+  // K rows land in the lane-pair staging layout, V rows contiguously; one commit group per unit
+  auto issue = [&](int64_t row, const T* kb, const T* vb) {
     const uint4* kp = reinterpret_cast<const uint4*>(kb + row * DH);
-#pragma unroll
-    for (int i = 0; i < KLD; ++i) kr[i] = kp[i * 32 + lane];
-    VT vr[kUnit];
-    const T* vp = vb + row * DH + lane * VD;
-#pragma unroll
-    for (int j = 0; j < kUnit; ++j) vr[j] = *reinterpret_cast<const VT*>(vp + (size_t)j * DH);
-    __syncwarp();
+    const uint4* vp = reinterpret_cast<const uint4*>(vb + row * DH);
 #pragma unroll
     for (int i = 0; i < KLD; ++i) {
       const int c = i * 32 + lane;
       const int w = (c % CPK) * 16;
-      *reinterpret_cast<uint4*>(kst + (c / CPK) * RS + w + (w >= HALF * 2 ? 16 : 0)) = kr[i];
+      cp_async16(kst + (c / CPK) * RS + w + (w >= HALF * 2 ? 16 : 0), kp + c);
+      cp_async16(vst + c * 16, vp + c);
     }
-    __syncwarp();
-    const uint4* kmine = reinterpret_cast<const uint4*>(kst + key * RS + half * HO);
+    cp_async_commit();
+  };
+
+  // one unit in flight per warp while the previous one is scored: its K/V copies are issued as
+  // soon as the staged rows of the current unit have been read into registers
+  int64_t row_c;
+  const T *kb_c, *vb_c;
+  int t0_c = 0, act0_c = -1;
+  bool ok_c = false, direct_c = false;
+  if (warp < U) {
+    ok_c = unit_at(warp, row_c, kb_c, vb_c, t0_c, act0_c, direct_c);
+    if (ok_c && !direct_c) issue(row_c, kb_c, vb_c);
+    else if (!ok_c && lane == 0) atomicCAS(&g_decode_fast_error, 0, kErrBoundsAttendDecode);
+  }
+  for (int u = warp; u < U; u += kAttWarps) {
+    uint4 kr[KLD];
+    VT vr[kUnit];
+    if (ok_c && direct_c) {
+      // whole lines per instruction (consecutive lanes, consecutive 16-byte pieces), K staged in
+      // shared memory for the lane pairs (no copy is in flight: none was issued for this unit)
+      const uint4* kp = reinterpret_cast<const uint4*>(kb_c + row_c * DH);
 #pragma unroll
-    for (int i = 0; i < KLD; ++i) kr[i] = kmine[i];
+      for (int i = 0; i < KLD; ++i) kr[i] = kp[i * 32 + lane];
+      const T* vp = vb_c + row_c * DH + lane * VD;
+#pragma unroll
+      for (int j = 0; j < kUnit; ++j) vr[j] = *reinterpret_cast<const VT*>(vp + (size_t)j * DH);
+#pragma unroll
+      for (int i = 0; i < KLD; ++i) {
+        const int c = i * 32 + lane;
+        const int w = (c % CPK) * 16;
+        *reinterpret_cast<uint4*>(kst + (c / CPK) * RS + w + (w >= HALF * 2 ? 16 : 0)) = kr[i];
+      }
+      __syncwarp();
+      const uint4* kmine = reinterpret_cast<const uint4*>(kst + key * RS + half * HO);
+#pragma unroll
+      for (int i = 0; i < KLD; ++i) kr[i] = kmine[i];
+      __syncwarp();
+    } else if (ok_c) {
+      cp_async_wait_all();
+      __syncwarp();
+      const uint4* kmine = reinterpret_cast<const uint4*>(kst + key * RS + half * HO);
+#pragma unroll
+      for (int i = 0; i < KLD; ++i) kr[i] = kmine[i];
+#pragma unroll
+      for (int j = 0; j < kUnit; ++j) vr[j] = *reinterpret_cast<const VT*>(vst + j * DH * 2 + lane * VD * 2);
+      __syncwarp();
+    }
+    const bool ok = ok_c;
+    const int t0 = t0_c, act0 = act0_c;
+    const int un = u + kAttWarps;
+    if (un < U) {
+      ok_c = unit_at(un, row_c, kb_c, vb_c, t0_c, act0_c, direct_c);
+      if (ok_c && !direct_c) issue(row_c, kb_c, vb_c);
+      else if (!ok_c && lane == 0) atomicCAS(&g_decode_fast_error, 0, kErrBoundsAttendDecode);
+    }
+    if (!ok) continue;  // warp-uniform
 
 #pragma unroll
     for (int t = 0; t < LM; ++t) {
@@ -464,15 +527,20 @@ static cudaError_t launch_att_fast(const hga_params& p, int L, const void* q, co
                                    int64_t cold_cap, const int32_t* og, const int32_t* ot, int Kg, void* out,
                                    cudaStream_t st) {
   const size_t smem = ((size_t)LM * DH + (size_t)kAttWarps * LM * DH + 2 * kAttWarps * LM) * 4 +
-                      (size_t)kAttWarps * kUnit * (DH * 2 + 32);
+                      (size_t)kAttWarps * kUnit * (DH * 2 + 32 + DH * 2) + (size_t)2 * Kg * 4;
   auto kern = attend_decode_fast_kernel<T, DH, LM>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
+  // opened groups in host memory (the RAM tier's record read in place) are loaded directly
+  cudaPointerAttributes pa;
+  int cold_direct = 0;
+  if (cudaPointerGetAttributes(&pa, ckk) == cudaSuccess) cold_direct = pa.type == cudaMemoryTypeHost;
+  else (void)cudaGetLastError();
   dim3 grid(p.nhead, p.batch);
   kern<<<grid, kAttWarps * 32, smem, st>>>(p, L, (const T*)q, seq_pos, (const T*)hk, (const T*)hv, hot_cap, hot_mode,
-                                           (const T*)ckk, (const T*)cvv, cold_cap, og, ot, Kg, (T*)out);
+                                           (const T*)ckk, (const T*)cvv, cold_cap, og, ot, Kg, cold_direct, (T*)out);
   return cudaGetLastError();
 }
 
