@@ -197,11 +197,14 @@ size_t route_decode1_smem(int Dh, int nkey_max, int hb) {
 }
 
 // Heads per CTA: the largest of 8, 4, 2 that divides the query heads of one KV head and still
-// leaves at least one CTA per SM (148 SMs), else 1 (small batches route with the most CTAs).
+// leaves at least 128 CTAs, else 1 (small batches route with the most CTAs).  A summary row read
+// once serves more heads, so with enough CTAs to cover most SMs fewer, fuller CTAs win: at 32K
+// tokens, 32 query / 4 KV heads, B=16 routes in 25 us with 4 heads per CTA (128 CTAs) against 31
+// us with 2 (256 CTAs), B=32 in 32 us with 8 against 34 us with 4.
 static int route_decode1_heads(const hga_params& p) {
   const int rep = p.nhead / p.kv_heads;
   for (int hb = 8; hb > 1; hb >>= 1)
-    if (rep % hb == 0 && (int64_t)p.batch * (p.nhead / hb) >= 148) return hb;
+    if (rep % hb == 0 && (int64_t)p.batch * (p.nhead / hb) >= 128) return hb;
   return 1;
 }
 
