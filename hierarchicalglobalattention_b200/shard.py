@@ -202,15 +202,25 @@ class ShardedPrefill:
         v = self._buf("v", (lay.B, lay.KVH, nblk * lay.rows, lay.Dh), lay.dtype, dev)
         self._unpack(lay, recv_kv, lay.kv_numel, 0, lay.rows, lay.Dh, k_rope)
         self._unpack(lay, recv_kv, lay.kv_numel, lay.k_numel, lay.rows, lay.Dh, v)
-        outs = []
-        for (lo, hi), q, routing in zip(state["blocks"], state["q"], routings):
-            if q is None:
-                continue
-            outs.append(ops.attend_prefill(hp, q, k_rope, v, routing["open_gid"], routing["open_t0"], seq_len=S,
-                                           chunk_range=(lo, hi)).transpose(1, 2))   # [B,SQ,H,Dh]
-        if not outs:
+        live = [(lo, hi, q, r) for (lo, hi), q, r in zip(state["blocks"], state["q"], routings) if q is not None]
+        if not live:
             return None
-        heads = outs[0] if len(outs) == 1 else torch.cat(outs, dim=1)
+        C = m.chunk_size
+        sqs = [min(S, hi * C) - lo * C for lo, hi, _, _ in live]
+        if lay.B == 1 and len(live) > 1:
+            # one sequence: each block's rows are a contiguous slice of the rank's [1, rows, H, Dh]
+            # output, which the attention writes in place (no concatenation copy)
+            heads = self._buf("heads", (1, sum(sqs), m.nhead, m.head_dim), lay.dtype, dev)
+            r0 = 0
+            for (lo, hi, q, routing), sq in zip(live, sqs):
+                ops.attend_prefill(hp, q, k_rope, v, routing["open_gid"], routing["open_t0"], seq_len=S,
+                                   chunk_range=(lo, hi), out=heads[:, r0:r0 + sq])
+                r0 += sq
+        else:
+            outs = [ops.attend_prefill(hp, q, k_rope, v, routing["open_gid"], routing["open_t0"], seq_len=S,
+                                       chunk_range=(lo, hi)).transpose(1, 2)   # [B,SQ,H,Dh]
+                    for lo, hi, q, routing in live]
+            heads = outs[0] if len(outs) == 1 else torch.cat(outs, dim=1)
         B, R = heads.shape[:2]
         return m.o_proj(heads.reshape(B, R, m.nhead * m.head_dim))
 
